@@ -1,0 +1,113 @@
+/*
+ * b200_sampler.h -- C ABI of the B200 token sampler.
+ *
+ * A drop-in for the CPU sampler of llama.zig (src/sampler.zig).  The entry
+ * points below are what a Zig caller binds with @cImport;
+ * they take plain pointers, sizes and a CUDA stream passed as void*.
+ *
+ * Interfaces replaced (reference file:line):
+ *   bs_config            <- SamplerConfig            src/sampler.zig:4-13
+ *   bs_create            <- Sampler.init             src/sampler.zig:19-24
+ *   bs_sample            <- Sampler.sample           src/sampler.zig:26-28
+ *                           (sampleWithRandom        src/sampler.zig:43-169)
+ *   bs_sample_host       <- Sampler.sample with host logits, as engine.zig:355
+ *                           and main.zig:667 call it today
+ *   bs_argmax            <- sampleArgmax             src/sampler.zig:31-41
+ *                           and Dispatcher.executeTopK src/compute_graph.zig:948-985
+ *   bs_get/set_rng_state <- the DefaultPrng field    src/sampler.zig:17
+ *   bs_destroy           <- (Zig: the Sampler goes out of scope)
+ *   bs_status            <- error.OutOfMemory        src/sampler.zig:26 (!TokenID)
+ *
+ * Semantics: every row r of a handle is one Sampler.  Its xoshiro256++ state
+ * is seeded like Sampler.init (seed, or 0xDEADBEEF when the seed is 0) and it
+ * advances only when a row actually draws, exactly as in sampler.zig.  Token
+ * ids are bit-identical to sampleWithRandom's on the same logits and state.
+ *
+ * Threading: a handle owns device buffers and per-row RNG state; calls on one
+ * handle must be ordered (same stream or externally synchronised), as a Zig
+ * Sampler is single-threaded.  Logits are borrowed device pointers; nothing is
+ * copied unless the _host variant is used.
+ */
+#ifndef B200_SAMPLER_H
+#define B200_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (replace Zig error unions). */
+typedef enum bs_status {
+    BS_OK = 0,
+    BS_EINVAL = 1,     /* bad argument (null pointer, size out of range)        */
+    BS_ENOMEM = 2,     /* device or host allocation failed (error.OutOfMemory)  */
+    BS_ECUDA = 3,      /* a CUDA runtime call failed                            */
+    BS_ENCCL = 4,      /* an NCCL call failed (vocab-sharded path)              */
+    BS_ETIMEOUT = 5,   /* a bounded device-side wait gave up                    */
+    BS_ENOTSUP = 6,    /* configuration outside what this build implements      */
+    BS_EINTERNAL = 7   /* a device-side consistency check failed                */
+} bs_status;
+
+/* SamplerConfig, field for field (src/sampler.zig:4-13); 40 bytes. */
+typedef struct bs_config {
+    float temperature;          /* :5  default 0.8 */
+    uint32_t top_k;             /* :6  default 0   */
+    float top_p;                /* :7  default 0.9 */
+    float min_p;                /* :8  default 0.0 */
+    float typical_p;            /* :9  default 1.0 */
+    uint32_t _pad0;             /* keeps seed 8-byte aligned; must be 0 */
+    uint64_t seed;              /* :10 default 0 (-> 0xDEADBEEF)        */
+    uint32_t repetition_window; /* :11 default 32  */
+    float repetition_penalty;   /* :12 default 1.1 */
+} bs_config;
+
+typedef struct bs_sampler bs_sampler;
+
+/* Fill *cfg with SamplerConfig's defaults (src/sampler.zig:5-12). */
+void bs_config_default(bs_config *cfg);
+
+/* Sampler.init for `batch` rows of `vocab` logits on CUDA device `device`.
+ * Row r is seeded with cfg->seed + r (0 -> 0xDEADBEEF), unless `seeds` is
+ * non-NULL, in which case row r is seeded with seeds[r]. */
+bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vocab, int device,
+                    const uint64_t *seeds, bs_sampler **out);
+
+/* Sampler.sample for rows [row0, row0 + rows) of the handle.
+ *   d_logits : device pointer, row i at d_logits + i*ld (ld >= vocab floats)
+ *   d_prev   : device pointer to rows x n_prev previous token ids (row-major),
+ *              or NULL; used only by the repetition penalty
+ *   d_out    : device pointer, rows token ids
+ *   stream   : cudaStream_t (NULL = legacy default stream)
+ * Stream-ordered; returns once the work is enqueued. */
+bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, uint32_t row0, uint32_t rows,
+                    const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, void *stream);
+
+/* Compatibility path with host buffers (what engine.zig:355 passes today):
+ * copies logits (and prev) to the device, samples, copies ids back and
+ * synchronises the handle's stream.  h_prev may be NULL. */
+bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t ld, uint32_t row0,
+                         uint32_t rows, const uint32_t *h_prev, uint32_t n_prev, uint32_t *h_out);
+
+/* sampleArgmax on `rows` device rows: first index of the maximum (strict >,
+ * lowest index on ties, a NaN never wins unless it is element 0). */
+bs_status bs_argmax(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
+                    uint32_t *d_out, void *stream);
+
+/* Per-row xoshiro256++ state, batch x 4 u64 (host memory).  Synchronous. */
+bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state);
+bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state);
+
+/* Status of the last bs_sample on this handle after the stream reached it:
+ * BS_OK, or the first device-side error (e.g. BS_EINTERNAL).  Synchronous. */
+bs_status bs_last_device_status(bs_sampler *s);
+
+void bs_destroy(bs_sampler *s);
+
+const char *bs_status_string(bs_status st);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_SAMPLER_H */

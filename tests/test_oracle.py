@@ -1,0 +1,166 @@
+"""CPU checks of the checker itself: the reference's own tests, known-answer
+tests for each sampler.zig quirk, the restated Zig stdlib pieces, and the
+checker-derived golden fixtures."""
+import glob
+import json
+import os
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def cfg(orc, **kw):
+    base = dict(temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, typical_p=1.0, seed=0,
+                repetition_window=0, repetition_penalty=1.0)
+    base.update(kw)
+    return orc.make_config(**base)
+
+
+# --- the reference's own tests (src/sampler.zig:171-213) -----------------------
+def test_reference_same_seed_is_deterministic(orc):
+    c = cfg(orc, temperature=1.0, seed=1234)
+    s1, s2 = orc.Sampler(c), orc.Sampler(c)
+    z = np.zeros(4, np.float32)
+    a = [s1.sample(z) for _ in range(8)]
+    b = [s2.sample(z) for _ in range(8)]
+    assert a == b
+
+
+def test_reference_top_k_1_is_argmax(orc):
+    c = cfg(orc, temperature=1.0, top_k=1, seed=1)
+    s = orc.Sampler(c)
+    x = np.array([2.0, 1.9, 1.8], np.float32)
+    assert [s.sample(x) for _ in range(16)] == [0] * 16
+
+
+# --- restated Zig stdlib pieces -------------------------------------------------
+def test_splitmix64_known_outputs(orc):
+    # the widely published first outputs of SplitMix64 from state 0
+    st = orc.rng_seed(0)
+    assert [int(v) for v in st] == [0xE220A8397B1DCDAF, 0x6E789E6AA1B965F4,
+                                    0x06C45D188009454F, 0xF88BB8A8724C81EC]
+
+
+def test_random_float_mapping(orc):
+    L = orc.lib()
+    import ctypes
+    st = (ctypes.c_uint64 * 4)(*[int(v) for v in orc.rng_seed(99)])
+    words = ctypes.c_uint32(0)
+    vals = []
+    for _ in range(20000):
+        st_copy = (ctypes.c_uint64 * 4)(*st)
+        w = L.orc_rng_next(st_copy)
+        f = L.orc_rng_float(st, ctypes.byref(words))
+        # one word per draw unless the 41 high bits are zero (p = 2^-41)
+        lz = 64 - int(w).bit_length()
+        expect = np.float32(2.0 ** (-1 - lz) * (1 + (int(w) & 0x7FFFFF) / 2.0 ** 23))
+        assert np.float32(f) == expect
+        vals.append(f)
+    v = np.array(vals)
+    assert v.min() >= 0.0 and v.max() < 1.0
+    assert abs(v.mean() - 0.5) < 0.01
+    assert words.value == 20000
+
+
+def test_exp_log_within_one_ulp(orc):
+    L = orc.lib()
+    rng = np.random.default_rng(7)
+    xs = np.concatenate([rng.uniform(-104, 0, 20000), rng.uniform(-0.5, 0.5, 5000)]).astype(np.float32)
+    e = np.array([L.orc_expf(float(x)) for x in xs], np.float32)
+    ref = np.exp(xs.astype(np.float64)).astype(np.float32)
+    ulps = np.abs(e.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert ulps.max() <= 1
+    ps = rng.uniform(1e-30, 1.0, 20000).astype(np.float32)
+    lg = np.array([L.orc_logf(float(p)) for p in ps], np.float32)
+    ref = np.log(ps.astype(np.float64)).astype(np.float32)
+    ulps = np.abs(lg.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert ulps.max() <= 1
+    assert L.orc_expf(0.0) == 1.0 and L.orc_expf(float("-inf")) == 0.0
+    assert L.orc_expf(-103.98) == 0.0 and L.orc_logf(1.0) == 0.0
+
+
+# --- known answers for each sampler.zig quirk -----------------------------------
+def test_top_p_excludes_crossing_token(orc):
+    # probs ~ [0.5, 0.3, 0.2]: cum 0.5 <= 0.6 kept; 0.8 > 0.6 -> token 1 deselected
+    x = np.log(np.array([0.5, 0.3, 0.2], np.float32))
+    for seed in range(1, 40):
+        s = orc.Sampler(cfg(orc, top_p=0.6, seed=seed))
+        tok, tr = s.sample(x, trace=True)
+        assert tok == 0 and tr.n_kept == 1
+
+
+def test_top_p_all_deselected_returns_argmax_without_draw(orc):
+    x = np.log(np.array([0.02, 0.95, 0.03], np.float32))
+    s = orc.Sampler(cfg(orc, top_p=0.9, seed=5))
+    before = s.state.copy()
+    tok, tr = s.sample(x, trace=True)
+    assert tok == 1 and tr.path == orc.PATH_EMPTY and tr.draws == 0
+    assert np.array_equal(s.state, before)
+
+
+def test_temperature_le_zero_is_raw_argmax_without_draw(orc):
+    x = np.array([1.0, 3.0, 3.0, -1.0], np.float32)
+    s = orc.Sampler(cfg(orc, temperature=0.0, repetition_window=4, repetition_penalty=5.0, seed=3))
+    before = s.state.copy()
+    assert s.sample(x, prev=[1, 2]) == 1  # raw logits, no penalty, lowest index on ties
+    assert np.array_equal(s.state, before)
+
+
+def test_min_p_uses_global_max(orc):
+    # top-k=1 removes everything but the max; min-p still compares with it
+    x = np.log(np.array([0.6, 0.3, 0.1], np.float32))
+    s = orc.Sampler(cfg(orc, top_k=2, min_p=0.6, seed=2))
+    tok, tr = s.sample(x, trace=True)
+    assert tok == 0 and tr.n_kept == 1
+
+
+def test_typical_entropy_over_full_distribution(orc):
+    p = np.array([0.4, 0.3, 0.2, 0.1], np.float64)
+    x = np.log(p).astype(np.float32)
+    s = orc.Sampler(cfg(orc, typical_p=0.45, seed=1))
+    tok, tr = s.sample(x, trace=True)
+    H = -(p * np.log(p)).sum()
+    assert abs(tr.entropy - H) < 1e-5
+    # |-log p - H| ascending: 0.3 (dev 0.08), 0.2 (0.33), 0.4, 0.1: 0.3 <= 0.45 kept, 0.3+0.2 > 0.45
+    assert tok == 1 and tr.n_kept == 1
+
+
+def test_nan_logit_returns_zero_after_one_draw(orc):
+    x = np.array([0.5, np.nan, 2.0, 1.0], np.float32)
+    s = orc.Sampler(cfg(orc, top_p=0.9, seed=7))
+    tok, tr = s.sample(x, trace=True)
+    assert tok == 0 and tr.draws == 1 and np.isnan(tr.sum)
+
+
+def test_ties_keep_index_order(orc):
+    x = np.array([1.0, 2.0, 2.0, 2.0, 0.0], np.float32)
+    s = orc.Sampler(cfg(orc, top_k=1, seed=4))
+    assert s.sample(x) == 1
+
+
+def test_repetition_penalty_applied_once(orc):
+    x = np.array([2.0, -1.0, 1.5], np.float32)
+    # token 0 appears twice in the window: divided by 2 once -> 1.0 < 1.5
+    s = orc.Sampler(cfg(orc, top_k=1, repetition_window=4, repetition_penalty=2.0, seed=1))
+    assert s.sample(x, prev=[0, 0]) == 2
+
+
+# --- checker-derived golden fixtures --------------------------------------------
+GOLDEN = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
+def test_golden_fixture_reproduces(orc, path):
+    f = np.load(path)
+    c = json.loads(str(f["config"]))
+    oc = orc.make_config(**c)
+    x = f["logits"]
+    states = None
+    for s in range(x.shape[0]):
+        prev = f["prev"][s] if "prev" in f.files else None
+        out, _, states = orc.sample_batch(oc, x[s], seeds=f["seeds"] if states is None else None,
+                                          states=states, prev=prev)
+        assert np.array_equal(out, f["tokens"][s])
+        assert np.array_equal(states, f["states"][s])
