@@ -1,0 +1,288 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token sampler: rows sampled per second.
+
+Metric: rows sampled/s at V=128256, B=256, fp32 logits, with
+config 1's filters (T=0.7, top_k=40, top_p=0.95, min_p=0.05), and the achieved
+HBM GB/s of the dominant kernel against the measured B200 peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+One step = one bs_sample call over one batch of B rows resident in HBM.  Four
+distinct batches rotate (4 x 131 MB > the 126 MB L2), so no step reads logits
+left in L2 by the previous one.  Under torchrun each rank samples its own B
+rows (weak scaling, seeds keyed by the global row); the data path has no
+collective.  `--impl reference` times the reference algorithm on the host
+cores instead (the C restatement of sampler.zig, all threads).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+import __graft_entry__ as graft  # noqa: E402
+
+ROTATE = 4
+NVML_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(workload):
+    """DRAM bytes per launch of the cluster pass from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p))
+    e = d.get(workload)
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons through NVML while running."""
+
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for b, n in NVML_REASONS.items() if self.reasons & b]
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def workload_desc(w):
+    return (f"{w.name}: B={w.rows} V={w.vocab} T={w.temperature} top_k={w.top_k} top_p={w.top_p} "
+            f"min_p={w.min_p} typical_p={w.typical_p}")
+
+
+def cpu_baseline(pkg, w, budget_s: float, nthreads: int):
+    """The checker (C restatement of sampler.zig) on the host cores, bounded sample."""
+    orc = graft.load_oracle()
+    n = max(nthreads, min(w.rows * 2, int(budget_s / 0.025)))
+    x = pkg.workloads.make_logits(w, rows=min(n, w.rows))
+    reps = (n + x.shape[0] - 1) // x.shape[0]
+    cfg = orc.make_config(**w.config())
+    t0 = time.perf_counter()
+    done = 0
+    for r in range(reps):
+        m = min(x.shape[0], n - done)
+        orc.sample_batch(cfg, x[:m], seeds=w.seeds(m), nthreads=nthreads)
+        done += m
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "rows/s", "cores": nthreads, "kind": "port",
+            "sample": f"{done} rows of {w.name} (V={w.vocab}) on {nthreads} threads, {dt:.1f} s"}
+
+
+def run_reference(args, pkg, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    orc = graft.load_oracle()
+    cfg = orc.make_config(**w.config())
+    x = pkg.workloads.make_logits(w, rows=min(w.rows, nthreads))
+    seeds = w.seeds(x.shape[0])
+    for _ in range(args.warmup):
+        orc.sample_batch(cfg, x, seeds=seeds, nthreads=nthreads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.sample_batch(cfg, x, seeds=seeds, nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    rows = x.shape[0] * args.steps
+    v = rows / dt
+    line = {
+        "impl": "reference", "metric": "rows sampled/sec", "value": v, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_desc(w), "rows_per_step": x.shape[0]},
+        "cpu_baseline": {"value": v, "unit": "rows/s", "cores": nthreads, "kind": "port",
+                         "sample": f"{x.shape[0]} rows per step (one per host thread), {args.steps} steps"},
+        "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="headline")
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    pkg = graft.load_package()
+    w = pkg.workloads.WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, pkg, w)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    B, V = w.rows, w.vocab
+    # this rank's rows; seeds keyed by the global row
+    host = [pkg.workloads.make_logits(w, step=s, rows=B, row_offset=rank * B) for s in range(ROTATE)]
+    dev = [torch.from_numpy(h).cuda() for h in host]
+    cfg = pkg.SamplerConfig(**w.config())
+    smp = pkg.Sampler(cfg, batch=B, vocab=V, device=local, seeds=w.seeds(B, offset=rank * B))
+    out = torch.empty(B, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    for i in range(args.warmup):
+        smp.sample(dev[i % ROTATE], out=out)
+    torch.cuda.synchronize()
+    if smp.last_status() != 0:
+        raise RuntimeError(f"sampler status {smp.last_status()}")
+
+    greedy = w.temperature <= 0.0
+    if not greedy:
+        smp.profile_enable(args.steps)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            smp.sample(dev[i % ROTATE], out=out)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if smp.last_status() != 0:
+        raise RuntimeError(f"sampler status {smp.last_status()}")
+    launches_per_step = 1 if greedy else 2
+    kernel_ms = None
+    if not greedy:
+        ka, kb = smp.profile_read()
+        kernel_ms = (float(ka.mean()), float(kb.mean()))
+        smp.profile_enable(0)
+
+    # end to end through the public host API: pinned host logits -> device,
+    # sample, token ids -> host, every step
+    pinned = [torch.from_numpy(h).pin_memory() for h in host[:2]]
+    pin_np = [p.numpy() for p in pinned]
+    for i in range(3):
+        smp.sample(pin_np[i % 2])
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        smp.sample(pin_np[i % 2])
+    e2e_s = time.perf_counter() - t0
+    e2e_rows = B * args.e2e_steps * world / e2e_s
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_rows = B * args.e2e_steps * world / float(t.item())
+
+    if rank == 0:
+        rows_per_s = B * args.steps * world / (ms / 1e3)
+        peak, peak_kind = peaks()
+        alg_bytes = 4.0 * V * B
+        roof = None
+        if kernel_ms is None:   # greedy: one argmax kernel per step
+            kernel_ms = (ms / args.steps, 0.0)
+        if kernel_ms is not None:
+            ach = alg_bytes / (kernel_ms[0] / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                    "traffic": profile_traffic(args.workload),
+                    "kernel": "kernel_a (cluster pass)", "peak_kind": peak_kind,
+                    "kernel_ms": kernel_ms[0], "walk_kernel_ms": kernel_ms[1],
+                    "algorithmic_bytes_per_launch": alg_bytes,
+                    "step_gbs": alg_bytes / (ms / args.steps / 1e3) / 1e9}
+        line = {
+            "metric": "rows sampled/sec", "value": rows_per_s, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": workload_desc(w), "rows_per_gpu": B, "vocab": V,
+                       "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": f"{ROTATE} rotating input batches ({ROTATE * alg_bytes / 1e6:.0f} MB) > L2"},
+            "roofline": roof,
+            "clocks": clk.summary(),
+            "e2e": {"value": e2e_rows, "unit": "rows/s", "h2d_bytes_per_step": int(alg_bytes),
+                    "d2h_bytes_per_step": 4 * B, "api": "bs_sample_host (pinned host logits)"},
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(pkg, w, args.cpu_budget, os.cpu_count() or 1)
+        print(json.dumps(line), flush=True)
+    smp.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -103,6 +103,14 @@ bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state);
  * BS_OK, or the first device-side error (e.g. BS_EINTERNAL).  Synchronous. */
 bs_status bs_last_device_status(bs_sampler *s);
 
+/* Profiling (the counterpart of the engine's --report-json timers,
+ * src/engine.zig:14-26 and :457-462): when enabled, each of the next
+ * `max_calls` bs_sample calls records CUDA events around its two kernels.
+ * bs_profile_read synchronises and returns their durations in ms
+ * (ms_a: the cluster pass, ms_b: the walk/draw pass), then resets the ring. */
+bs_status bs_profile_enable(bs_sampler *s, uint32_t max_calls);
+bs_status bs_profile_read(bs_sampler *s, float *ms_a, float *ms_b, uint32_t *n_calls);
+
 void bs_destroy(bs_sampler *s);
 
 const char *bs_status_string(bs_status st);

@@ -255,7 +255,8 @@ struct KAParams {
     RowHdr *hdr;              // per handle row
     Item *items;              // per handle row: ntiles_total slots
     float *wcdata;            // per handle row: WC_CAP x 32
-    Candidate *cand;          // per handle row: CAND_CAP
+    Candidate *cand;          // per handle row: cand_stride
+    uint32_t cand_stride;     // >= vocab: every token can be a candidate
 };
 
 struct XSlot {   // per-CTA values exchanged through distributed shared memory
@@ -436,6 +437,8 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
     __shared__ uint32_t wnan[KA_WARPS];
     __shared__ float kth_sh;
     __shared__ float kgather[MAX_CLUSTER * KSEL_MAX];
+    __shared__ float hist[HIST_BINS];
+    __shared__ float ghist[HIST_BINS];
 
     RowHdr *hdr = P.hdr + hrow;
     const uint32_t seg0 = rank * P.seg_len;
@@ -565,7 +568,8 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
     for (uint32_t t = warp; t < NT; t += KA_WARPS) {
         const float v = seg[t * TILE + lane];
         const float d = __fsub_rn(v, M);
-        const bool isn = (d != d) || t_nan || (isinf(d) && t_inf);
+        const bool real = seg0 + t * TILE + lane < V;   // not padding
+        const bool isn = real && ((d != d) || t_nan || (isinf(d) && t_inf));
         nan_local |= isn ? 1u : 0u;
         const float x2 = (d == 0.0f) ? 0.0f : d * c2;
         const float pt = isn ? 0.0f : ex2_approx(x2);
@@ -601,6 +605,18 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
         row_nan |= o->nan_any;
     }
 
+    // top-p tail-mass histogram: elements with log2 p >= f0 (f0 bounds the mass
+    // below it by a quarter of the top-p budget, V * 2^f0 <= (1-top_p) S / 4)
+    const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
+    const bool hist_on = p_active && (1.0f - P.top_p) >= 1e-3f;
+    const double s_lo = fmax(1.0, 0.99 * s_raw);
+    const float f0 = hist_on ? (float)(log2((1.0 - (double)P.top_p) * s_lo / (4.0 * (double)V)) - 1e-3)
+                             : 0.0f;
+    const float binw = fmaxf(0.125f, -f0 / (float)HIST_BINS);
+    const float inv_binw = 1.0f / binw;
+    for (uint32_t b = tid; b < HIST_BINS; b += KA_THREADS) hist[b] = 0.0f;
+    __syncthreads();
+
     // ---- phase 3b: rounding-aware tile sums ---------------------------------
     for (uint32_t t = warp; t < NT; t += KA_WARPS) {
         const double Pt = base_raw + pref[t];
@@ -618,6 +634,10 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
             } else {
                 big = ex2_approx(x2);                 // far above the grid: p itself
             }
+        }
+        if (hist_on && !isn && x2 >= f0) {
+            const int b = min(HIST_BINS - 1, (int)((x2 - f0) * inv_binw));
+            atomicAdd(&hist[b], ex2_approx(x2));
         }
         const float s = warp_sum(q);
         const float sb = warp_sum(big);
@@ -660,6 +680,14 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
         const XSlot *o = cluster.map_shared_rank(&xs, r);
         if (r < rank) base2 += o->tot2;
         s_tot += o->tot2;
+    }
+    if (hist_on) {
+        for (uint32_t b = tid; b < HIST_BINS; b += KA_THREADS) {
+            float m = 0.0f;
+            for (uint32_t r = 0; r < P.C; r++) m += cluster.map_shared_rank(hist, r)[b];
+            ghist[b] = m;
+        }
+        __syncthreads();
     }
     float xk2 = NEG_INF;
     if (k_floor) {
@@ -708,12 +736,21 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
     // floors in log2 units of p (x2 = log2 p, approximately)
     float xf2 = -151.0f;   // p > 0 only
     uint32_t binding = 0;  // 0 none, 1 k, 2 p, 3 min-p
-    const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
     if (k_floor && xk2 > xf2) { xf2 = xk2; binding = 1; }
-    if (p_active && (1.0f - P.top_p) >= 1e-3f) {
-        const double slo = fmax(1.0, 0.999 * s_tot);
-        const double xp = log2((1.0 - (double)P.top_p) * slo / (2.0 * (double)V)) - 1e-3;
-        if ((float)xp > xf2) { xf2 = (float)xp; binding = 2; }
+    if (hist_on) {
+        // highest bin edge f* with (mass in [f0, f*)) <= (1-top_p) S / 4, so the
+        // mass below f* is at most half of the top-p budget: the cumulative
+        // probability of the tokens above f* exceeds top_p with margin.
+        const float budget = (float)((1.0 - (double)P.top_p) * s_lo / 4.0);
+        float acc = 0.0f;
+        int bstar = 0;
+        for (int b = 0; b < HIST_BINS; b++) {
+            acc += ghist[b] * 1.001f;
+            if (acc > budget) break;
+            bstar = b + 1;
+        }
+        const float xp = f0 + (float)bstar * binw - 1e-3f;
+        if (xp > xf2) { xf2 = xp; binding = 2; }
     }
     if (P.min_p > 0.0f) {
         const double xm = fmin(0.0, log2((double)P.min_p)) - 0.01;
@@ -727,7 +764,7 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
     }
 
     // ---- phase 4: classify tiles, grid counts, candidates ---------------------
-    Candidate *cand = P.cand + (size_t)hrow * CAND_CAP;
+    Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
     float *wcd = P.wcdata + (size_t)hrow * WC_CAP * TILE;
     for (uint32_t t = warp; t < NT; t += KA_WARPS) {
         const double Ps = base2 + pref[t];
@@ -760,7 +797,7 @@ __global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
             basec = __shfl_sync(0xffffffffu, basec, 0);
             if (cnd && p > 0.0f) {
                 const uint32_t pos = basec + __popc(cmask & ((1u << lane) - 1u));
-                if (pos < CAND_CAP) cand[pos] = Candidate{gidx, p};
+                if (pos < P.cand_stride) cand[pos] = Candidate{gidx, p};
             }
         }
         uint32_t aux = 0;
@@ -863,7 +900,9 @@ struct KBParams {
     RowHdr *hdr;
     Item *items;
     float *wcdata;
-    Candidate *cand;
+    Candidate *cand;     // per handle row: cand_stride entries (Kernel A output)
+    unsigned long long *ctmp;  // per handle row: 2 x cand_stride keys (large-set path)
+    uint32_t cand_stride;
     uint64_t *rng;       // per handle row, 4 words
     RowTrace *trace;     // per handle row
     uint32_t *out;       // per call row
@@ -883,6 +922,69 @@ __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M
     return prob_unnorm(v, M, P.T);
 }
 
+// Candidate key: ascending key order == (p descending, index ascending).
+__device__ __forceinline__ unsigned long long cand_key(Candidate c) {
+    return ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(c.p)) << 32) | c.idx;
+}
+__device__ __forceinline__ float key_p(unsigned long long k) {
+    return __uint_as_float(0xFFFFFFFFu - (uint32_t)(k >> 32));
+}
+
+// Stable LSD radix sort (4-bit digits) of n keys by one CTA, global memory.
+// Returns the buffer holding the sorted keys (a or b).
+__device__ unsigned long long *cta_radix_sort(unsigned long long *a, unsigned long long *b, uint32_t n,
+                                              uint32_t *cnt /* smem, 16 * KB_THREADS */,
+                                              unsigned long long *red /* smem, 2 */) {
+    const int tid = threadIdx.x;
+    // bits that differ between keys
+    unsigned long long o = 0, an = ~0ull;
+    for (uint32_t i = tid; i < n; i += KB_THREADS) {
+        o |= a[i];
+        an &= a[i];
+    }
+    if (tid == 0) {
+        red[0] = 0;
+        red[1] = ~0ull;
+    }
+    __syncthreads();
+    atomicOr(&red[0], o);
+    atomicAnd(&red[1], an);
+    __syncthreads();
+    const unsigned long long vary = red[0] ^ red[1];
+    const uint32_t chunk = (n + KB_THREADS - 1) / KB_THREADS;
+    const uint32_t lo = min(n, tid * chunk), hi = min(n, lo + chunk);
+    for (int sh = 0; sh < 64; sh += 4) {
+        if (((vary >> sh) & 0xFull) == 0) continue;
+        uint32_t c[16];
+#pragma unroll
+        for (int d = 0; d < 16; d++) c[d] = 0;
+        for (uint32_t i = lo; i < hi; i++) c[(a[i] >> sh) & 0xF]++;
+#pragma unroll
+        for (int d = 0; d < 16; d++) cnt[d * KB_THREADS + tid] = c[d];
+        __syncthreads();
+        if (tid == 0) {   // exclusive scan, digit-major
+            uint32_t run = 0;
+            for (int i = 0; i < 16 * KB_THREADS; i++) {
+                const uint32_t v = cnt[i];
+                cnt[i] = run;
+                run += v;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int d = 0; d < 16; d++) c[d] = cnt[d * KB_THREADS + tid];
+        for (uint32_t i = lo; i < hi; i++) {
+            const unsigned long long k = a[i];
+            b[c[(k >> sh) & 0xF]++] = k;
+        }
+        __syncthreads();
+        unsigned long long *t = a;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+
 __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t row = blockIdx.x;
     const uint32_t hrow = P.row0 + row;
@@ -894,16 +996,17 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
     __shared__ uint32_t walk_flags;
+    __shared__ unsigned long long red2[2];
     extern __shared__ __align__(16) unsigned char smem[];
-    unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem);   // CAND_CAP
-    float *wcs = reinterpret_cast<float *>(keys + CAND_CAP);                   // WC_CAP*32
-    float *probs = wcs + WC_CAP * TILE;                                        // CAND_CAP
+    unsigned long long *skeys = reinterpret_cast<unsigned long long *>(smem);  // CAND_SMEM
+    float *wcs = reinterpret_cast<float *>(skeys + CAND_SMEM);                 // WC_CAP*32
+    float *sprobs = wcs + WC_CAP * TILE;                                       // CAND_SMEM
 
     const float M = hdr->M;
     const uint32_t flags0 = hdr->flags;
-    const uint32_t n_cand_all = hdr->n_cand;
-    const uint32_t n_cand = min(n_cand_all, (uint32_t)CAND_CAP);
+    const uint32_t n_cand = min(hdr->n_cand, P.cand_stride);
     const uint32_t n_wc = min(hdr->n_wc, (uint32_t)WC_CAP);
+    const bool big = n_cand > (uint32_t)CAND_SMEM;
 
     // penalty window (for the recompute path)
     uint32_t nwin = 0;
@@ -913,19 +1016,15 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         for (uint32_t j = tid; j < win; j += KB_THREADS) swin[j] = P.prev[(size_t)row * P.n_prev + start + j];
         nwin = win;
     }
-    // stored window/complex tiles and candidate keys
     const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
     for (uint32_t i = tid; i < n_wc * TILE; i += KB_THREADS) wcs[i] = wcg[i];
-    const Candidate *cg_ = P.cand + (size_t)hrow * CAND_CAP;
+    const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
+    unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
+    unsigned long long *gk1 = gk0 + P.cand_stride;
     uint32_t npow = 1;
-    while (npow < n_cand) npow <<= 1;
-    for (uint32_t i = tid; i < npow; i += KB_THREADS) {
-        unsigned long long k = ~0ull;
-        if (i < n_cand) {
-            const Candidate c = cg_[i];
-            k = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(c.p)) << 32) | c.idx;
-        }
-        keys[i] = k;
+    if (!big) {
+        while (npow < n_cand) npow <<= 1;
+        for (uint32_t i = tid; i < npow; i += KB_THREADS) skeys[i] = i < n_cand ? cand_key(cg_[i]) : ~0ull;
     }
     if (tid == 0) walk_flags = 0;
     __syncthreads();
@@ -967,12 +1066,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                     const uint32_t ntl = it.kind == CLS_SIMPLE ? min(it.aux, P.ntiles_total) : 1u;
                     if (!stored) wflags |= RF_SLOW_WALK;
                     for (uint32_t tt = 0; tt < ntl; tt++) {
-                        float pv;
-                        if (stored) {
-                            pv = wcs[it.aux * TILE + lane];
-                        } else {
-                            pv = exact_p_at(P, row, (it.tile + tt) * TILE + lane, M, swin, nwin);
-                        }
+                        const float pv = stored ? wcs[it.aux * TILE + lane]
+                                                : exact_p_at(P, row, (it.tile + tt) * TILE + lane, M, swin, nwin);
                         tilep[lane] = pv;
                         __syncwarp();
                         if (lane == 0) {
@@ -989,8 +1084,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             S_sh = float_of(st);
             walk_flags = wflags;
         }
-    } else {
-        // ---- candidate sort: (p desc, idx asc) == ascending key ----
+    } else if (!big) {
+        // ---- candidate sort in shared memory: ascending key ----
         const int t2 = tid - 32, nthr = KB_THREADS - 32;
         for (uint32_t size = 2; size <= npow; size <<= 1) {
             for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
@@ -999,10 +1094,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                     const uint32_t a = 2 * i - (i & (stride - 1));
                     const uint32_t b = a + stride;
                     const bool up = ((a & size) == 0);
-                    const unsigned long long ka = keys[a], kb = keys[b];
+                    const unsigned long long ka = skeys[a], kb = skeys[b];
                     if (up ? (ka > kb) : (ka < kb)) {
-                        keys[a] = kb;
-                        keys[b] = ka;
+                        skeys[a] = kb;
+                        skeys[b] = ka;
                     }
                 }
             }
@@ -1011,13 +1106,22 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     }
     __syncthreads();
 
+    // large candidate sets: stable radix sort in global memory (whole CTA)
+    unsigned long long *keys = skeys;
+    float *probs = sprobs;
+    if (big) {
+        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) gk0[i] = cand_key(cg_[i]);
+        __syncthreads();
+        uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // 16 * KB_THREADS words
+        keys = cta_radix_sort(gk0, gk1, n_cand, cnt, red2);
+        probs = reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0);
+        __syncthreads();
+    }
+
     const float S = S_sh;
     const bool nan_row = (flags0 & RF_NAN) != 0;
     // exact probs in sorted order (sampler.zig:90)
-    for (uint32_t i = tid; i < n_cand; i += KB_THREADS) {
-        const float p = __uint_as_float(0xFFFFFFFFu - (uint32_t)(keys[i] >> 32));
-        probs[i] = __fdiv_rn(p, S);
-    }
+    for (uint32_t i = tid; i < n_cand; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
     __syncthreads();
     if (tid != 0) return;
 
@@ -1029,7 +1133,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     uint64_t s4[4];
     uint64_t *rng = P.rng + (size_t)hrow * 4;
     s4[0] = rng[0]; s4[1] = rng[1]; s4[2] = rng[2]; s4[3] = rng[3];
-    uint32_t flags = flags0 | walk_flags;
+    uint32_t flags = flags0 | walk_flags | (big ? RF_CAND_BIG : 0u);
+    float S_rep = S;
 
     if (nan_row) {
         // sum is NaN (sampler.zig:87-90): every comparison is false, the stable
@@ -1039,18 +1144,16 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         token = 0;
         path = 5;
         total = __int_as_float(0x7fc00000);
+        S_rep = total;
     } else if (!(S > 0.0f)) {
         token = hdr->raw_arg;   // sampler.zig:89
         path = 1;
-    } else if (n_cand_all > CAND_CAP) {
-        status = ROW_ENOTSUP;
-        flags |= RF_CAND_OVERFLOW;
     } else {
+        // idxs[2*i] aliases the low word of keys[i]
+        uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);
         // ties: equal probs from distinct p keep index order (stable sort)
-        uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);  // reuse: low words
-        for (uint32_t i = 0; i < n_cand; i++) idxs[2 * i] = (uint32_t)(keys[i] & 0xFFFFFFFFu);
         for (uint32_t i = 1; i < n_cand; i++) {
-            if (probs[i] == probs[i - 1]) {
+            if (probs[i] == probs[i - 1] && idxs[2 * (i - 1)] > idxs[2 * i]) {
                 uint32_t j = i;
                 const uint32_t id = idxs[2 * j];
                 const float pr = probs[j];
@@ -1061,24 +1164,24 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                 idxs[2 * j] = id;
             }
         }
+        // The candidates are every token above a floor, i.e. a prefix of the
+        // reference's sorted order.  The kept prefix is settled inside it when
+        // some filter cuts before its end, when the candidates are all tokens
+        // with p > 0, or when the floor is the binding filter's own bound.
         uint32_t n_sel = n_cand;
         const uint32_t binding = hdr->binding;
-        bool cover_ok = (binding == 0 || binding == 1 || binding == 3);
+        const bool k_act = P.top_k > 0 && P.top_k < P.vocab;
         // top-k (sampler.zig:106-109)
-        if (P.top_k > 0 && P.top_k < P.vocab) {
-            if (n_sel > P.top_k) n_sel = P.top_k;
-        }
+        if (k_act && n_sel > P.top_k) n_sel = P.top_k;
         // top-p (sampler.zig:111-118): the crossing token is deselected too
         if (P.top_p > 0.0f && P.top_p < 1.0f) {
             float cum = 0.0f;
-            uint32_t j = 0;
-            for (; j < n_sel; j++) {
+            for (uint32_t j = 0; j < n_sel; j++) {
                 cum = __fadd_rn(cum, probs[j]);
-                if (cum > P.top_p) break;
-            }
-            if (j < n_sel) {
-                n_sel = j;
-                cover_ok = true;
+                if (cum > P.top_p) {
+                    n_sel = j;
+                    break;
+                }
             }
         }
         // min-p (sampler.zig:120-126) against probs[indices[0]]
@@ -1088,8 +1191,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             while (j < n_sel && !(probs[j] < thr)) j++;
             n_sel = j;
         }
-        if (!cover_ok && binding != 0) {
-            status = ROW_ENOTSUP;
+        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || n_sel < n_cand ||
+                              (k_act && P.top_k <= n_cand);
+        if (!cover_ok) {
+            status = ROW_EINTERNAL;
             flags |= RF_CAND_SHORT;
         } else if (P.typical_p > 0.0f && P.typical_p < 1.0f) {
             status = ROW_ENOTSUP;  // typical-p runs in its own pass (not in this build)
@@ -1123,13 +1228,13 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         P.out[row] = 0xFFFFFFFFu;
     }
     RowTrace tr;
-    tr.S = S;
+    tr.S = S_rep;
     tr.total = total;
     tr.u = u;
     tr.n_kept = n_kept;
     tr.path = path;
     tr.flags = flags;
-    tr.n_cand = n_cand_all;
+    tr.n_cand = n_cand;
     tr.status = status;
     P.trace[hrow] = tr;
 }
@@ -1153,6 +1258,8 @@ struct bs_sampler {
     Item *d_items;
     float *d_wc;
     Candidate *d_cand;
+    unsigned long long *d_ctmp;
+    uint32_t cand_stride;
     RowTrace *d_trace;
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
@@ -1160,6 +1267,8 @@ struct bs_sampler {
     size_t stage_floats;
     size_t stage_prev;
     cudaStream_t stream;
+    cudaEvent_t *prof_ev;    // profiling ring: 3 events per bs_sample call
+    uint32_t prof_cap, prof_n;
 };
 
 static bs_status cuda_status(cudaError_t e) { return e == cudaSuccess ? BS_OK : BS_ECUDA; }
@@ -1208,11 +1317,14 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_items);
     cudaFree(s->d_wc);
     cudaFree(s->d_cand);
+    cudaFree(s->d_ctmp);
     cudaFree(s->d_trace);
     cudaFree(s->d_logits_stage);
     cudaFree(s->d_prev_stage);
     cudaFree(s->d_out_stage);
     if (s->stream) cudaStreamDestroy(s->stream);
+    for (uint32_t i = 0; s->prof_ev && i < 3 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
+    delete[] s->prof_ev;
 }
 
 // The dynamic shared-memory limit is a per-function attribute: keep it at the
@@ -1260,14 +1372,16 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     s->ksort = ks;
     s->smem_a = (size_t)seg * 4 + (size_t)s->ntiles_seg * 16 + (size_t)ks * 4 +
                 (size_t)s->ntiles_seg * (sizeof(TileRec) + 4 + sizeof(Comp)) + 64;
-    s->smem_b = (size_t)CAND_CAP * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_CAP * 4;
+    s->smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+    s->cand_stride = (vocab + 31u) & ~31u;
 
     cudaError_t e = cudaSuccess;
     e = cudaMalloc(&s->d_rng, (size_t)batch * 4 * sizeof(uint64_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_hdr, (size_t)batch * sizeof(RowHdr));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_items, (size_t)batch * s->ntiles_total * sizeof(Item));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_wc, (size_t)batch * WC_CAP * TILE * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s->d_cand, (size_t)batch * CAND_CAP * sizeof(Candidate));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_cand, (size_t)batch * s->cand_stride * sizeof(Candidate));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_ctmp, (size_t)batch * 2 * s->cand_stride * sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_trace, (size_t)batch * sizeof(RowTrace));
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
@@ -1350,6 +1464,7 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.items = s->d_items;
     A.wcdata = s->d_wc;
     A.cand = s->d_cand;
+    A.cand_stride = s->cand_stride;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(s->C, rows, 1);
@@ -1363,6 +1478,9 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    cudaEvent_t *ev = nullptr;
+    if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 3 * s->prof_n++;
+    if (ev) cudaEventRecord(ev[0], st);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_a, A);
     if (e != cudaSuccess) {
         fprintf(stderr, "b200_sampler: kernel A launch failed: %s\n", cudaGetErrorString(e));
@@ -1388,10 +1506,14 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.items = s->d_items;
     B.wcdata = s->d_wc;
     B.cand = s->d_cand;
+    B.ctmp = s->d_ctmp;
+    B.cand_stride = s->cand_stride;
     B.rng = s->d_rng;
     B.trace = s->d_trace;
     B.out = d_out;
+    if (ev) cudaEventRecord(ev[1], st);
     kernel_b<<<rows, KB_THREADS, s->smem_b, st>>>(B);
+    if (ev) cudaEventRecord(ev[2], st);
     return cuda_status(cudaGetLastError());
 }
 
@@ -1474,5 +1596,34 @@ extern "C" bs_status bs_debug_row_traces(bs_sampler *s, void *h_traces, size_t b
     BS_CUDA(cudaSetDevice(s->device));
     BS_CUDA(cudaDeviceSynchronize());
     BS_CUDA(cudaMemcpy(h_traces, s->d_trace, (size_t)s->batch * sizeof(RowTrace), cudaMemcpyDeviceToHost));
+    return BS_OK;
+}
+
+extern "C" bs_status bs_profile_enable(bs_sampler *s, uint32_t max_calls) {
+    if (!s) return BS_EINVAL;
+    BS_CUDA(cudaSetDevice(s->device));
+    for (uint32_t i = 0; s->prof_ev && i < 3 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
+    delete[] s->prof_ev;
+    s->prof_ev = nullptr;
+    s->prof_cap = s->prof_n = 0;
+    if (max_calls == 0) return BS_OK;
+    s->prof_ev = new (std::nothrow) cudaEvent_t[3 * (size_t)max_calls];
+    if (!s->prof_ev) return BS_ENOMEM;
+    for (uint32_t i = 0; i < 3 * max_calls; i++) BS_CUDA(cudaEventCreate(&s->prof_ev[i]));
+    s->prof_cap = max_calls;
+    return BS_OK;
+}
+
+extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms_a, float *ms_b, uint32_t *n_calls) {
+    if (!s || !ms_a || !ms_b || !n_calls) return BS_EINVAL;
+    BS_CUDA(cudaSetDevice(s->device));
+    const uint32_t n = s->prof_n;
+    for (uint32_t i = 0; i < n; i++) {
+        BS_CUDA(cudaEventSynchronize(s->prof_ev[3 * i + 2]));
+        BS_CUDA(cudaEventElapsedTime(&ms_a[i], s->prof_ev[3 * i], s->prof_ev[3 * i + 1]));
+        BS_CUDA(cudaEventElapsedTime(&ms_b[i], s->prof_ev[3 * i + 1], s->prof_ev[3 * i + 2]));
+    }
+    *n_calls = n;
+    s->prof_n = 0;
     return BS_OK;
 }

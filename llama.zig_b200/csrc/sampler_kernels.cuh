@@ -13,7 +13,8 @@ constexpr int KB_THREADS = 256;          // Kernel B block size
 constexpr int MAX_CLUSTER = 8;           // portable cluster size
 constexpr int SEG_TARGET = 16384;        // target elements per CTA segment
 constexpr int SEG_MAX = 32768;           // hard cap (128 KB of shared memory)
-constexpr int CAND_CAP = 4096;           // candidates kept per row
+constexpr int CAND_SMEM = 4096;          // candidates sorted in shared memory (fast path)
+constexpr int HIST_BINS = 256;           // top-p tail-mass histogram bins
 constexpr int WC_CAP = 256;              // window/complex tiles with stored p per row
 constexpr int KSEL_MAX = 256;            // largest top_k served by the tile-max floor
 constexpr int ITEM_CHUNK = 128;          // items staged per step in Kernel B
@@ -24,7 +25,7 @@ enum : uint32_t { CLS_SIMPLE = 0, CLS_WINDOW = 1, CLS_COMPLEX = 2 };
 // Row flags.
 enum : uint32_t {
     RF_NAN = 1u << 0,           // some p_i is NaN: sum is NaN (sampler.zig:87)
-    RF_CAND_OVERFLOW = 1u << 1, // more than CAND_CAP candidates
+    RF_CAND_BIG = 1u << 1,      // more than CAND_SMEM candidates (global-memory path)
     RF_CAND_SHORT = 1u << 2,    // candidate set did not cover the kept prefix
     RF_SLOW_WALK = 1u << 3,     // walker needed the recompute path (diagnostic)
     RF_BAD_CONFIG = 1u << 4,
@@ -39,7 +40,7 @@ struct RowHdr {
     float raw_max;       // sampleArgmax of the raw logits, value ...
     uint32_t raw_arg;    // ... and index (sampler.zig:89 fallback)
     uint32_t flags;      // RF_*
-    uint32_t n_cand;     // candidates appended (may exceed CAND_CAP)
+    uint32_t n_cand;     // candidates appended
     uint32_t n_wc;       // window/complex tiles with stored p (may exceed WC_CAP)
     float s_approx;      // approximate normaliser
     float v_floor;       // candidate floor (logit domain)

@@ -33,7 +33,7 @@ BS_OK, BS_EINVAL, BS_ENOMEM, BS_ECUDA, BS_ENCCL, BS_ETIMEOUT, BS_ENOTSUP, BS_EIN
 EXPORTS = [
     "bs_config_default", "bs_create", "bs_sample", "bs_sample_host", "bs_argmax",
     "bs_get_rng_state", "bs_set_rng_state", "bs_last_device_status", "bs_destroy",
-    "bs_status_string",
+    "bs_status_string", "bs_profile_enable", "bs_profile_read",
 ]
 
 
@@ -119,8 +119,11 @@ def lib() -> ctypes.CDLL:
         L.bs_status_string.argtypes = [ctypes.c_int]
         L.bs_status_string.restype = ctypes.c_char_p
         L.bs_debug_row_traces.argtypes = [vp, vp, ctypes.c_size_t]
+        L.bs_profile_enable.argtypes = [vp, u32]
+        L.bs_profile_read.argtypes = [vp, vp, vp, ctypes.POINTER(u32)]
         for name in ("bs_create", "bs_sample", "bs_sample_host", "bs_argmax", "bs_get_rng_state",
-                     "bs_set_rng_state", "bs_last_device_status", "bs_debug_row_traces"):
+                     "bs_set_rng_state", "bs_last_device_status", "bs_debug_row_traces",
+                     "bs_profile_enable", "bs_profile_read"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -246,6 +249,20 @@ class Sampler:
 
     def last_status(self) -> int:
         return lib().bs_last_device_status(self._h)
+
+    def profile_enable(self, max_calls: int) -> None:
+        """Record CUDA events around both kernels of the next max_calls calls."""
+        _check(lib().bs_profile_enable(self._h, max_calls), "bs_profile_enable")
+
+    def profile_read(self):
+        """(ms_a, ms_b) arrays: per-call durations of the two kernels."""
+        cap = 1 << 20
+        a = np.zeros(cap, np.float32)
+        b = np.zeros(cap, np.float32)
+        n = ctypes.c_uint32(0)
+        _check(lib().bs_profile_read(self._h, a.ctypes.data, b.ctypes.data, ctypes.byref(n)),
+               "bs_profile_read")
+        return a[:n.value].copy(), b[:n.value].copy()
 
     def traces(self):
         tr = (RowTrace * self.batch)()
