@@ -55,7 +55,6 @@ namespace bs {
 
 constexpr uint32_t QSAT = 1u << 30;      // saturation of grid counts
 constexpr uint32_t QLIM = 1u << 24;      // mantissa range of one binade
-constexpr double DELTA = 1e-5;           // speculation window (relative)
 constexpr float NEG_INF = -__builtin_huge_valf();
 
 // ---------------------------------------------------------------------------
@@ -65,6 +64,15 @@ constexpr float NEG_INF = -__builtin_huge_valf();
 // parity of m.  A composite stores the total count for entry parity 0 and 1.
 struct Comp {
     uint32_t q0, q1;
+};
+
+// Per-tile prefix (binade lo) and suffix (binade lo+1) counts inside a
+// WINDOW stretch: the walker locates the crossing tile with them.
+struct WTile {
+    Comp pre_lo;   // counts from the stretch start through this tile, binade lo
+    Comp suf_hi;   // counts from this tile through the stretch end, binade lo+1
+    uint32_t slot; // stored exact p of this tile (window/complex store) or ~0u
+    uint32_t pad;
 };
 
 __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
@@ -233,41 +241,13 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
 }
 
 // ---------------------------------------------------------------------------
-struct KAParams {
-    const float *logits;
-    size_t ld;
-    const uint32_t *prev;     // rows x n_prev (device) or null
-    uint32_t n_prev;
-    uint32_t vocab;
-    uint32_t row0;            // first handle row of this call
-    float T;                  // temperature
-    float c2;                 // log2(e) / T (approximate paths only)
-    uint32_t top_k;
-    float top_p;
-    float min_p;
-    uint32_t rep_window;
-    float rep_penalty;
-    uint32_t C;               // cluster size (segments per row)
-    uint32_t seg_len;         // elements per segment (multiple of 32)
-    uint32_t ntiles_seg;      // seg_len / 32
-    uint32_t ntiles_total;    // ceil(vocab / 32)
-    uint32_t ksort;           // power of two >= ntiles_seg (top-k tile-max sort)
-    RowHdr *hdr;              // per handle row
-    Item *items;              // per handle row: ntiles_total slots
-    float *wcdata;            // per handle row: WC_CAP x 32
-    Candidate *cand;          // per handle row: cand_stride
-    uint32_t cand_stride;     // >= vocab: every token can be a candidate
-};
 
-struct XSlot {   // per-CTA values exchanged through distributed shared memory
-    float pmax;
-    float rmax;
-    uint32_t rarg;
-    uint32_t nan_any;
-    double tot_raw;
-    double tot2;
-    uint32_t klen;
-    uint32_t pad;
+struct TileParam {   // per-tile values K2's main loop needs (16 bytes)
+    int32_t lo;        // lowest candidate binade of the running sum
+    uint16_t cls;      // CLS_*
+    uint16_t special;  // the tile goes to the warp-cooperative exact pass
+    float K;           // 23 - lo: log2(p / u_lo) = x2 + K
+    float thr;         // x2 below this: p < u_lo / 2
 };
 
 struct TileRec {
@@ -278,93 +258,66 @@ struct TileRec {
     Comp qhi;
 };
 
-__device__ __forceinline__ bool penalty_active(const KAParams &P) {
-    return P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0;
-}
-
-// Block-wide exclusive scan of n (<= 2*KA_THREADS) doubles in place; returns total.
-__device__ double block_exscan_d(double *a, uint32_t n, double *wtmp) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t i0 = 2 * tid, i1 = 2 * tid + 1;
-    const double a0 = i0 < n ? a[i0] : 0.0;
-    const double a1 = i1 < n ? a[i1] : 0.0;
-    double v = a0 + a1, incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-    }
-    if (lane == 31) wtmp[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        double w = lane < KA_WARPS ? wtmp[lane] : 0.0, wi = w;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double t = __shfl_up_sync(0xffffffffu, wi, o);
-            if (lane >= o) wi += t;
-        }
-        if (lane < KA_WARPS) wtmp[lane] = wi - w;  // exclusive warp offsets
-        if (lane == KA_WARPS - 1) wtmp[KA_WARPS] = wi;
-    }
-    __syncthreads();
-    const double ex = wtmp[warp] + incl - v;
-    if (i0 < n) a[i0] = ex;
-    if (i1 < n) a[i1] = ex + a0;
-    const double total = wtmp[KA_WARPS];
-    __syncthreads();
-    return total;
-}
-
-// Block-wide exclusive scan of n (<= 2*KA_THREADS) uint32 flags; returns total.
+// Block-wide exclusive scan of n (<= 2*NT) uint32 in place; returns the total.
+template <int NT>
 __device__ uint32_t block_exscan_u(uint32_t *a, uint32_t n, uint32_t *wtmp) {
+    constexpr int NW = NT / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t i0 = 2 * tid, i1 = 2 * tid + 1;
-    const uint32_t a0 = i0 < n ? a[i0] : 0u;
-    const uint32_t a1 = i1 < n ? a[i1] : 0u;
+    const uint32_t a0 = (tid < NT && i0 < n) ? a[i0] : 0u;
+    const uint32_t a1 = (tid < NT && i1 < n) ? a[i1] : 0u;
     uint32_t v = a0 + a1, incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += t;
     }
-    if (lane == 31) wtmp[warp] = incl;
+    if (lane == 31 && warp < NW) wtmp[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-        uint32_t w = lane < KA_WARPS ? wtmp[lane] : 0u, wi = w;
+        uint32_t w = lane < NW ? wtmp[lane] : 0u, wi = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
             if (lane >= o) wi += t;
         }
-        if (lane < KA_WARPS) wtmp[lane] = wi - w;
-        if (lane == KA_WARPS - 1) wtmp[KA_WARPS] = wi;
+        if (lane < NW) wtmp[lane] = wi - w;
+        if (lane == NW - 1) wtmp[NW] = wi;
     }
     __syncthreads();
-    const uint32_t ex = wtmp[warp] + incl - v;
-    if (i0 < n) a[i0] = ex;
-    if (i1 < n) a[i1] = ex + a0;
-    const uint32_t total = wtmp[KA_WARPS];
+    if (tid < NT) {
+        const uint32_t ex = wtmp[warp] + incl - v;
+        if (i0 < n) a[i0] = ex;
+        if (i1 < n) a[i1] = ex + a0;
+    }
+    const uint32_t total = wtmp[NW];
     __syncthreads();
     return total;
 }
 
-// Segmented inclusive scan of composites: head[i] starts a new segment.
-// In: c[i], head[i] for i < n (n <= 2*KA_THREADS).  Out: c[i] = composite
-// from the segment start to i.
+// Segmented inclusive scan of composites over n (<= 2*NT) elements by the
+// first NT threads.  Forward (REV = false): flag[i] starts a segment,
+// c[i] <- c[start..i].  Reverse (REV = true): flag[i] ends a segment,
+// c[i] <- c[i..end] (composition order is always index order).
 struct SegComp {
     uint32_t f;
     Comp c;
 };
-__device__ __forceinline__ SegComp seg_then(SegComp a, SegComp b) {
+template <bool REV>
+__device__ __forceinline__ SegComp seg_then(SegComp a, SegComp b) {   // a precedes b in scan order
     if (b.f) return b;
-    return SegComp{a.f, comp_then(a.c, b.c)};
+    return SegComp{a.f, REV ? comp_then(b.c, a.c) : comp_then(a.c, b.c)};
 }
-__device__ void block_segscan_comp(Comp *c, const uint32_t *head, uint32_t n, SegComp *wtmp) {
+template <bool REV, int NT>
+__device__ void block_segscan_comp(Comp *c, const uint32_t *flag, uint32_t n, SegComp *wtmp) {
+    constexpr int NW = NT / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t i0 = 2 * tid, i1 = 2 * tid + 1;
-    SegComp s0{i0 < n ? head[i0] : 1u, i0 < n ? c[i0] : Comp{0, 0}};
-    SegComp s1{i1 < n ? head[i1] : 1u, i1 < n ? c[i1] : Comp{0, 0}};
-    SegComp v = seg_then(s0, s1);
+    const uint32_t j0 = 2 * tid, j1 = 2 * tid + 1;           // scan order
+    const uint32_t i0 = REV ? n - 1 - j0 : j0, i1 = REV ? n - 2 - j0 : j1;   // physical
+    const bool act = tid < NT;
+    SegComp s0{(act && j0 < n) ? flag[i0] : 1u, (act && j0 < n) ? c[i0] : Comp{0, 0}};
+    SegComp s1{(act && j1 < n) ? flag[i1] : 1u, (act && j1 < n) ? c[i1] : Comp{0, 0}};
+    SegComp v = seg_then<REV>(s0, s1);
     SegComp incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -372,12 +325,12 @@ __device__ void block_segscan_comp(Comp *c, const uint32_t *head, uint32_t n, Se
         t.f = __shfl_up_sync(0xffffffffu, incl.f, o);
         t.c.q0 = __shfl_up_sync(0xffffffffu, incl.c.q0, o);
         t.c.q1 = __shfl_up_sync(0xffffffffu, incl.c.q1, o);
-        if (lane >= o) incl = seg_then(t, incl);
+        if (lane >= o) incl = seg_then<REV>(t, incl);
     }
-    if (lane == 31) wtmp[warp] = incl;
+    if (lane == 31 && warp < NW) wtmp[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-        SegComp w = lane < KA_WARPS ? wtmp[lane] : SegComp{0u, {0, 0}};
+        SegComp w = lane < NW ? wtmp[lane] : SegComp{0u, {0, 0}};
         SegComp wi = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -385,13 +338,12 @@ __device__ void block_segscan_comp(Comp *c, const uint32_t *head, uint32_t n, Se
             t.f = __shfl_up_sync(0xffffffffu, wi.f, o);
             t.c.q0 = __shfl_up_sync(0xffffffffu, wi.c.q0, o);
             t.c.q1 = __shfl_up_sync(0xffffffffu, wi.c.q1, o);
-            if (lane >= o) wi = seg_then(t, wi);
+            if (lane >= o) wi = seg_then<REV>(t, wi);
         }
         __syncwarp();
-        if (lane < KA_WARPS) wtmp[KA_WARPS + 1 + lane] = wi;  // inclusive over warps 0..lane
+        if (lane < NW) wtmp[NW + 1 + lane] = wi;  // inclusive over warps 0..lane
     }
     __syncthreads();
-    // exclusive prefix for this thread = (warp carry) then (lanes before me)
     SegComp excl_lane;
     {
         SegComp t;
@@ -400,485 +352,793 @@ __device__ void block_segscan_comp(Comp *c, const uint32_t *head, uint32_t n, Se
         t.c.q1 = __shfl_up_sync(0xffffffffu, incl.c.q1, 1);
         excl_lane = lane > 0 ? t : SegComp{0u, {0, 0}};
     }
-    SegComp carry = warp > 0 ? wtmp[KA_WARPS + 1 + warp - 1] : SegComp{0u, {0, 0}};
-    SegComp pre = lane > 0 ? seg_then(carry, excl_lane) : carry;
-    // element 0 then element 1
-    SegComp r0 = seg_then(pre, s0);
-    SegComp r1 = seg_then(r0, s1);
+    SegComp carry = (warp > 0 && warp <= NW) ? wtmp[NW + 1 + warp - 1] : SegComp{0u, {0, 0}};
+    SegComp pre = lane > 0 ? seg_then<REV>(carry, excl_lane) : carry;
+    SegComp r0 = seg_then<REV>(pre, s0);
+    SegComp r1 = seg_then<REV>(r0, s1);
     __syncthreads();
-    if (i0 < n) c[i0] = r0.c;
-    if (i1 < n) c[i1] = r1.c;
+    if (act && j0 < n) c[i0] = r0.c;
+    if (act && j1 < n) c[i1] = r1.c;
     __syncthreads();
 }
+// ===========================================================================
+// Decoupled passes.  A row is cut into segments of SEG_TILES tiles; K1 and K2
+// run one CTA per segment with one thread per tile (32 logits in registers).
+//   K1 streams the logits from HBM (L2 evict_last) and writes per-tile
+//      maxima and sums (relative to the tile maximum) plus per-segment
+//      aggregates and histograms; the last CTA of a row to finish reduces them
+//      to the row maximum, the prefix estimate at every segment start and the
+//      candidate floors (no CTA ever waits for another).
+//   K2 runs segments in reverse order, so it re-reads logits K1 left in L2,
+//      classifies tiles, computes the certified grid counts, writes the walk
+//      items and the candidates.
+// ===========================================================================
+constexpr int SEG_TILES = 256;               // tiles per segment == K1/K2 block size
+constexpr int SEG_ELEMS = SEG_TILES * TILE;  // 8192 logits
+constexpr int K12_THREADS = SEG_TILES;
+constexpr int MAX_SEG = 64;                  // vocab <= 524288
+constexpr int KH_BINS = 256;                 // quarter-octave bins over 64 octaves
+constexpr int RED_CHUNK = 4;                 // segments per step of the row reduction
 
-__global__ void __launch_bounds__(KA_THREADS, 2) kernel_a(KAParams P) {
-    cg::cluster_group cluster = cg::this_cluster();
-    const uint32_t rank = cluster.block_rank();
-    const uint32_t row = blockIdx.y;
-    const uint32_t hrow = P.row0 + row;
+// Speculation window of the running sum around the raw prefix estimate: the
+// reference's sum lies below the exact prefix (elements under half an ulp are
+// dropped) by up to ~2e-3 on flat rows, and above it by rounding noise only.
+constexpr double WIN_LO = 4e-3;
+constexpr double WIN_HI = 3e-5;
+
+// Relative error bound of ex2.approx(x2) against the exact p = exp_ref(x/T)
+// (argument and division roundings grow with |x2|; the rest is constant).
+// The GPU test suite checks the bound on millions of samples.
+__device__ __forceinline__ float approx_p_eps(float x2) { return fabsf(x2) * 4.8e-7f + 3.9e-6f; }
+
+__device__ __forceinline__ double pow2d(int k) {   // 2^k, -1022 <= k <= 1023
+    return __longlong_as_double((long long)(k + 1023) << 52);
+}
+
+struct TileStat {
+    float tmax;   // tile maximum (penalised logits)
+    float tsr;    // sum of 2^((v - tmax) log2e / T) over the tile
+};
+
+struct SegStat {
+    float smax;        // segment maximum
+    uint32_t nonfin;   // a non-finite logit in the segment
+    double ssum;       // sum of tile sums relative to smax
+    double base;       // (row reduction) raw prefix estimate at the segment start
+    double pad;
+};
+
+struct RowInfo {   // written by K1's row reduction, read by K2 and K3
+    float M;
+    float xf2;         // candidate floor, log2 p units
+    uint32_t binding;  // 0 none (all p > 0), 1 top-k, 2 top-p, 3 min-p
+    uint32_t check_nan;
+    double S_raw;
+};
+
+struct K12Params {
+    const float *logits;
+    size_t ld;
+    const uint32_t *prev;
+    uint32_t n_prev;
+    uint32_t vocab;
+    uint32_t row0;
+    uint32_t rows;
+    float T;
+    float c2;                 // log2(e) / T (approximate paths only)
+    uint32_t top_k;
+    float top_p;
+    float min_p;
+    uint32_t rep_window;
+    float rep_penalty;
+    uint32_t nseg;
+    uint32_t ntiles_total;
+    TileStat *tstat;          // per handle row: ntiles_total
+    SegStat *sstat;           // per handle row: MAX_SEG
+    uint32_t *khist;          // per handle row: MAX_SEG x KH_BINS tile counts
+    float *mhist;             // per handle row: MAX_SEG x KH_BINS masses
+    uint32_t *done;           // per handle row: K1 segments finished
+    RowInfo *rinfo;           // per handle row
+    RowHdr *hdr;
+    Item *items;
+    WTile *wpre;
+    float *wcdata;
+    Candidate *cand;          // per handle row: cand_stride entries (idx, logit)
+    uint32_t cand_stride;
+};
+
+__device__ __forceinline__ bool penalty_active(const K12Params &P) {
+    return P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ float4 ldg_policy(const float4 *p, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+
+// Load tile t of a row (32 logits; -inf beyond the vocabulary) and apply the
+// repetition penalty (sampler.zig:54-75: each distinct id of the last
+// `window` previous tokens, once).
+__device__ __forceinline__ void load_tile(const K12Params &P, const float *x, uint32_t t, uint64_t pol,
+                                          const uint32_t *win, uint32_t nwin, float v[TILE]) {
+    const uint32_t g0 = t * TILE;
+    if (g0 + TILE <= P.vocab && (reinterpret_cast<uintptr_t>(x + g0) & 15u) == 0) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(x + g0);
+#pragma unroll
+        for (int j = 0; j < TILE / 4; j++) {
+            const float4 q = ldg_policy(x4 + j, pol);
+            v[4 * j] = q.x;
+            v[4 * j + 1] = q.y;
+            v[4 * j + 2] = q.z;
+            v[4 * j + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < TILE; j++) v[j] = (g0 + j < P.vocab) ? x[g0 + j] : NEG_INF;
+    }
+    for (uint32_t j = 0; j < nwin; j++) {
+        const uint32_t id = win[j];
+        if (id - g0 < (uint32_t)TILE) {
+            bool first = true;
+            for (uint32_t jj = 0; jj < j; jj++)
+                if (win[jj] == id) { first = false; break; }
+            if (first) {
+#pragma unroll
+                for (int k = 0; k < TILE; k++) {
+                    if ((uint32_t)k == id - g0) {
+                        const float a = v[k];
+                        v[k] = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
+                    }
+                }
+            }
+        }
+    }
+}
+
+__device__ uint32_t load_window(const K12Params &P, uint32_t row, uint32_t *swin) {
+    if (!penalty_active(P)) return 0;
+    const uint32_t win = min(min(P.n_prev, P.rep_window), 256u);
+    const uint32_t start = P.n_prev - win;
+    for (uint32_t j = threadIdx.x; j < win; j += blockDim.x) swin[j] = P.prev[(size_t)row * P.n_prev + start + j];
+    return win;
+}
+
+// Block-wide (K12_THREADS) exclusive scan of one double per thread.
+__device__ double block_exscan1_d(double v, double *wtmp, double *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int NW = K12_THREADS / 32;
+    double incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) wtmp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        double w = lane < NW ? wtmp[lane] : 0.0, wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double t = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += t;
+        }
+        if (lane < NW) wtmp[lane] = wi - w;
+        if (lane == NW - 1) wtmp[NW] = wi;
+    }
+    __syncthreads();
+    const double ex = wtmp[warp] + incl - v;
+    *total = wtmp[NW];
+    __syncthreads();
+    return ex;
+}
+
+// One warp handles four tiles at a time: lane l holds elements 4(l%8)..+3 of
+// tile l/8 (an 8-lane group per tile, one float4 load per lane).
+__device__ __forceinline__ float4 load_quad(const K12Params &P, const float *x, uint32_t g, uint64_t pol,
+                                            const uint32_t *win, uint32_t nwin) {
+    float4 q;
+    if (g + 4 <= P.vocab && (reinterpret_cast<uintptr_t>(x + g) & 15u) == 0) {
+        q = ldg_policy(reinterpret_cast<const float4 *>(x + g), pol);
+    } else {
+        q.x = g < P.vocab ? x[g] : NEG_INF;
+        q.y = g + 1 < P.vocab ? x[g + 1] : NEG_INF;
+        q.z = g + 2 < P.vocab ? x[g + 2] : NEG_INF;
+        q.w = g + 3 < P.vocab ? x[g + 3] : NEG_INF;
+    }
+    // repetition penalty (sampler.zig:54-75): each distinct id of the last
+    // `window` previous tokens, once
+    for (uint32_t j = 0; j < nwin; j++) {
+        const uint32_t id = win[j];
+        if (id - g < 4u) {
+            bool first = true;
+            for (uint32_t jj = 0; jj < j; jj++)
+                if (win[jj] == id) { first = false; break; }
+            if (first) {
+                float *e = (&q.x) + (id - g);
+                const float a = *e;
+                *e = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
+            }
+        }
+    }
+    return q;
+}
+
+__device__ __forceinline__ float group8_max(float v) {
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+}
+__device__ __forceinline__ float group8_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v + __shfl_xor_sync(0xffffffffu, v, 4);
+}
+__device__ __forceinline__ uint32_t group8_sum_u(uint32_t v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v + __shfl_xor_sync(0xffffffffu, v, 4);
+}
+__device__ __forceinline__ uint32_t group8_or(uint32_t v) {
+    v |= __shfl_xor_sync(0xffffffffu, v, 1);
+    v |= __shfl_xor_sync(0xffffffffu, v, 2);
+    return v | __shfl_xor_sync(0xffffffffu, v, 4);
+}
+
+// ---------------------------------------------------------------------------
+// K1: tile statistics (HBM pass), then the row reduction by the last CTA.
+__global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
+    const uint32_t seg = blockIdx.x, row = blockIdx.y, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t V = P.vocab;
-    const uint32_t NT = P.ntiles_seg;
+    constexpr int NW = K12_THREADS / 32;
+    const float *x = P.logits + (size_t)row * P.ld;
+    const float c2 = P.c2;
+    const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
+    __shared__ uint32_t swin[256];
+    __shared__ uint32_t kh[KH_BINS];
+    __shared__ uint32_t mh[KH_BINS];   // tail element counts per bin
+    __shared__ float stm[SEG_TILES];   // tile maxima of this segment
+    __shared__ float sts[SEG_TILES];   // tile sums relative to the tile maxima
+    __shared__ float wm[NW];
+    __shared__ uint32_t wf[NW];
+    __shared__ double wd[NW];
+    __shared__ uint32_t is_last;
+    const uint32_t nwin = load_window(P, row, swin);
+    for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) {
+        kh[b] = 0u;
+        mh[b] = 0u;
+    }
+    const bool k_floor = P.top_k > 0 && P.top_k < P.vocab && P.top_k <= KSEL_MAX;
+    const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
+    const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
+    const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
+    if (nwin) __syncthreads();
 
-    extern __shared__ __align__(16) unsigned char smem[];
-    float *seg = reinterpret_cast<float *>(smem);
-    double *tsum = reinterpret_cast<double *>(seg + P.seg_len);          // NT
-    double *pref = tsum + NT;                                             // NT
-    float *tmax = reinterpret_cast<float *>(pref + NT);                   // ksort
-    TileRec *rec = reinterpret_cast<TileRec *>(tmax + P.ksort);           // NT
-    uint32_t *uarr = reinterpret_cast<uint32_t *>(rec + NT);              // NT
-    Comp *carr = reinterpret_cast<Comp *>(uarr + NT);                     // NT
-    __shared__ XSlot xs;
-    __shared__ double wtmp_d[KA_WARPS + 1];
-    __shared__ uint32_t wtmp_u[KA_WARPS + 1];
-    __shared__ SegComp wtmp_s[2 * KA_WARPS + 2];
-    __shared__ ArgBest wbest[KA_WARPS];
-    __shared__ float wmax[KA_WARPS];
-    __shared__ uint32_t wnan[KA_WARPS];
-    __shared__ float kth_sh;
-    __shared__ float kgather[MAX_CLUSTER * KSEL_MAX];
-    __shared__ float hist[HIST_BINS];
-    __shared__ float ghist[HIST_BINS];
+    const uint64_t pol = l2_policy_evict_last();
+    const uint32_t sub = lane >> 3, l8 = lane & 7;
+    float smax = NEG_INF;
+    uint32_t nonfin = 0;
+    constexpr int ITERS = SEG_TILES / (4 * NW);   // 8
+    // whole segment in range, 16-byte aligned and without penalised ids:
+    // plain vector loads
+    const bool fast = nwin == 0 && (seg + 1) * SEG_ELEMS <= P.vocab &&
+                      (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
+    const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
+#pragma unroll 4
+    for (int it = 0; it < ITERS; it++) {
+        const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
+        const uint32_t t = seg * SEG_TILES + tl;
+        float4 q;
+        if (fast) {
+            q = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
+        } else {
+            q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+            if (tl < ntile) q = load_quad(P, x, t * TILE + 4 * l8, pol, swin, nwin);
+        }
+        const float tm = group8_max(fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
+        float s = 0.0f;
+        if (tm > NEG_INF) {
+            const float tc = tm * c2;
+            s = ex2_approx(fmaf(q.x, c2, -tc)) + ex2_approx(fmaf(q.y, c2, -tc)) +
+                ex2_approx(fmaf(q.z, c2, -tc)) + ex2_approx(fmaf(q.w, c2, -tc));
+        }
+        s = group8_sum(s);
+        if (l8 == 0 && tl < ntile) {
+            // a non-finite logit may make the sum NaN: +inf shows in the tile
+            // maximum, a NaN (and -inf with T = +inf) in the tile sum
+            nonfin |= (!(fabsf(tm) <= 3.4028235e38f) || s != s) ? 1u : 0u;
+            if (s != s) s = 0.0f;
+            stm[tl] = tm;
+            sts[tl] = s;
+            P.tstat[(size_t)hrow * P.ntiles_total + t] = TileStat{tm, s};
+        }
+        smax = fmaxf(smax, tm);
+    }
+    smax = warp_max(smax);
+    nonfin = __any_sync(0xffffffffu, nonfin != 0) ? 1u : 0u;
+    if (lane == 0) {
+        wm[warp] = smax;
+        wf[warp] = nonfin;
+    }
+    __syncthreads();
+    float sm = wm[0];
+    uint32_t nfs = wf[0];
+#pragma unroll
+    for (int w = 1; w < NW; w++) {
+        sm = fmaxf(sm, wm[w]);
+        nfs |= wf[w];
+    }
+    // segment sum relative to the segment maximum; tile-maximum histogram
+    double ss = 0.0;
+    if ((uint32_t)tid < ntile) {
+        const float tm = stm[tid];
+        if (tm > NEG_INF) {
+            const float xr = (tm - sm) * c2;
+            ss = (double)sts[tid] * (double)ex2_approx(xr);
+            if (k_floor && xr > -64.0f) atomicAdd(&kh[min(KH_BINS - 1, (int)(-xr * 4.0f))], 1u);
+        }
+    }
+    // top-p without a top-k floor: tail-mass histogram relative to the
+    // segment maximum (second read of the segment, from L2)
+    if (p_floor && sm > NEG_INF) {
+        const float sc = sm * c2;
+        for (int it = 0; it < ITERS; it++) {
+            const uint32_t tl = 4 * (warp + NW * it) + sub;
+            if (tl >= ntile) continue;
+            const float4 q = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
+            const float a[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float xr = fmaf(a[k], c2, -sc);   // log2(p / p(segment max))
+                if (xr > -64.0f) atomicAdd(&mh[min(KH_BINS - 1, (int)(-xr * 4.0f))], 1u);
+            }
+        }
+    }
+    ss = warp_sum_d(ss);
+    if (lane == 0) wd[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double s = 0.0;
+        for (int w = 0; w < NW; w++) s += wd[w];
+        SegStat st;
+        st.smax = sm;
+        st.nonfin = nfs;
+        st.ssum = s;
+        st.base = 0.0;
+        st.pad = 0.0;
+        P.sstat[(size_t)hrow * MAX_SEG + seg] = st;
+    }
+    if (k_floor)
+        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) P.khist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = kh[b];
+    if (p_floor)
+        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS)   // mass bound: count x the bin's upper edge
+            P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = (float)mh[b] * exp2f(-0.25f * (float)b);
+    // the last segment of the row to finish reduces the row
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = (atomicAdd(&P.done[hrow], 1u) == P.nseg - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
 
-    RowHdr *hdr = P.hdr + hrow;
-    const uint32_t seg0 = rank * P.seg_len;
-    const uint32_t segn = seg0 < V ? min(P.seg_len, V - seg0) : 0u;
-    const uint32_t tile0 = rank * NT;
-    const float *src = P.logits + (size_t)row * P.ld + seg0;
-
-    if (rank == 0 && tid == 0) {
+    __shared__ float off[MAX_SEG];   // (segment max - M) log2e / T
+    __shared__ float ssc[MAX_SEG];   // segment tail mass scale 2^off
+    __shared__ RowInfo ri;
+    const SegStat *S = P.sstat + (size_t)hrow * MAX_SEG;
+    const uint32_t ns = P.nseg;
+    if (warp == 0) {
+        float m = NEG_INF;
+        uint32_t nf = 0;
+        for (uint32_t c = lane; c < ns; c += 32) {
+            const SegStat st = S[c];
+            m = fmaxf(m, st.smax);
+            nf |= st.nonfin;
+        }
+        m = warp_max(m);
+        nf = __any_sync(0xffffffffu, nf != 0) ? 1u : 0u;
+        // raw prefix at each segment start, in units of p(M) = 1
+        double run = 0.0;
+        for (uint32_t c0 = 0; c0 < ns; c0 += 32) {
+            const uint32_t c = c0 + lane;
+            double sv = 0.0;
+            float o = NEG_INF;
+            if (c < ns) {
+                const SegStat st = S[c];
+                o = (st.smax > NEG_INF) ? (st.smax - m) * c2 : NEG_INF;
+                sv = st.smax > NEG_INF ? st.ssum * (double)ex2_approx(o) : 0.0;
+                off[c] = o;
+                ssc[c] = ex2_approx(o);
+            }
+            double incl = sv;
+#pragma unroll
+            for (int k = 1; k < 32; k <<= 1) {
+                const double u = __shfl_up_sync(0xffffffffu, incl, k);
+                if (lane >= k) incl += u;
+            }
+            if (c < ns) {
+                P.sstat[(size_t)hrow * MAX_SEG + c].base = run + incl - sv;
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) {
+            ri.M = m;
+            ri.check_nan = nf | ((P.T != P.T) ? 1u : 0u);
+            ri.S_raw = run;
+        }
+    }
+    __syncthreads();
+    // floors on the quarter-octave grid f_j = -j/4 (log2 p, relative to M).
+    // Segment c's bin b spans [off_c - (b+1)/4, off_c - b/4).  One warp per
+    // segment turns its histograms into cumulative ones in shared memory;
+    // then thread j evaluates grid point j.
+    // Segments are processed in chunks of RED_CHUNK: one warp per segment
+    // turns its histograms into cumulative ones in shared memory, then thread
+    // j accumulates grid point j.
+    __shared__ uint32_t cumk[RED_CHUNK * KH_BINS];
+    __shared__ float cumm[RED_CHUNK * KH_BINS];
+    __shared__ float mtot[RED_CHUNK];
+    const uint32_t *KH = P.khist + (size_t)hrow * MAX_SEG * KH_BINS;
+    const float *MH = P.mhist + (size_t)hrow * MAX_SEG * KH_BINS;
+    uint32_t kcount = 0;   // tiles whose maximum is surely >= f_j (under-count)
+    float mbelow = 0.0f;   // mass possibly below f_j (over-count), units of p(M)
+    if (k_floor || p_floor) {
+        for (uint32_t c0 = 0; c0 < ns; c0 += RED_CHUNK) {
+            const uint32_t nc = min((uint32_t)RED_CHUNK, ns - c0);
+            __syncthreads();
+            for (uint32_t cc = warp; cc < nc; cc += NW) {
+                const uint32_t c = c0 + cc;
+                uint32_t kc[8];
+                float mc[8];
+                uint32_t ks = 0;
+                float ms = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    kc[j] = k_floor ? KH[(size_t)c * KH_BINS + lane * 8 + j] : 0u;
+                    mc[j] = p_floor ? MH[(size_t)c * KH_BINS + lane * 8 + j] : 0.0f;
+                    ks += kc[j];
+                    ms += mc[j];
+                    kc[j] = ks;
+                    mc[j] = ms;
+                }
+                uint32_t ki = ks;
+                float mi = ms;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t u = __shfl_up_sync(0xffffffffu, ki, o);
+                    const float w2 = __shfl_up_sync(0xffffffffu, mi, o);
+                    if (lane >= o) {
+                        ki += u;
+                        mi += w2;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    cumk[cc * KH_BINS + lane * 8 + j] = kc[j] + ki - ks;
+                    cumm[cc * KH_BINS + lane * 8 + j] = mc[j] + mi - ms;
+                }
+                if (lane == 31) mtot[cc] = mi;
+            }
+            __syncthreads();
+            for (uint32_t cc = 0; cc < nc; cc++) {
+                const float o = off[c0 + cc];
+                if (!(o > NEG_INF)) continue;
+                // bins entirely above f_j: b <= floor(4 o) + j - 1
+                const float fb = floorf(4.0f * o);
+                const int bmax = fb < -1e6f ? -1 : min(KH_BINS - 1, (int)fb + tid - 1);
+                kcount += bmax >= 0 ? cumk[cc * KH_BINS + bmax] : 0u;
+                const float ma = bmax >= 0 ? cumm[cc * KH_BINS + bmax] : 0.0f;
+                // mass below -64 octaves of the segment maximum is not binned:
+                // at most SEG_ELEMS * 2^-64 of it
+                mbelow += (mtot[cc] - ma + 4.4e-16f) * ssc[c0 + cc];
+            }
+        }
+    }
+    const uint32_t kmask = __ballot_sync(0xffffffffu, kcount >= P.top_k);
+    __shared__ int kj_w[NW], pj_w[NW];
+    const double budget = (1.0 - (double)P.top_p - p_margin) * fmax(1.0, 0.99 * ri.S_raw);
+    const uint32_t pmask = __ballot_sync(0xffffffffu, (double)mbelow * 1.01 + 1e-30 <= budget);
+    if (lane == 0) {
+        kj_w[warp] = kmask ? warp * 32 + __ffs(kmask) - 1 : 1 << 20;
+        pj_w[warp] = pmask ? warp * 32 + __ffs(pmask) - 1 : 1 << 20;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int kj = 1 << 20, pj = 1 << 20;
+        for (int w = 0; w < NW; w++) {
+            kj = min(kj, kj_w[w]);
+            pj = min(pj, pj_w[w]);
+        }
+        float xf2 = -150.01f;   // every p > 0
+        uint32_t binding = 0;
+        if (k_floor && kj < KH_BINS) {
+            const float xk = -(float)kj * 0.25f - 1e-3f;
+            if (xk > xf2) { xf2 = xk; binding = 1; }
+        }
+        if (p_floor && pj < KH_BINS) {
+            const float xp = -(float)pj * 0.25f - 1e-3f;
+            if (xp > xf2) { xf2 = xp; binding = 2; }
+        }
+        if (P.min_p > 0.0f) {
+            const float xm = fminf(0.0f, log2f(P.min_p)) - 0.01f;
+            if (xm > xf2) { xf2 = xm; binding = 3; }
+        }
+        RowInfo r = ri;
+        r.xf2 = xf2;
+        r.binding = binding;
+        P.rinfo[hrow] = r;
+        RowHdr *hdr = P.hdr + hrow;
+        hdr->M = r.M;
+        hdr->v_floor = xf2;
+        hdr->binding = binding;
+        hdr->s_approx = (float)r.S_raw;
         hdr->n_cand = 0;
         hdr->n_wc = 0;
         hdr->flags = 0;
-        hdr->nseg = P.C;
+        hdr->nseg = ns;
+        P.done[hrow] = 0;   // ready for the next call
     }
+}
 
-    // ---- phase 1: segment -> shared memory; raw argmax; penalised max -----
-    ArgBest best{NEG_INF, 0xFFFFFFFFu};
-    float lmax = NEG_INF;
-    {
-        uint32_t done = 0;
-        if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-            const uint32_t n4 = segn / 4;
-            const float4 *s4 = reinterpret_cast<const float4 *>(src);
-            float4 *d4 = reinterpret_cast<float4 *>(seg);
-            uint32_t i = tid;
-            for (; i + 3 * KA_THREADS < n4; i += 4 * KA_THREADS) {
-                float4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) v[u] = ldg_stream(s4 + i + u * KA_THREADS);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    d4[i + u * KA_THREADS] = v[u];
-                    const float a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        lmax = fmaxf(lmax, a[k]);
-                        best = arg_better(best, ArgBest{a[k] != a[k] ? NEG_INF : a[k],
-                                                        seg0 + 4 * (i + u * KA_THREADS) + k});
-                    }
-                }
-            }
-            for (; i < n4; i += KA_THREADS) {
-                const float4 v = ldg_stream(s4 + i);
-                d4[i] = v;
-                const float a[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    lmax = fmaxf(lmax, a[k]);
-                    best = arg_better(best, ArgBest{a[k] != a[k] ? NEG_INF : a[k], seg0 + 4 * i + k});
-                }
-            }
-            done = n4 * 4;
-        }
-        for (uint32_t i = done + tid; i < segn; i += KA_THREADS) {
-            const float a = src[i];
-            seg[i] = a;
-            lmax = fmaxf(lmax, a);
-            best = arg_better(best, ArgBest{a != a ? NEG_INF : a, seg0 + i});
-        }
-        for (uint32_t i = segn + tid; i < NT * TILE; i += KA_THREADS) seg[i] = NEG_INF;
-    }
-    if (rank == 0 && tid == 0) xs.nan_any = (segn > 0 && src[0] != src[0]) ? 1u : 0u;  // leading NaN
-    // repetition penalty (sampler.zig:54-75): each distinct id of the last
-    // `window` previous tokens, once.
-    const bool pen = penalty_active(P);
-    if (pen) {
-        __syncthreads();
-        const uint32_t win = min(P.n_prev, P.rep_window);
-        const uint32_t start = P.n_prev - win;
-        const uint32_t *pv = P.prev + (size_t)row * P.n_prev + start;
-        for (uint32_t j = tid; j < win; j += KA_THREADS) {
-            const uint32_t id = pv[j];
-            bool first = true;
-            for (uint32_t jj = 0; jj < j; jj++)
-                if (pv[jj] == id) { first = false; break; }
-            if (first && id >= seg0 && id < seg0 + segn) {
-                const float v = seg[id - seg0];
-                seg[id - seg0] = v > 0.0f ? __fdiv_rn(v, P.rep_penalty) : __fmul_rn(v, P.rep_penalty);
-            }
-        }
-        __syncthreads();
-        lmax = NEG_INF;
-        for (uint32_t i = tid; i < segn; i += KA_THREADS) lmax = fmaxf(lmax, seg[i]);
-    }
-    best = warp_arg(best);
-    lmax = warp_max(lmax);
-    if (lane == 0) {
-        wbest[warp] = best;
-        wmax[warp] = lmax;
-    }
-    __syncthreads();
+// ---------------------------------------------------------------------------
+// K2: classification, certified grid counts, candidates, walk items.
+__global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
+    // rows in reverse order: the rows K1 streamed last are still in L2; the
+    // first segments (most of the exact-pass tiles) start first
+    const uint32_t seg = blockIdx.x, row = P.rows - 1 - blockIdx.y, hrow = P.row0 + row;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = K12_THREADS / 32;
+    const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
+    const bool live = (uint32_t)tid < ntile;   // thread-per-tile phases below
+    const float *x = P.logits + (size_t)row * P.ld;
+    const float c2 = P.c2, T = P.T;
+    const RowInfo ri = P.rinfo[hrow];
+    const float M = ri.M;
+    RowHdr *hdr = P.hdr + hrow;
+
+    __shared__ uint32_t swin[256];
+    __shared__ double wtmp_d[NW + 1];
+    __shared__ uint32_t wtmp_u[NW + 1];
+    __shared__ SegComp wtmp_s[2 * NW + 2];
+    __shared__ TileRec rec[SEG_TILES];
+    __shared__ TileParam tpar[SEG_TILES];
+    __shared__ uint32_t uarr[SEG_TILES], uarr2[SEG_TILES];
+    __shared__ Comp carr[SEG_TILES], carr2[SEG_TILES];
+    __shared__ uint32_t wlist[SEG_TILES];
+    __shared__ uint32_t nlist, nanflag;
+    const uint32_t nwin = load_window(P, row, swin);
     if (tid == 0) {
-        ArgBest b = wbest[0];
-        float m = wmax[0];
-        for (int w = 1; w < KA_WARPS; w++) {
-            b = arg_better(b, wbest[w]);
-            m = fmaxf(m, wmax[w]);
-        }
-        xs.pmax = m;
-        xs.rmax = b.v;
-        xs.rarg = b.i;
+        nlist = 0;
+        nanflag = 0;
     }
-    cluster.sync();  // #1
 
-    // ---- phase 2: row max ----------------------------------------------------
-    float M = NEG_INF;
+    // raw prefix estimate at every tile start of the segment, and from it
+    // each tile's candidate binades of the running sum
     {
-        ArgBest b{NEG_INF, 0xFFFFFFFFu};
-        for (uint32_t r = 0; r < P.C; r++) {
-            const XSlot *o = cluster.map_shared_rank(&xs, r);
-            M = fmaxf(M, o->pmax);
-            b = arg_better(b, ArgBest{o->rmax, o->rarg});
+        double ct = 0.0;
+        if (live) {
+            const TileStat ts = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
+            ct = ts.tmax > NEG_INF ? (double)ts.tsr * (double)ex2_approx((ts.tmax - M) * c2) : 0.0;
         }
-        if (rank == 0 && tid == 0) {
-            hdr->M = M;
-            hdr->raw_max = b.v;
-            hdr->raw_arg = (xs.nan_any || b.i == 0xFFFFFFFFu) ? 0u : b.i;
-            for (uint32_t r = 0; r < P.C; r++) hdr->seg_tile0[r] = r * NT;
-        }
+        double segtot;
+        const double Ps = P.sstat[(size_t)hrow * MAX_SEG + seg].base + block_exscan1_d(ct, wtmp_d, &segtot);
+        const double Pe = Ps + ct;
+        const int lo = binade_of(Ps * (1.0 - WIN_LO));
+        const int hi = binade_of(Pe * (1.0 + WIN_HI));
+        TileParam tp;
+        tp.lo = lo;
+        tp.cls = hi == lo ? CLS_SIMPLE : (hi == lo + 1 ? CLS_WINDOW : CLS_COMPLEX);
+        tp.special = (tp.cls == CLS_COMPLEX || lo < -100) ? 1u : 0u;
+        tp.K = (float)(23 - max(lo, -100));        // log2(p / u_lo) = x2 + K
+        tp.thr = (float)(lo - 24) - 0.01f;         // p < u_lo / 2 below this
+        tpar[tid] = tp;
     }
-    const float T = P.T;
-    const float c2 = P.c2;
-    const bool t_nan = (T != T);
-    const bool t_inf = isinf(T);
-
-    // ---- phase 3a: approximate tile sums and tile maxima ---------------------
-    uint32_t nan_local = 0;
-    for (uint32_t t = warp; t < NT; t += KA_WARPS) {
-        const float v = seg[t * TILE + lane];
-        const float d = __fsub_rn(v, M);
-        const bool real = seg0 + t * TILE + lane < V;   // not padding
-        const bool isn = real && ((d != d) || t_nan || (isinf(d) && t_inf));
-        nan_local |= isn ? 1u : 0u;
-        const float x2 = (d == 0.0f) ? 0.0f : d * c2;
-        const float pt = isn ? 0.0f : ex2_approx(x2);
-        const float s = warp_sum(pt);
-        const float mx = warp_max(v);
-        if (lane == 0) {
-            tsum[t] = (double)s;
-            tmax[t] = mx;
-        }
-    }
-    nan_local = __any_sync(0xffffffffu, nan_local != 0) ? 1u : 0u;
-    if (lane == 0) wnan[warp] = nan_local;
-    for (uint32_t t = NT + tid; t < P.ksort; t += KA_THREADS) tmax[t] = NEG_INF;
-    __syncthreads();
-    if (tid == 0) {
-        uint32_t n = 0;
-        for (int w = 0; w < KA_WARPS; w++) n |= wnan[w];
-        xs.nan_any = n;   // (the leading-NaN bit was consumed in phase 2)
-    }
-    {
-        for (uint32_t t = tid; t < NT; t += KA_THREADS) pref[t] = tsum[t];
-        __syncthreads();
-        const double tot = block_exscan_d(pref, NT, wtmp_d);
-        if (tid == 0) xs.tot_raw = tot;
-    }
-    cluster.sync();  // #2
-    double base_raw = 0.0, s_raw = 0.0;
-    uint32_t row_nan = 0;
-    for (uint32_t r = 0; r < P.C; r++) {
-        const XSlot *o = cluster.map_shared_rank(&xs, r);
-        if (r < rank) base_raw += o->tot_raw;
-        s_raw += o->tot_raw;
-        row_nan |= o->nan_any;
-    }
-
-    // top-p tail-mass histogram: elements with log2 p >= f0 (f0 bounds the mass
-    // below it by a quarter of the top-p budget, V * 2^f0 <= (1-top_p) S / 4)
-    const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
-    const bool hist_on = p_active && (1.0f - P.top_p) >= 1e-3f;
-    const double s_lo = fmax(1.0, 0.99 * s_raw);
-    const float f0 = hist_on ? (float)(log2((1.0 - (double)P.top_p) * s_lo / (4.0 * (double)V)) - 1e-3)
-                             : 0.0f;
-    const float binw = fmaxf(0.125f, -f0 / (float)HIST_BINS);
-    const float inv_binw = 1.0f / binw;
-    for (uint32_t b = tid; b < HIST_BINS; b += KA_THREADS) hist[b] = 0.0f;
     __syncthreads();
 
-    // ---- phase 3b: rounding-aware tile sums ---------------------------------
-    for (uint32_t t = warp; t < NT; t += KA_WARPS) {
-        const double Pt = base_raw + pref[t];
-        const int e = binade_of(Pt);
-        const float v = seg[t * TILE + lane];
-        const float d = __fsub_rn(v, M);
-        const bool isn = (d != d) || t_nan || (isinf(d) && t_inf);
-        const float x2 = (d == 0.0f) ? 0.0f : d * c2;
-        float q = 0.0f, big = 0.0f;
-        const float ex = x2 - (float)(e - 23);   // log2(p / u_e)
-        if (!isn && ex >= -1.01f) {
-            if (ex < 22.0f) {
-                const float y = ex2_approx(ex);
-                q = (y + 12582912.0f) - 12582912.0f;  // round to the grid (rint)
-            } else {
-                big = ex2_approx(x2);                 // far above the grid: p itself
-            }
-        }
-        if (hist_on && !isn && x2 >= f0) {
-            const int b = min(HIST_BINS - 1, (int)((x2 - f0) * inv_binw));
-            atomicAdd(&hist[b], ex2_approx(x2));
-        }
-        const float s = warp_sum(q);
-        const float sb = warp_sum(big);
-        if (lane == 0) tsum[t] = (double)s * exp2((double)(e - 23)) + (double)sb;
-    }
-    __syncthreads();
-    {
-        for (uint32_t t = tid; t < NT; t += KA_THREADS) pref[t] = tsum[t];
-        __syncthreads();
-        const double tot = block_exscan_d(pref, NT, wtmp_d);
-        if (tid == 0) xs.tot2 = tot;
-    }
-
-    // ---- candidate floor: top-k tile-max sort (local part) -------------------
-    const bool k_active = P.top_k > 0 && P.top_k < V;
-    const bool k_floor = k_active && P.top_k <= KSEL_MAX && P.ntiles_total >= P.top_k;
-    if (k_floor) {
-        // bitonic sort, descending, of tmax[0..ksort)
-        for (uint32_t size = 2; size <= P.ksort; size <<= 1) {
-            for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-                __syncthreads();
-                for (uint32_t i = tid; i < P.ksort / 2; i += KA_THREADS) {
-                    const uint32_t lo_i = 2 * i - (i & (stride - 1));
-                    const uint32_t hi_i = lo_i + stride;
-                    const bool desc = ((lo_i & size) == 0);
-                    const float a = tmax[lo_i], b = tmax[hi_i];
-                    if (desc ? (a < b) : (a > b)) {
-                        tmax[lo_i] = b;
-                        tmax[hi_i] = a;
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        if (tid == 0) xs.klen = min(P.top_k, NT);
-    }
-    cluster.sync();  // #3
-    double base2 = 0.0, s_tot = 0.0;
-    for (uint32_t r = 0; r < P.C; r++) {
-        const XSlot *o = cluster.map_shared_rank(&xs, r);
-        if (r < rank) base2 += o->tot2;
-        s_tot += o->tot2;
-    }
-    if (hist_on) {
-        for (uint32_t b = tid; b < HIST_BINS; b += KA_THREADS) {
-            float m = 0.0f;
-            for (uint32_t r = 0; r < P.C; r++) m += cluster.map_shared_rank(hist, r)[b];
-            ghist[b] = m;
-        }
-        __syncthreads();
-    }
-    float xk2 = NEG_INF;
-    if (k_floor) {
-        const uint32_t K = P.top_k;
-        // gather every CTA's sorted top list
-        uint32_t lens[MAX_CLUSTER];
-        for (uint32_t r = 0; r < P.C; r++) {
-            const XSlot *o = cluster.map_shared_rank(&xs, r);
-            lens[r] = o->klen;
-            const float *lst = cluster.map_shared_rank(tmax, r);
-            for (uint32_t j = tid; j < o->klen; j += KA_THREADS) kgather[r * KSEL_MAX + j] = lst[j];
-        }
-        if (tid == 0) kth_sh = NEG_INF;
-        __syncthreads();
-        // the K-th largest value w satisfies  #(> w) < K <= #(>= w)
-        const uint32_t total = P.C * KSEL_MAX;
-        for (uint32_t i = tid; i < total; i += KA_THREADS) {
-            const uint32_t r0 = i / KSEL_MAX, j0 = i % KSEL_MAX;
-            if (j0 >= lens[r0]) continue;
-            const float w = kgather[i];
-            uint32_t gt = 0, ge = 0;
-            for (uint32_t r = 0; r < P.C; r++) {
-                const float *l = kgather + r * KSEL_MAX;
-                uint32_t a = 0, b = lens[r];  // count of l[j] > w (sorted desc)
-                while (a < b) {
-                    const uint32_t mid = (a + b) >> 1;
-                    if (l[mid] > w) a = mid + 1; else b = mid;
-                }
-                gt += a;
-                uint32_t a2 = a, b2 = lens[r];  // count of l[j] >= w
-                while (a2 < b2) {
-                    const uint32_t mid = (a2 + b2) >> 1;
-                    if (l[mid] >= w) a2 = mid + 1; else b2 = mid;
-                }
-                ge += a2;
-            }
-            if (gt < K && K <= ge) kth_sh = w;   // unique value; benign race
-        }
-        __syncthreads();
-        const float vk = kth_sh;
-        const float dk = __fsub_rn(vk, M);
-        xk2 = (dk == 0.0f ? 0.0f : dk * c2) - 1e-3f - fabsf(dk * c2) * 1e-6f;
-    }
-    cluster.sync();  // #4: no distributed shared memory access after this point
-
-    // floors in log2 units of p (x2 = log2 p, approximately)
-    float xf2 = -151.0f;   // p > 0 only
-    uint32_t binding = 0;  // 0 none, 1 k, 2 p, 3 min-p
-    if (k_floor && xk2 > xf2) { xf2 = xk2; binding = 1; }
-    if (hist_on) {
-        // highest bin edge f* with (mass in [f0, f*)) <= (1-top_p) S / 4, so the
-        // mass below f* is at most half of the top-p budget: the cumulative
-        // probability of the tokens above f* exceeds top_p with margin.
-        const float budget = (float)((1.0 - (double)P.top_p) * s_lo / 4.0);
-        float acc = 0.0f;
-        int bstar = 0;
-        for (int b = 0; b < HIST_BINS; b++) {
-            acc += ghist[b] * 1.001f;
-            if (acc > budget) break;
-            bstar = b + 1;
-        }
-        const float xp = f0 + (float)bstar * binw - 1e-3f;
-        if (xp > xf2) { xf2 = xp; binding = 2; }
-    }
-    if (P.min_p > 0.0f) {
-        const double xm = fmin(0.0, log2((double)P.min_p)) - 0.01;
-        if ((float)xm > xf2) { xf2 = (float)xm; binding = 3; }
-    }
-    if (rank == 0 && tid == 0) {
-        hdr->s_approx = (float)s_tot;
-        hdr->v_floor = xf2;
-        hdr->binding = binding;
-        if (row_nan) hdr->flags |= RF_NAN;
-    }
-
-    // ---- phase 4: classify tiles, grid counts, candidates ---------------------
+    const float xf2 = ri.xf2;
+    const uint64_t pol = l2_policy_evict_first();
+    const uint32_t sub = lane >> 3, l8 = lane & 7;
+    const bool t_nan = T != T, t_inf = isinf(T);
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
-    float *wcd = P.wcdata + (size_t)hrow * WC_CAP * TILE;
-    for (uint32_t t = warp; t < NT; t += KA_WARPS) {
-        const double Ps = base2 + pref[t];
-        const double Pe = Ps + tsum[t];
-        const int lo = binade_of(Ps * (1.0 - DELTA));
-        const int hi = binade_of(Pe * (1.0 + DELTA));
-        const uint32_t cls = hi == lo ? CLS_SIMPLE : (hi == lo + 1 ? CLS_WINDOW : CLS_COMPLEX);
-        const uint32_t gidx = seg0 + t * TILE + lane;
-        const float v = seg[t * TILE + lane];
-        const float d = __fsub_rn(v, M);
-        const float x2 = (d == 0.0f) ? 0.0f : d * c2;
-        const bool valid = gidx < V && !row_nan;
-        const bool sig = valid && (lo - 24 <= -149 || x2 >= (float)(lo - 24) - 0.01f);
-        const bool cnd = valid && x2 >= xf2;
-        float p = 0.0f;
-        if (sig || cnd || (valid && cls != CLS_SIMPLE)) p = prob_unnorm(v, M, T);
-        Comp clo{0u, 0u}, chi{0u, 0u};
-        if (sig) {
-            clo = elem_comp(p, lo);
-            if (cls == CLS_WINDOW) chi = elem_comp(p, lo + 1);
+    constexpr int ITERS = SEG_TILES / (4 * NW);   // 8
+    uint32_t nanl = 0;
+#pragma unroll 2
+    for (int it = 0; it < ITERS; it++) {
+        const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
+        const uint32_t t = seg * SEG_TILES + tl;
+        const bool tlive = tl < ntile;
+        const uint32_t g0 = t * TILE + 4 * l8;
+        float4 q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+        if (tlive) q = load_quad(P, x, g0, pol, swin, nwin);
+        const float a[4] = {q.x, q.y, q.z, q.w};
+        const TileParam tp = tpar[tl < SEG_TILES ? tl : 0];
+        const int lo = tp.lo;
+        const uint32_t cls = tp.cls;
+        uint32_t special = tp.special;
+        uint32_t qlo = 0, qhi = 0, nc = 0;
+        float x2v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float d = __fsub_rn(a[k], M);
+            if (ri.check_nan) nanl |= (g0 + k < P.vocab && ((d != d) || t_nan || (isinf(d) && t_inf))) ? 1u : 0u;
+            const float x2 = (d == 0.0f) ? 0.0f : d * c2;
+            x2v[k] = x2;
+            nc += x2 >= xf2 ? 1u : 0u;
+            // grid count from the fast exp, certified by its error bound
+            // (branch-free: evaluated for every element, used when x2 >= thr)
+            const float y = fminf(ex2_approx(x2 + tp.K), 1048576.0f);
+            const float eps = fmaf(x2, -4.8e-7f, 4.0e-6f);       // approx_p_eps(x2) + the shift's rounding
+            const float yr = y + 12582912.0f;                     // rint via 1.5 * 2^23
+            bool ok = y < 1048576.0f && fabsf(y - (yr - 12582912.0f)) < fmaf(-y, eps, 0.5f - 1e-6f);
+            uint32_t ih = 0;
+            if (cls == CLS_WINDOW) {
+                const float yh = 0.5f * y;
+                const float yhr = yh + 12582912.0f;
+                ok = ok && fabsf(yh - (yhr - 12582912.0f)) < fmaf(-yh, eps, 0.5f - 1e-6f);
+                ih = __float_as_uint(yhr) - 0x4B400000u;
+            }
+            const bool sig = x2 >= tp.thr;
+            special |= (sig && !ok) ? 1u : 0u;   // large or near a rounding boundary: exact pass
+            qlo += sig ? __float_as_uint(yr) - 0x4B400000u : 0u;
+            qhi += sig ? ih : 0u;
         }
-        if (__any_sync(0xffffffffu, sig)) {
-            clo = warp_comp_reduce(clo);
-            if (cls == CLS_WINDOW) chi = warp_comp_reduce(chi);
+        qlo = group8_sum_u(qlo);
+        qhi = group8_sum_u(qhi);
+        special = group8_or(special);
+        if (l8 == 0 && tlive) {
+            TileRec rr;
+            rr.lo = lo;
+            rr.cls = cls;
+            rr.aux = 0xFFFFFFFFu;
+            rr.qlo = Comp{qlo, qlo};
+            rr.qhi = Comp{qhi, qhi};
+            rec[tl] = rr;
+            if (special) wlist[atomicAdd(&nlist, 1u)] = tl;
         }
-        const uint32_t cmask = __ballot_sync(0xffffffffu, cnd && p > 0.0f);
-        if (cmask) {
-            uint32_t basec = 0;
-            if (lane == 0) basec = atomicAdd(&hdr->n_cand, (uint32_t)__popc(cmask));
-            basec = __shfl_sync(0xffffffffu, basec, 0);
-            if (cnd && p > 0.0f) {
-                const uint32_t pos = basec + __popc(cmask & ((1u << lane) - 1u));
-                if (pos < P.cand_stride) cand[pos] = Candidate{gidx, p};
+        // candidates (index, logit): warp-aggregated reservation
+        if (__any_sync(0xffffffffu, nc != 0)) {
+            uint32_t incl = nc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += u;
+            }
+            const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+            uint32_t cb = 0;
+            if (lane == 31) cb = atomicAdd(&hdr->n_cand, wtot);
+            cb = __shfl_sync(0xffffffffu, cb, 31);
+            uint32_t pos = cb + incl - nc;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (x2v[k] >= xf2) {
+                    if (pos < P.cand_stride) cand[pos] = Candidate{g0 + k, a[k]};
+                    pos++;
+                }
             }
         }
-        uint32_t aux = 0;
-        if (cls != CLS_SIMPLE) {
+    }
+    if (__any_sync(0xffffffffu, nanl != 0) && lane == 0) atomicOr(&nanflag, 1u);
+    __syncthreads();
+    if (nanflag && tid == 0) atomicOr(&hdr->flags, RF_NAN);
+    // warp-cooperative exact pass (lane = element, index order) for tiles
+    // whose counts need ordered composition (ties), tiny binades or several
+    // binades; several-binade tiles also keep their exact p for the walker
+    const uint32_t nl = nlist;
+    float *wcd = P.wcdata + (size_t)hrow * WC_CAP * TILE;
+    for (uint32_t li = warp; li < nl; li += NW) {
+        const uint32_t lt = wlist[li];
+        const uint32_t tt = seg * SEG_TILES + lt;
+        TileRec r = rec[lt];
+        const uint32_t g = tt * TILE + lane;
+        float a = NEG_INF;
+        if (g < P.vocab) a = x[g];
+        // the penalty, as in load_tile
+        for (uint32_t j = 0; j < nwin; j++) {
+            if (swin[j] == g) {
+                bool first = true;
+                for (uint32_t jj = 0; jj < j; jj++)
+                    if (swin[jj] == g) { first = false; break; }
+                if (first) a = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
+                break;
+            }
+        }
+        const float p = g < P.vocab ? prob_unnorm(a, M, T) : 0.0f;
+        r.qlo = warp_comp_reduce(elem_comp(p, r.lo));
+        if (r.cls == CLS_WINDOW) r.qhi = warp_comp_reduce(elem_comp(p, r.lo + 1));
+        if (r.cls == CLS_COMPLEX) {
             uint32_t slot = 0;
             if (lane == 0) slot = atomicAdd(&hdr->n_wc, 1u);
             slot = __shfl_sync(0xffffffffu, slot, 0);
             if (slot < WC_CAP) {
-                wcd[slot * TILE + lane] = sig ? p : 0.0f;
-                aux = slot;
-            } else {
-                aux = 0xFFFFFFFFu;
+                wcd[slot * TILE + lane] = p;
+                r.aux = slot;
             }
         }
-        if (lane == 0) {
-            TileRec r;
-            r.lo = lo;
-            r.cls = cls;
-            r.aux = aux;
-            r.qlo = clo;
-            r.qhi = chi;
-            rec[t] = r;
-        }
+        if (lane == 0) rec[lt] = r;
     }
     __syncthreads();
 
-    // ---- phase 5: items ------------------------------------------------------
-    // head[t]: tile t starts an item (every WINDOW/COMPLEX tile, and a SIMPLE
-    // tile whose predecessor is not a SIMPLE tile of the same binade).
-    for (uint32_t t = tid; t < NT; t += KA_THREADS) {
-        const TileRec r = rec[t];
-        uint32_t h = 1;
-        if (t > 0) {
-            const TileRec q = rec[t - 1];
-            h = (r.cls != CLS_SIMPLE || q.cls != CLS_SIMPLE || r.lo != q.lo) ? 1u : 0u;
+    // ---- items: a stretch of SIMPLE tiles of one binade, a stretch of WINDOW
+    // tiles of one lower binade, or one COMPLEX tile
+    const uint32_t NT = ntile;
+    if (live) {
+        const TileRec r = rec[tid];
+        uint32_t h = 1, e = 1;
+        if (tid > 0) {
+            const TileRec q = rec[tid - 1];
+            h = (r.cls == CLS_COMPLEX || q.cls != r.cls || r.lo != q.lo) ? 1u : 0u;
         }
-        uarr[t] = h;
-        carr[t] = r.qlo;
+        if ((uint32_t)tid + 1 < NT) {
+            const TileRec q = rec[tid + 1];
+            e = (r.cls == CLS_COMPLEX || q.cls != r.cls || r.lo != q.lo) ? 1u : 0u;
+        }
+        uarr[tid] = h;
+        uarr2[tid] = e;
+        carr[tid] = r.qlo;
+        carr2[tid] = r.qhi;
     }
     __syncthreads();
-    block_segscan_comp(carr, uarr, NT, wtmp_s);   // carr[t]: composite from item start to t
-    const uint32_t nitems = block_exscan_u(uarr, NT, wtmp_u);  // uarr[t]: heads before t
-    uint32_t *sstart = reinterpret_cast<uint32_t *>(tmax);     // free after the floor phase
-    for (uint32_t t = tid; t < NT; t += KA_THREADS) {
-        const uint32_t nxt = (t + 1 < NT) ? uarr[t + 1] : nitems;
-        if (nxt != uarr[t]) sstart[uarr[t]] = t;             // t is a head
+    block_segscan_comp<false, K12_THREADS / 2>(carr, uarr, NT, wtmp_s);
+    block_segscan_comp<true, K12_THREADS / 2>(carr2, uarr2, NT, wtmp_s);
+    const uint32_t nitems = block_exscan_u<K12_THREADS / 2>(uarr, NT, wtmp_u);
+    uint32_t *sstart = uarr2;
+    __syncthreads();
+    if (live) {
+        const uint32_t nxt = ((uint32_t)tid + 1 < NT) ? uarr[tid + 1] : nitems;
+        if (nxt != uarr[tid]) sstart[uarr[tid]] = tid;
     }
     __syncthreads();
+    const uint32_t tile0 = seg * SEG_TILES;
     Item *items = P.items + (size_t)hrow * P.ntiles_total + tile0;
-    for (uint32_t t = tid; t < NT; t += KA_THREADS) {
-        const uint32_t id = ((t + 1 < NT) ? uarr[t + 1] : nitems) - 1u;  // item of tile t
-        bool is_end = (t + 1 == NT);
+    WTile *wpre = P.wpre + (size_t)hrow * P.ntiles_total + tile0;
+    if (live) {
+        const uint32_t id = (((uint32_t)tid + 1 < NT) ? uarr[tid + 1] : nitems) - 1u;
+        const TileRec r = rec[tid];
+        if (r.cls == CLS_WINDOW) wpre[tid] = WTile{carr[tid], carr2[tid], 0xFFFFFFFFu, 0u};
+        bool is_end = ((uint32_t)tid + 1 == NT);
         if (!is_end) {
-            const uint32_t nxt2 = (t + 2 < NT) ? uarr[t + 2] : nitems;
-            is_end = (nxt2 != uarr[t + 1]);                                // t+1 is a head
+            const uint32_t nxt2 = ((uint32_t)tid + 2 < NT) ? uarr[tid + 2] : nitems;
+            is_end = (nxt2 != uarr[tid + 1]);
         }
         if (is_end) {
-            const TileRec r = rec[t];
             const uint32_t start = sstart[id];
             Item it;
             it.kind = r.cls;
             it.lo = r.lo;
-            if (r.cls == CLS_SIMPLE) {
-                const Comp c = carr[t];
-                it.q[0] = c.q0;
-                it.q[1] = c.q1;
-                it.q[2] = 0u;
-                it.q[3] = 0u;
-                it.aux = t - start + 1u;
-            } else {
+            it.tile = tile0 + start;
+            if (r.cls == CLS_COMPLEX) {
                 it.q[0] = r.qlo.q0;
                 it.q[1] = r.qlo.q1;
-                it.q[2] = r.qhi.q0;
-                it.q[3] = r.qhi.q1;
+                it.q[2] = 0u;
+                it.q[3] = 0u;
                 it.aux = r.aux;
+            } else {
+                const Comp c = carr[tid];
+                const Comp hh = r.cls == CLS_WINDOW ? carr2[start] : Comp{0u, 0u};
+                it.q[0] = c.q0;
+                it.q[1] = c.q1;
+                it.q[2] = hh.q0;
+                it.q[3] = hh.q1;
+                it.aux = tid - start + 1u;
             }
-            it.tile = tile0 + start;
             items[id] = it;
         }
     }
-    if (tid == 0) hdr->seg_items[rank] = nitems;
+    if (tid == 0) {
+        hdr->seg_items[seg] = nitems;
+        hdr->seg_tile0[seg] = tile0;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -900,6 +1160,7 @@ struct KBParams {
     RowHdr *hdr;
     Item *items;
     float *wcdata;
+    const WTile *wpre;
     Candidate *cand;     // per handle row: cand_stride entries (Kernel A output)
     unsigned long long *ctmp;  // per handle row: 2 x cand_stride keys (large-set path)
     uint32_t cand_stride;
@@ -923,8 +1184,8 @@ __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M
 }
 
 // Candidate key: ascending key order == (p descending, index ascending).
-__device__ __forceinline__ unsigned long long cand_key(Candidate c) {
-    return ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(c.p)) << 32) | c.idx;
+__device__ __forceinline__ unsigned long long cand_key(uint32_t idx, float p) {
+    return ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | idx;
 }
 __device__ __forceinline__ float key_p(unsigned long long k) {
     return __uint_as_float(0xFFFFFFFFu - (uint32_t)(k >> 32));
@@ -995,7 +1256,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __shared__ float tilep[TILE];
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
-    __shared__ uint32_t walk_flags;
+    __shared__ uint32_t walk_flags, walk_items, walk_slow, n_zero;
     __shared__ unsigned long long red2[2];
     extern __shared__ __align__(16) unsigned char smem[];
     unsigned long long *skeys = reinterpret_cast<unsigned long long *>(smem);  // CAND_SMEM
@@ -1022,22 +1283,60 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
     unsigned long long *gk1 = gk0 + P.cand_stride;
     uint32_t npow = 1;
+    if (tid == 0) {
+        walk_flags = 0;
+        n_zero = 0;
+    }
+    __syncthreads();
+    uint32_t nz = 0;
     if (!big) {
         while (npow < n_cand) npow <<= 1;
-        for (uint32_t i = tid; i < npow; i += KB_THREADS) skeys[i] = i < n_cand ? cand_key(cg_[i]) : ~0ull;
+        for (uint32_t i = tid; i < npow; i += KB_THREADS) {
+            unsigned long long k = ~0ull;
+            if (i < n_cand) {
+                const Candidate c = cg_[i];
+                const float p = prob_unnorm(c.v, M, P.T);
+                k = cand_key(c.idx, p);
+                nz += p > 0.0f ? 0u : 1u;
+            }
+            skeys[i] = k;
+        }
+    } else {
+        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) {
+            const Candidate c = cg_[i];
+            const float p = prob_unnorm(c.v, M, P.T);
+            gk0[i] = cand_key(c.idx, p);
+            nz += p > 0.0f ? 0u : 1u;
+        }
     }
-    if (tid == 0) walk_flags = 0;
+    if (nz) atomicAdd(&n_zero, nz);
     __syncthreads();
+    const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
 
     if (warp == 0) {
         // ---- the exact walk of the sequential f32 sum ----
         SumState st{-126, 0u};
-        uint32_t wflags = 0;
-        const uint32_t nseg = min(hdr->nseg, (uint32_t)MAX_CLUSTER);
+        uint32_t wflags = 0, nitems_all = 0, nslow = 0;
+        const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
+        // add one tile element by element, p recomputed from the logits
+        auto add_tile = [&](uint32_t tile) {
+            tilep[lane] = exact_p_at(P, row, tile * TILE + lane, M, swin, nwin);
+            __syncwarp();
+            if (lane == 0) {
+                float s = float_of(st);
+                for (int k = 0; k < TILE; k++) s = __fadd_rn(s, tilep[k]);
+                st = state_of(s);
+            }
+            __syncwarp();
+            st.e = __shfl_sync(0xffffffffu, st.e, 0);
+            st.m = __shfl_sync(0xffffffffu, st.m, 0);
+        };
+        const uint32_t nseg = min(hdr->nseg, (uint32_t)MAX_SEG);
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
             const uint32_t t0 = min(hdr->seg_tile0[sgi], P.ntiles_total);
             const uint32_t nit = min(hdr->seg_items[sgi], P.ntiles_total - t0);
             const Item *ig = P.items + (size_t)hrow * P.ntiles_total + t0;
+            nitems_all += nit;
             for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
                 const uint32_t nc = min((uint32_t)ITEM_CHUNK, nit - i0);
                 __syncwarp();
@@ -1045,30 +1344,29 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                 __syncwarp();
                 for (uint32_t j = 0; j < nc; j++) {
                     const Item it = sitems[j];
-                    bool done = false;
-                    if (lane == 0) {
-                        const uint32_t par = st.m & 1u;
-                        if (st.e == it.lo) {
-                            const uint32_t q = par ? it.q[1] : it.q[0];
-                            if (st.m + q < QLIM && q < QSAT) { st.m += q; done = true; }
-                        } else if (it.kind == CLS_WINDOW && st.e == it.lo + 1) {
-                            const uint32_t q = par ? it.q[3] : it.q[2];
-                            if (st.m + q < QLIM && q < QSAT) { st.m += q; done = true; }
+                    const uint32_t ntl = it.kind == CLS_COMPLEX ? 1u : min(it.aux, P.ntiles_total - it.tile);
+                    // 0 applied, 1 window crossing, 2 recompute every tile, 3 stored p
+                    int action = 2;
+                    const uint32_t par = st.m & 1u;
+                    if (st.e == it.lo) {
+                        const uint32_t q = par ? it.q[1] : it.q[0];
+                        if (st.m + q < QLIM && q < QSAT) {
+                            st.m += q;
+                            action = 0;
+                        } else if (it.kind == CLS_WINDOW) {
+                            action = 1;
+                        }
+                    } else if (it.kind == CLS_WINDOW && st.e == it.lo + 1) {
+                        const uint32_t q = par ? it.q[3] : it.q[2];
+                        if (st.m + q < QLIM && q < QSAT) {
+                            st.m += q;
+                            action = 0;
                         }
                     }
-                    done = __shfl_sync(0xffffffffu, done, 0);
-                    if (done) continue;
-                    // element-wise: stored p (valid when the state is at or above
-                    // binade lo), else recomputed from the logits
-                    const int e_now = __shfl_sync(0xffffffffu, st.e, 0);
-                    const bool stored = it.kind != CLS_SIMPLE && it.aux != 0xFFFFFFFFu &&
-                                        it.aux < n_wc && e_now >= it.lo;
-                    const uint32_t ntl = it.kind == CLS_SIMPLE ? min(it.aux, P.ntiles_total) : 1u;
-                    if (!stored) wflags |= RF_SLOW_WALK;
-                    for (uint32_t tt = 0; tt < ntl; tt++) {
-                        const float pv = stored ? wcs[it.aux * TILE + lane]
-                                                : exact_p_at(P, row, (it.tile + tt) * TILE + lane, M, swin, nwin);
-                        tilep[lane] = pv;
+                    if (action == 2 && it.kind == CLS_COMPLEX && it.aux < n_wc) action = 3;
+                    if (action == 0) continue;
+                    if (action == 3) {
+                        tilep[lane] = wcs[it.aux * TILE + lane];   // stored exact p
                         __syncwarp();
                         if (lane == 0) {
                             float s = float_of(st);
@@ -1076,6 +1374,68 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                             st = state_of(s);
                         }
                         __syncwarp();
+                        st.e = __shfl_sync(0xffffffffu, st.e, 0);
+                        st.m = __shfl_sync(0xffffffffu, st.m, 0);
+                        continue;
+                    }
+                    uint32_t from = 0;
+                    if (action == 1) {
+                        // the running sum leaves binade lo inside this stretch:
+                        // first tile c whose prefix count reaches 2^24
+                        const WTile *wp = wrow + it.tile;
+                        const uint32_t pi = par;
+                        uint32_t lo_i = 0, hi_i = ntl - 1;
+                        while (lo_i < hi_i) {
+                            const uint32_t step = (hi_i - lo_i + 32) / 32;
+                            const uint32_t pos = lo_i + lane * step;
+                            bool pr = false;
+                            if (pos <= hi_i) {
+                                const Comp c = wp[pos].pre_lo;
+                                pr = st.m + (pi ? c.q1 : c.q0) >= QLIM;
+                            }
+                            const uint32_t mask = __ballot_sync(0xffffffffu, pr);
+                            if (mask == 0) {
+                                lo_i = lo_i + 31 * step + 1;
+                            } else {
+                                const uint32_t f = __ffs(mask) - 1;
+                                hi_i = lo_i + f * step;
+                                if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
+                            }
+                        }
+                        const uint32_t c = lo_i;
+                        if (c > 0) {
+                            const Comp pc = wp[c - 1].pre_lo;
+                            st.m += pi ? pc.q1 : pc.q0;
+                        }
+                        const uint32_t sl = wp[c].slot;
+                        if (sl < n_wc) {
+                            tilep[lane] = wcs[sl * TILE + lane];   // stored exact p
+                            __syncwarp();
+                            if (lane == 0) {
+                                float s = float_of(st);
+                                for (int k = 0; k < TILE; k++) s = __fadd_rn(s, tilep[k]);
+                                st = state_of(s);
+                            }
+                            __syncwarp();
+                            st.e = __shfl_sync(0xffffffffu, st.e, 0);
+                            st.m = __shfl_sync(0xffffffffu, st.m, 0);
+                        } else {
+                            add_tile(it.tile + c);
+                        }
+                        from = c + 1;
+                        if (from < ntl && st.e == it.lo + 1) {
+                            const Comp sh = wp[from].suf_hi;
+                            const uint32_t q = (st.m & 1u) ? sh.q1 : sh.q0;
+                            if (st.m + q < QLIM && q < QSAT) {
+                                st.m += q;
+                                from = ntl;
+                            }
+                        }
+                    }
+                    if (from < ntl) {
+                        wflags |= RF_SLOW_WALK;
+                        nslow += ntl - from;
+                        for (uint32_t tt = from; tt < ntl; tt++) add_tile(it.tile + tt);
                     }
                 }
             }
@@ -1083,6 +1443,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         if (lane == 0) {
             S_sh = float_of(st);
             walk_flags = wflags;
+            walk_items = nitems_all;
+            walk_slow = nslow;
         }
     } else if (!big) {
         // ---- candidate sort in shared memory: ascending key ----
@@ -1110,7 +1472,6 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     unsigned long long *keys = skeys;
     float *probs = sprobs;
     if (big) {
-        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) gk0[i] = cand_key(cg_[i]);
         __syncthreads();
         uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // 16 * KB_THREADS words
         keys = cta_radix_sort(gk0, gk1, n_cand, cnt, red2);
@@ -1120,8 +1481,29 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
 
     const float S = S_sh;
     const bool nan_row = (flags0 & RF_NAN) != 0;
+    __shared__ uint32_t rawarg_sh;
+    __shared__ ArgBest rbest[KB_THREADS / 32];
+    if (!nan_row && !(S > 0.0f)) {
+        // sum <= 0 (sampler.zig:89): sampleArgmax of the raw logits.  Not
+        // reachable with a finite maximum (its own term is exp(0) = 1).
+        const float *x = P.logits + (size_t)row * P.ld;
+        ArgBest b{NEG_INF, 0xFFFFFFFFu};
+        for (uint32_t i = tid; i < P.vocab; i += KB_THREADS) {
+            const float f = x[i];
+            b = arg_better(b, ArgBest{f != f ? NEG_INF : f, i});
+        }
+        b = warp_arg(b);
+        if (lane == 0) rbest[warp] = b;
+        __syncthreads();
+        if (tid == 0) {
+            ArgBest bb = rbest[0];
+            for (int w = 1; w < KB_THREADS / 32; w++) bb = arg_better(bb, rbest[w]);
+            rawarg_sh = (x[0] != x[0] || bb.i == 0xFFFFFFFFu) ? 0u : bb.i;
+        }
+        __syncthreads();
+    }
     // exact probs in sorted order (sampler.zig:90)
-    for (uint32_t i = tid; i < n_cand; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
+    for (uint32_t i = tid; i < n_pos; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
     __syncthreads();
     if (tid != 0) return;
 
@@ -1146,13 +1528,13 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         total = __int_as_float(0x7fc00000);
         S_rep = total;
     } else if (!(S > 0.0f)) {
-        token = hdr->raw_arg;   // sampler.zig:89
+        token = rawarg_sh;   // sampler.zig:89
         path = 1;
     } else {
         // idxs[2*i] aliases the low word of keys[i]
         uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);
         // ties: equal probs from distinct p keep index order (stable sort)
-        for (uint32_t i = 1; i < n_cand; i++) {
+        for (uint32_t i = 1; i < n_pos; i++) {
             if (probs[i] == probs[i - 1] && idxs[2 * (i - 1)] > idxs[2 * i]) {
                 uint32_t j = i;
                 const uint32_t id = idxs[2 * j];
@@ -1168,7 +1550,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         // reference's sorted order.  The kept prefix is settled inside it when
         // some filter cuts before its end, when the candidates are all tokens
         // with p > 0, or when the floor is the binding filter's own bound.
-        uint32_t n_sel = n_cand;
+        uint32_t n_sel = n_pos;
         const uint32_t binding = hdr->binding;
         const bool k_act = P.top_k > 0 && P.top_k < P.vocab;
         // top-k (sampler.zig:106-109)
@@ -1185,14 +1567,14 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             }
         }
         // min-p (sampler.zig:120-126) against probs[indices[0]]
-        if (P.min_p > 0.0f && n_cand > 0) {
+        if (P.min_p > 0.0f && n_pos > 0) {
             const float thr = __fmul_rn(probs[0], P.min_p);
             uint32_t j = 0;
             while (j < n_sel && !(probs[j] < thr)) j++;
             n_sel = j;
         }
-        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || n_sel < n_cand ||
-                              (k_act && P.top_k <= n_cand);
+        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || n_sel < n_pos ||
+                              (k_act && P.top_k <= n_pos);
         if (!cover_ok) {
             status = ROW_EINTERNAL;
             flags |= RF_CAND_SHORT;
@@ -1203,7 +1585,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             for (uint32_t j = 0; j < n_sel; j++) total = __fadd_rn(total, probs[j]);
             n_kept = n_sel;
             if (!(total > 0.0f)) {
-                token = n_cand > 0 ? idxs[0] : 0u;  // sampler.zig:160
+                token = n_pos > 0 ? idxs[0] : 0u;  // sampler.zig:160
                 path = 2;
             } else {
                 u = rng_float(s4);
@@ -1236,6 +1618,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     tr.flags = flags;
     tr.n_cand = n_cand;
     tr.status = status;
+    tr.n_items = walk_items;
+    tr.n_wc = hdr->n_wc;
+    tr.n_slow = walk_slow;
+    tr.pad = 0;
     P.trace[hrow] = tr;
 }
 
@@ -1251,11 +1637,18 @@ struct bs_sampler {
     uint32_t batch;
     uint32_t vocab;
     int device;
-    uint32_t C, seg_len, ntiles_seg, ntiles_total, ksort;
+    uint32_t nseg, ntiles_total;
     size_t smem_a, smem_b;
     uint64_t *d_rng;
     RowHdr *d_hdr;
+    TileStat *d_tstat;
+    SegStat *d_sstat;
+    uint32_t *d_khist;
+    float *d_mhist;
+    uint32_t *d_done;
+    RowInfo *d_rinfo;
     Item *d_items;
+    WTile *d_wpre;
     float *d_wc;
     Candidate *d_cand;
     unsigned long long *d_ctmp;
@@ -1267,7 +1660,7 @@ struct bs_sampler {
     size_t stage_floats;
     size_t stage_prev;
     cudaStream_t stream;
-    cudaEvent_t *prof_ev;    // profiling ring: 3 events per bs_sample call
+    cudaEvent_t *prof_ev;    // profiling ring: 4 events per bs_sample call
     uint32_t prof_cap, prof_n;
 };
 
@@ -1314,7 +1707,14 @@ static void free_all(bs_sampler *s) {
     if (!s) return;
     cudaFree(s->d_rng);
     cudaFree(s->d_hdr);
+    cudaFree(s->d_tstat);
+    cudaFree(s->d_sstat);
+    cudaFree(s->d_khist);
+    cudaFree(s->d_mhist);
+    cudaFree(s->d_done);
+    cudaFree(s->d_rinfo);
     cudaFree(s->d_items);
+    cudaFree(s->d_wpre);
     cudaFree(s->d_wc);
     cudaFree(s->d_cand);
     cudaFree(s->d_ctmp);
@@ -1323,7 +1723,7 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_prev_stage);
     cudaFree(s->d_out_stage);
     if (s->stream) cudaStreamDestroy(s->stream);
-    for (uint32_t i = 0; s->prof_ev && i < 3 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
+    for (uint32_t i = 0; s->prof_ev && i < 4 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
     delete[] s->prof_ev;
 }
 
@@ -1333,7 +1733,7 @@ static size_t g_smem_a = 0, g_smem_b = 0;
 static cudaError_t raise_smem_limits(size_t a, size_t b) {
     cudaError_t e = cudaSuccess;
     if (a > g_smem_a) {
-        e = cudaFuncSetAttribute(kernel_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)a);
+        e = cudaFuncSetAttribute(k1_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)a);
         if (e == cudaSuccess) g_smem_a = a;
     }
     if (e == cudaSuccess && b > g_smem_b) {
@@ -1346,7 +1746,7 @@ static cudaError_t raise_smem_limits(size_t a, size_t b) {
 extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vocab, int device,
                                const uint64_t *seeds, bs_sampler **out) {
     if (!cfg || !out || batch == 0 || vocab == 0) return BS_EINVAL;
-    if (vocab > (uint32_t)(MAX_CLUSTER * SEG_MAX)) return BS_ENOTSUP;
+    if (vocab > (uint32_t)(MAX_SEG * SEG_ELEMS)) return BS_ENOTSUP;
     *out = nullptr;
     BS_CUDA(cudaSetDevice(device));
     bs_sampler *s = new (std::nothrow) bs_sampler();
@@ -1356,29 +1756,23 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     s->batch = batch;
     s->vocab = vocab;
     s->device = device;
-    // segments: one CTA per ~SEG_TARGET elements, at most MAX_CLUSTER per row
-    uint32_t C = (vocab + SEG_TARGET - 1) / SEG_TARGET;
-    if (C < 1) C = 1;
-    if (C > (uint32_t)MAX_CLUSTER) C = MAX_CLUSTER;
-    uint32_t seg = (vocab + C - 1) / C;
-    seg = (seg + TILE - 1) / TILE * TILE;
-    while (C > 1 && (C - 1) * seg >= vocab) C--;   // no empty segment
-    s->C = C;
-    s->seg_len = seg;
-    s->ntiles_seg = seg / TILE;
-    s->ntiles_total = C * s->ntiles_seg;
-    uint32_t ks = 1;
-    while (ks < s->ntiles_seg) ks <<= 1;
-    s->ksort = ks;
-    s->smem_a = (size_t)seg * 4 + (size_t)s->ntiles_seg * 16 + (size_t)ks * 4 +
-                (size_t)s->ntiles_seg * (sizeof(TileRec) + 4 + sizeof(Comp)) + 64;
+    s->ntiles_total = (vocab + TILE - 1) / TILE;
+    s->nseg = (s->ntiles_total + SEG_TILES - 1) / SEG_TILES;
+    s->smem_a = 0;
     s->smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
     s->cand_stride = (vocab + 31u) & ~31u;
 
     cudaError_t e = cudaSuccess;
     e = cudaMalloc(&s->d_rng, (size_t)batch * 4 * sizeof(uint64_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_hdr, (size_t)batch * sizeof(RowHdr));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_tstat, (size_t)batch * s->ntiles_total * sizeof(TileStat));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_sstat, (size_t)batch * MAX_SEG * sizeof(SegStat));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_khist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_mhist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_done, (size_t)batch * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_rinfo, (size_t)batch * sizeof(RowInfo));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_items, (size_t)batch * s->ntiles_total * sizeof(Item));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_wpre, (size_t)batch * s->ntiles_total * sizeof(WTile));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_wc, (size_t)batch * WC_CAP * TILE * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_cand, (size_t)batch * s->cand_stride * sizeof(Candidate));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_ctmp, (size_t)batch * 2 * s->cand_stride * sizeof(unsigned long long));
@@ -1404,6 +1798,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     e = cudaMemcpy(s->d_rng, h, (size_t)batch * 4 * sizeof(uint64_t), cudaMemcpyHostToDevice);
     delete[] h;
     if (e == cudaSuccess) e = cudaMemset(s->d_trace, 0, (size_t)batch * sizeof(RowTrace));
+    if (e == cudaSuccess) e = cudaMemset(s->d_done, 0, (size_t)batch * sizeof(uint32_t));
     if (e == cudaSuccess) e = raise_smem_limits(s->smem_a, s->smem_b);
     if (e != cudaSuccess) {
         fprintf(stderr, "b200_sampler: setup failed: %s\n", cudaGetErrorString(e));
@@ -1441,13 +1836,14 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     // sampler.zig:50 -- temperature <= 0: argmax of the raw logits, no draw
     if (c.temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, s->vocab, d_out, stream);
 
-    KAParams A;
+    K12Params A;
     A.logits = d_logits;
     A.ld = ld;
     A.prev = d_prev;
     A.n_prev = d_prev ? n_prev : 0;
     A.vocab = s->vocab;
     A.row0 = row0;
+    A.rows = rows;
     A.T = c.temperature;
     A.c2 = (float)(1.4426950408889634 / (double)c.temperature);
     A.top_k = c.top_k;
@@ -1455,35 +1851,31 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.min_p = c.min_p;
     A.rep_window = c.repetition_window;
     A.rep_penalty = c.repetition_penalty;
-    A.C = s->C;
-    A.seg_len = s->seg_len;
-    A.ntiles_seg = s->ntiles_seg;
+    A.nseg = s->nseg;
     A.ntiles_total = s->ntiles_total;
-    A.ksort = s->ksort;
+    A.tstat = s->d_tstat;
+    A.sstat = s->d_sstat;
+    A.khist = s->d_khist;
+    A.mhist = s->d_mhist;
+    A.done = s->d_done;
+    A.rinfo = s->d_rinfo;
     A.hdr = s->d_hdr;
     A.items = s->d_items;
+    A.wpre = s->d_wpre;
     A.wcdata = s->d_wc;
     A.cand = s->d_cand;
     A.cand_stride = s->cand_stride;
 
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(s->C, rows, 1);
-    cfg.blockDim = dim3(KA_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = s->smem_a;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = s->C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     cudaEvent_t *ev = nullptr;
-    if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 3 * s->prof_n++;
+    if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
     if (ev) cudaEventRecord(ev[0], st);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_a, A);
+    k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    if (ev) cudaEventRecord(ev[1], st);
+    k2_main<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    if (ev) cudaEventRecord(ev[2], st);
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
-        fprintf(stderr, "b200_sampler: kernel A launch failed: %s\n", cudaGetErrorString(e));
+        fprintf(stderr, "b200_sampler: pass launch failed: %s\n", cudaGetErrorString(e));
         return BS_ECUDA;
     }
 
@@ -1505,15 +1897,15 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.hdr = s->d_hdr;
     B.items = s->d_items;
     B.wcdata = s->d_wc;
+    B.wpre = s->d_wpre;
     B.cand = s->d_cand;
     B.ctmp = s->d_ctmp;
     B.cand_stride = s->cand_stride;
     B.rng = s->d_rng;
     B.trace = s->d_trace;
     B.out = d_out;
-    if (ev) cudaEventRecord(ev[1], st);
     kernel_b<<<rows, KB_THREADS, s->smem_b, st>>>(B);
-    if (ev) cudaEventRecord(ev[2], st);
+    if (ev) cudaEventRecord(ev[3], st);
     return cuda_status(cudaGetLastError());
 }
 
@@ -1602,26 +1994,26 @@ extern "C" bs_status bs_debug_row_traces(bs_sampler *s, void *h_traces, size_t b
 extern "C" bs_status bs_profile_enable(bs_sampler *s, uint32_t max_calls) {
     if (!s) return BS_EINVAL;
     BS_CUDA(cudaSetDevice(s->device));
-    for (uint32_t i = 0; s->prof_ev && i < 3 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
+    for (uint32_t i = 0; s->prof_ev && i < 4 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
     delete[] s->prof_ev;
     s->prof_ev = nullptr;
     s->prof_cap = s->prof_n = 0;
     if (max_calls == 0) return BS_OK;
-    s->prof_ev = new (std::nothrow) cudaEvent_t[3 * (size_t)max_calls];
+    s->prof_ev = new (std::nothrow) cudaEvent_t[4 * (size_t)max_calls];
     if (!s->prof_ev) return BS_ENOMEM;
-    for (uint32_t i = 0; i < 3 * max_calls; i++) BS_CUDA(cudaEventCreate(&s->prof_ev[i]));
+    for (uint32_t i = 0; i < 4 * max_calls; i++) BS_CUDA(cudaEventCreate(&s->prof_ev[i]));
     s->prof_cap = max_calls;
     return BS_OK;
 }
 
-extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms_a, float *ms_b, uint32_t *n_calls) {
-    if (!s || !ms_a || !ms_b || !n_calls) return BS_EINVAL;
+extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uint32_t *n_calls) {
+    if (!s || !ms || !n_calls) return BS_EINVAL;
     BS_CUDA(cudaSetDevice(s->device));
-    const uint32_t n = s->prof_n;
+    const uint32_t n = s->prof_n < cap ? s->prof_n : cap;
     for (uint32_t i = 0; i < n; i++) {
-        BS_CUDA(cudaEventSynchronize(s->prof_ev[3 * i + 2]));
-        BS_CUDA(cudaEventElapsedTime(&ms_a[i], s->prof_ev[3 * i], s->prof_ev[3 * i + 1]));
-        BS_CUDA(cudaEventElapsedTime(&ms_b[i], s->prof_ev[3 * i + 1], s->prof_ev[3 * i + 2]));
+        BS_CUDA(cudaEventSynchronize(s->prof_ev[4 * i + 3]));
+        for (int j = 0; j < 3; j++)
+            BS_CUDA(cudaEventElapsedTime(&ms[3 * i + j], s->prof_ev[4 * i + j], s->prof_ev[4 * i + j + 1]));
     }
     *n_calls = n;
     s->prof_n = 0;

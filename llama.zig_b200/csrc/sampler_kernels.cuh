@@ -44,8 +44,8 @@ struct RowHdr {
     uint32_t n_wc;       // window/complex tiles with stored p (may exceed WC_CAP)
     float s_approx;      // approximate normaliser
     float v_floor;       // candidate floor (logit domain)
-    uint32_t seg_items[MAX_CLUSTER];
-    uint32_t seg_tile0[MAX_CLUSTER];
+    uint32_t seg_items[64];   // walk items per segment (MAX_SEG)
+    uint32_t seg_tile0[64];
     uint32_t nseg;
     uint32_t binding;    // which filter set the candidate floor (0 none, 1 k, 2 p, 3 min-p)
     uint32_t pad[2];
@@ -71,11 +71,15 @@ struct RowTrace {
     uint32_t flags;
     uint32_t n_cand;
     uint32_t status;
+    uint32_t n_items;  // walk items of the row
+    uint32_t n_wc;     // window/complex tiles
+    uint32_t n_slow;   // tiles the walk recomputed from the logits
+    uint32_t pad;
 };
 
 struct Candidate {
     uint32_t idx;
-    float p;           // exact exp((v - M)/T)
+    float v;           // the (penalised) logit; the walk kernel computes p exactly
 };
 
 }  // namespace bs

@@ -71,6 +71,10 @@ class RowTrace(ctypes.Structure):
         ("flags", ctypes.c_uint32),
         ("n_cand", ctypes.c_uint32),
         ("status", ctypes.c_uint32),
+        ("n_items", ctypes.c_uint32),
+        ("n_wc", ctypes.c_uint32),
+        ("n_slow", ctypes.c_uint32),
+        ("pad", ctypes.c_uint32),
     ]
 
 
@@ -120,7 +124,7 @@ def lib() -> ctypes.CDLL:
         L.bs_status_string.restype = ctypes.c_char_p
         L.bs_debug_row_traces.argtypes = [vp, vp, ctypes.c_size_t]
         L.bs_profile_enable.argtypes = [vp, u32]
-        L.bs_profile_read.argtypes = [vp, vp, vp, ctypes.POINTER(u32)]
+        L.bs_profile_read.argtypes = [vp, vp, u32, ctypes.POINTER(u32)]
         for name in ("bs_create", "bs_sample", "bs_sample_host", "bs_argmax", "bs_get_rng_state",
                      "bs_set_rng_state", "bs_last_device_status", "bs_debug_row_traces",
                      "bs_profile_enable", "bs_profile_read"):
@@ -255,14 +259,13 @@ class Sampler:
         _check(lib().bs_profile_enable(self._h, max_calls), "bs_profile_enable")
 
     def profile_read(self):
-        """(ms_a, ms_b) arrays: per-call durations of the two kernels."""
-        cap = 1 << 20
-        a = np.zeros(cap, np.float32)
-        b = np.zeros(cap, np.float32)
+        """(n_calls, 3) array of per-call kernel durations in ms: statistics
+        pass, main pass, walk/draw pass."""
+        cap = 1 << 18
+        a = np.zeros(3 * cap, np.float32)
         n = ctypes.c_uint32(0)
-        _check(lib().bs_profile_read(self._h, a.ctypes.data, b.ctypes.data, ctypes.byref(n)),
-               "bs_profile_read")
-        return a[:n.value].copy(), b[:n.value].copy()
+        _check(lib().bs_profile_read(self._h, a.ctypes.data, cap, ctypes.byref(n)), "bs_profile_read")
+        return a[:3 * n.value].reshape(n.value, 3).copy()
 
     def traces(self):
         tr = (RowTrace * self.batch)()
