@@ -914,7 +914,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     __shared__ TileRec rec[SEG_TILES];
     __shared__ TileParam tpar[SEG_TILES];
     __shared__ uint32_t uarr[SEG_TILES], uarr2[SEG_TILES];
-    __shared__ Comp carr[SEG_TILES], carr2[SEG_TILES];
+    __shared__ __align__(16) Comp carr[SEG_TILES];    // also read as uint64_t by the fast item path
+    __shared__ __align__(16) Comp carr2[SEG_TILES];
     __shared__ uint32_t wlist[SEG_TILES];
     __shared__ uint32_t nlist, nanflag;
     const uint32_t nwin = load_window(P, row, swin);
@@ -1072,6 +1073,121 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // ---- items: a stretch of SIMPLE tiles of one binade, a stretch of WINDOW
     // tiles of one lower binade, or one COMPLEX tile
     const uint32_t NT = ntile;
+    const uint32_t tile0 = seg * SEG_TILES;
+    Item *items = P.items + (size_t)hrow * P.ntiles_total + tile0;
+    WTile *wpre = P.wpre + (size_t)hrow * P.ntiles_total + tile0;
+    // counts that depend on the entry parity (ties) need ordered composition;
+    // otherwise plain sums suffice and one warp builds the items
+    const bool ties = __syncthreads_or(live && (rec[tid].qlo.q0 != rec[tid].qlo.q1 ||
+                                                rec[tid].qhi.q0 != rec[tid].qhi.q1)) != 0;
+    if (!ties) {
+        if (warp == 0) {
+            uint32_t nitems = 0;
+            uint64_t carry_a = 0, carry_b = 0;
+            uint32_t carry_start = 0;
+            uint32_t *sid = uarr;                                   // item of each WINDOW tile
+            uint64_t *sb = reinterpret_cast<uint64_t *>(carr);      // hi prefix of each WINDOW tile
+            uint64_t *itb = reinterpret_cast<uint64_t *>(carr2);    // hi total of each item
+            for (uint32_t c0 = 0; c0 < NT; c0 += 32) {
+                const uint32_t j = c0 + lane;
+                const bool valid = j < NT;
+                TileRec r;
+                r.lo = 0;
+                r.cls = CLS_SIMPLE;
+                r.aux = 0u;
+                r.qlo = Comp{0u, 0u};
+                r.qhi = Comp{0u, 0u};
+                if (valid) r = rec[j];
+                bool h = valid, e = valid;
+                if (valid && j > 0) {
+                    const TileRec q = rec[j - 1];
+                    h = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
+                }
+                if (valid && j + 1 < NT) {
+                    const TileRec q = rec[j + 1];
+                    e = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
+                }
+                const uint32_t heads = __ballot_sync(0xffffffffu, h);
+                const uint64_t a = r.qlo.q0, b = r.qhi.q0;
+                uint64_t Pa = a, Pb = b;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint64_t ua = __shfl_up_sync(0xffffffffu, Pa, o);
+                    const uint64_t ub = __shfl_up_sync(0xffffffffu, Pb, o);
+                    if (lane >= o) {
+                        Pa += ua;
+                        Pb += ub;
+                    }
+                }
+                const uint32_t upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+                const uint32_t m = heads & upto;
+                const int sl = m ? 31 - __clz(m) : 0;
+                const uint64_t pa0 = __shfl_sync(0xffffffffu, Pa, sl > 0 ? sl - 1 : 0);
+                const uint64_t pb0 = __shfl_sync(0xffffffffu, Pb, sl > 0 ? sl - 1 : 0);
+                uint64_t seg_a, seg_b;
+                uint32_t start, id;
+                if (m) {
+                    seg_a = Pa - (sl > 0 ? pa0 : 0);
+                    seg_b = Pb - (sl > 0 ? pb0 : 0);
+                    start = c0 + (uint32_t)sl;
+                    id = nitems + __popc(m) - 1u;
+                } else {   // continues the stretch open at the chunk start
+                    seg_a = carry_a + Pa;
+                    seg_b = carry_b + Pb;
+                    start = carry_start;
+                    id = nitems - 1u;
+                }
+                if (valid && r.cls == CLS_WINDOW) {
+                    const uint32_t pa = (uint32_t)min(seg_a, (uint64_t)QSAT);
+                    wpre[j] = WTile{Comp{pa, pa}, Comp{0u, 0u}, 0xFFFFFFFFu, 0u};
+                    sid[j] = id;
+                    sb[j] = seg_b - b;   // exclusive hi prefix
+                }
+                if (valid && e) {
+                    Item it;
+                    it.kind = r.cls;
+                    it.lo = r.lo;
+                    it.tile = tile0 + start;
+                    const uint32_t qa = (uint32_t)min(seg_a, (uint64_t)QSAT);
+                    const uint32_t qb = (uint32_t)min(seg_b, (uint64_t)QSAT);
+                    if (r.cls == CLS_COMPLEX) {
+                        it.q[0] = r.qlo.q0;
+                        it.q[1] = r.qlo.q1;
+                        it.q[2] = 0u;
+                        it.q[3] = 0u;
+                        it.aux = r.aux;
+                    } else {
+                        it.q[0] = qa;
+                        it.q[1] = qa;
+                        it.q[2] = r.cls == CLS_WINDOW ? qb : 0u;
+                        it.q[3] = r.cls == CLS_WINDOW ? qb : 0u;
+                        it.aux = j - start + 1u;
+                    }
+                    items[id] = it;
+                    itb[id] = seg_b;
+                }
+                carry_a = __shfl_sync(0xffffffffu, seg_a, 31);
+                carry_b = __shfl_sync(0xffffffffu, seg_b, 31);
+                carry_start = __shfl_sync(0xffffffffu, start, 31);
+                nitems += __popc(heads);
+            }
+            __syncwarp();
+            // suffix counts (binade lo+1) of the WINDOW tiles
+            for (uint32_t j = lane; j < NT; j += 32) {
+                const TileRec r = rec[j];
+                if (r.cls == CLS_WINDOW) {
+                    const uint64_t suf = itb[sid[j]] - sb[j];
+                    const uint32_t qs = (uint32_t)min(suf, (uint64_t)QSAT);
+                    wpre[j].suf_hi = Comp{qs, qs};
+                }
+            }
+            if (lane == 0) {
+                hdr->seg_items[seg] = nitems;
+                hdr->seg_tile0[seg] = tile0;
+            }
+        }
+        return;
+    }
     if (live) {
         const TileRec r = rec[tid];
         uint32_t h = 1, e = 1;
@@ -1099,9 +1215,6 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         if (nxt != uarr[tid]) sstart[uarr[tid]] = tid;
     }
     __syncthreads();
-    const uint32_t tile0 = seg * SEG_TILES;
-    Item *items = P.items + (size_t)hrow * P.ntiles_total + tile0;
-    WTile *wpre = P.wpre + (size_t)hrow * P.ntiles_total + tile0;
     if (live) {
         const uint32_t id = (((uint32_t)tid + 1 < NT) ? uarr[tid + 1] : nitems) - 1u;
         const TileRec r = rec[tid];
