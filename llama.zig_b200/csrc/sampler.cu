@@ -636,17 +636,25 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const bool fast = nwin == 0 && (seg + 1) * SEG_ELEMS <= P.vocab &&
                       (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
     const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
-#pragma unroll 4
+    // all eight quads of the thread are requested before any is used: the
+    // pass streams from HBM and needs many loads in flight per SM
+    float4 qv[ITERS];
+    if (fast) {
+#pragma unroll
+        for (int it = 0; it < ITERS; it++) qv[it] = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
+    } else {
+#pragma unroll
+        for (int it = 0; it < ITERS; it++) {
+            const uint32_t tl = 4 * (warp + NW * it) + sub;
+            qv[it] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+            if (tl < ntile) qv[it] = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
+        }
+    }
+#pragma unroll
     for (int it = 0; it < ITERS; it++) {
         const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
         const uint32_t t = seg * SEG_TILES + tl;
-        float4 q;
-        if (fast) {
-            q = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
-        } else {
-            q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
-            if (tl < ntile) q = load_quad(P, x, t * TILE + 4 * l8, pol, swin, nwin);
-        }
+        const float4 q = qv[it];
         const float tm = group8_max(fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
         float s = 0.0f;
         if (tm > NEG_INF) {
