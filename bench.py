@@ -47,7 +47,7 @@ def peaks():
 
 
 def profile_traffic(workload):
-    """DRAM bytes per launch of the cluster pass from the committed ncu summary."""
+    """DRAM bytes of one sampling step (the three kernels) from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if not os.path.exists(p):
         return None
