@@ -113,6 +113,26 @@ bs_status bs_last_device_status(bs_sampler *s);
 bs_status bs_profile_enable(bs_sampler *s, uint32_t max_calls);
 bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uint32_t *n_calls);
 
+/* No counterpart in the reference (sampler.zig always allocates through the
+ * caller's allocator).  bs_sample for callers that must not allocate device
+ * memory while sampling: no handle, no cudaMalloc.  Scratch is one fixed
+ * static device array of this library (about 14 MB per device), so at most
+ * BS_STATIC_MAX_ROWS rows of at most BS_STATIC_MAX_VOCAB logits per call;
+ * larger calls return BS_EINVAL with a message on stderr.
+ *   cfg    : the sampler settings (typical_p in (0,1) -> BS_ENOTSUP)
+ *   d_rng  : device buffer of rows x 4 u64 xoshiro256++ states, in the layout
+ *            bs_get_rng_state returns; advanced in place like bs_sample's
+ * Other arguments as bs_sample (row i of this call uses d_rng[4i..4i+3]).
+ * All calls on one device share the scratch: calls that may overlap in time
+ * (different streams or host threads) race and must be ordered by the
+ * caller.  The first call on each device resolves the scratch address
+ * (cudaGetSymbolAddress) and must not be made while a stream is capturing. */
+#define BS_STATIC_MAX_ROWS 4
+#define BS_STATIC_MAX_VOCAB 131072
+bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, const float *d_logits, size_t ld,
+                           uint32_t rows, uint32_t vocab, const uint32_t *d_prev, uint32_t n_prev,
+                           uint32_t *d_out, void *stream);
+
 void bs_destroy(bs_sampler *s);
 
 const char *bs_status_string(bs_status st);

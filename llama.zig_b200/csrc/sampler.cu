@@ -43,6 +43,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "../../include/b200_sampler.h"
@@ -2139,4 +2140,116 @@ extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uin
     *n_calls = n;
     s->prof_n = 0;
     return BS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// bs_sample_static: the same three passes with every scratch buffer carved
+// from one fixed static device array instead of a handle's allocations.  The
+// caller owns the RNG state (a device buffer of rows x 4 u64).
+constexpr size_t r256(size_t b) { return (b + 255) & ~(size_t)255; }
+constexpr int STATIC_NBUF = 13;
+struct StaticSizes {
+    size_t b[STATIC_NBUF];
+};
+constexpr StaticSizes static_sizes(uint32_t rows, uint32_t vocab) {
+    const size_t nt = (vocab + TILE - 1) / TILE, cs = (vocab + 31u) & ~31u;
+    return StaticSizes{{r256(rows * sizeof(RowHdr)), r256(rows * nt * sizeof(TileStat)),
+                        r256(rows * MAX_SEG * sizeof(SegStat)), r256(rows * MAX_SEG * KH_BINS * sizeof(uint32_t)),
+                        r256(rows * MAX_SEG * KH_BINS * sizeof(float)), r256(rows * sizeof(uint32_t)),
+                        r256(rows * sizeof(RowInfo)), r256(rows * nt * sizeof(Item)), r256(rows * nt * sizeof(WTile)),
+                        r256(rows * WC_CAP * TILE * sizeof(float)), r256(rows * cs * sizeof(Candidate)),
+                        r256(rows * 2 * cs * sizeof(unsigned long long)), r256(rows * sizeof(RowTrace))}};
+}
+constexpr size_t static_total(uint32_t rows, uint32_t vocab) {
+    const StaticSizes s = static_sizes(rows, vocab);
+    size_t t = 0;
+    for (int i = 0; i < STATIC_NBUF; i++) t += s.b[i];
+    return t;
+}
+// every buffer size grows with rows and vocab, so any call within the limits
+// fits in the array sized for the limits
+constexpr size_t STATIC_BYTES = static_total(BS_STATIC_MAX_ROWS, BS_STATIC_MAX_VOCAB);
+static __device__ __align__(256) unsigned char g_static_scratch[STATIC_BYTES];
+
+constexpr int STATIC_MAX_DEVICES = 64;
+static unsigned char *g_static_base[STATIC_MAX_DEVICES];
+static std::mutex g_static_mu;
+
+// Address of this device's copy of the static scratch, resolved once per
+// device (with the kernel's shared-memory attribute raised there).
+static cudaError_t static_scratch_base(int dev, unsigned char **base) {
+    if (dev < 0 || dev >= STATIC_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_base[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return e;
+        const size_t smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+        e = cudaFuncSetAttribute(kernel_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
+        if (e != cudaSuccess) return e;
+        g_static_base[dev] = static_cast<unsigned char *>(p);
+    }
+    *base = g_static_base[dev];
+    return cudaSuccess;
+}
+
+extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, const float *d_logits, size_t ld,
+                                      uint32_t rows, uint32_t vocab, const uint32_t *d_prev, uint32_t n_prev,
+                                      uint32_t *d_out, void *stream) {
+    if (!cfg || !d_rng || !d_logits || !d_out || vocab == 0 || ld < vocab) return BS_EINVAL;
+    if (rows > BS_STATIC_MAX_ROWS || vocab > BS_STATIC_MAX_VOCAB) {
+        fprintf(stderr,
+                "b200_sampler: bs_sample_static: %u rows of %u logits exceed the static scratch "
+                "(at most %u rows of at most %u logits); use a handle (bs_create)\n",
+                rows, vocab, (unsigned)BS_STATIC_MAX_ROWS, (unsigned)BS_STATIC_MAX_VOCAB);
+        return BS_EINVAL;
+    }
+    if (cfg->typical_p > 0.0f && cfg->typical_p < 1.0f) return BS_ENOTSUP;
+    if (rows == 0) return BS_OK;
+    if (cfg->temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, vocab, d_out, stream);
+    int dev = 0;
+    BS_CUDA(cudaGetDevice(&dev));
+    unsigned char *base = nullptr;
+    const cudaError_t e = static_scratch_base(dev, &base);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "b200_sampler: bs_sample_static: static scratch set-up failed: %s\n", cudaGetErrorString(e));
+        return BS_ECUDA;
+    }
+    // a handle on the host stack whose buffers point into the static scratch
+    bs_sampler s;
+    memset(&s, 0, sizeof(s));
+    s.cfg = *cfg;
+    s.batch = rows;
+    s.vocab = vocab;
+    s.device = dev;
+    s.ntiles_total = (vocab + TILE - 1) / TILE;
+    s.nseg = (s.ntiles_total + SEG_TILES - 1) / SEG_TILES;
+    s.smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+    s.cand_stride = (vocab + 31u) & ~31u;
+    s.d_rng = d_rng;
+    const StaticSizes sz = static_sizes(rows, vocab);
+    void *ptr[STATIC_NBUF];
+    size_t off = 0;
+    for (int i = 0; i < STATIC_NBUF; i++) {
+        ptr[i] = base + off;
+        off += sz.b[i];
+    }
+    s.d_hdr = static_cast<RowHdr *>(ptr[0]);
+    s.d_tstat = static_cast<TileStat *>(ptr[1]);
+    s.d_sstat = static_cast<SegStat *>(ptr[2]);
+    s.d_khist = static_cast<uint32_t *>(ptr[3]);
+    s.d_mhist = static_cast<float *>(ptr[4]);
+    s.d_done = static_cast<uint32_t *>(ptr[5]);
+    s.d_rinfo = static_cast<RowInfo *>(ptr[6]);
+    s.d_items = static_cast<Item *>(ptr[7]);
+    s.d_wpre = static_cast<WTile *>(ptr[8]);
+    s.d_wc = static_cast<float *>(ptr[9]);
+    s.d_cand = static_cast<Candidate *>(ptr[10]);
+    s.d_ctmp = static_cast<unsigned long long *>(ptr[11]);
+    s.d_trace = static_cast<RowTrace *>(ptr[12]);
+    // the per-row completion counters of the statistics pass must start at
+    // zero; the pass leaves them at zero, but a call that failed part-way
+    // might not have
+    BS_CUDA(cudaMemsetAsync(s.d_done, 0, (size_t)rows * sizeof(uint32_t), (cudaStream_t)stream));
+    return bs_sample(&s, d_logits, ld, 0, rows, d_prev, n_prev, d_out, stream);
 }
