@@ -159,6 +159,16 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+__device__ __forceinline__ uint32_t warp_incl_scan_u(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
 // Ordered reduction of lane composites (lane 0 = first element).  Result in lane 0.
 __device__ __forceinline__ Comp warp_comp_reduce(Comp c) {
     const int lane = threadIdx.x & 31;
@@ -243,13 +253,13 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
 
 // ---------------------------------------------------------------------------
 
-struct TileParam {   // per-tile values K2's main loop needs (16 bytes)
-    int32_t lo;        // lowest candidate binade of the running sum
-    uint16_t cls;      // CLS_*
-    uint16_t special;  // the tile goes to the warp-cooperative exact pass
+struct TileParam {   // per-tile values of K2's main loop (16 bytes)
     float K;           // 23 - lo: log2(p / u_lo) = x2 + K
-    float thr;         // x2 below this: p < u_lo / 2
+    float fhi, flo;    // 1 +- the certificate's relative error bound
+    uint32_t info;     // TP_* flags | cls << 2 | (lo + 128) << 8
 };
+constexpr uint32_t TP_SPECIAL = 1u;   // counted by the warp-cooperative exact pass
+constexpr uint32_t TP_CAND = 2u;      // the tile maximum reaches the candidate floor
 
 struct TileRec {
     int32_t lo;
@@ -387,10 +397,20 @@ constexpr int RED_CHUNK = 4;                 // segments per step of the row red
 constexpr double WIN_LO = 4e-3;
 constexpr double WIN_HI = 3e-5;
 
-// Relative error bound of ex2.approx(x2) against the exact p = exp_ref(x/T)
-// (argument and division roundings grow with |x2|; the rest is constant).
-// The GPU test suite checks the bound on millions of samples.
-__device__ __forceinline__ float approx_p_eps(float x2) { return fabsf(x2) * 4.8e-7f + 3.9e-6f; }
+// Relative error bound, for the main loop's certificate, between
+// y = ex2.approx(min(fma(d, c2, K), 17.5)) and the exact p / u_lo, where
+// p = exp_ref(fdiv_rn(d, T)), d = fsub_rn(v, M), c2 = fl(log2(e) / T).
+// Only elements with y >= 1/2 can count, so |x2| <= K + 1 for them.  Terms
+// (relative error of y, natural-log units of the exponent times ln 2):
+//   the reference's divide: |x2| ln2 2^-24;  its expf: 2^-23 (one ulp);
+//   c2's rounding: |x2| ln2 2^-24;  the FFMA's rounding: 17.5 ln2 2^-24;
+//   ex2.approx: 2^-22 (documented 2^-22.5 or better).
+// The bound is doubled; the caller also floors it at 2^-17 so that the
+// clamped values (y = 2^17.5) always fail the certificate.  The GPU suite
+// checks it against the exact count on random inputs (bs_debug_cert_check).
+__host__ __device__ __forceinline__ float cert_eps(float K) {
+    return 2.0f * ((K + 1.0f) * 8.27e-8f + 1.2e-7f + 7.3e-7f + 2.4e-7f);
+}
 
 __device__ __forceinline__ double pow2d(int k) {   // 2^k, -1022 <= k <= 1023
     return __longlong_as_double((long long)(k + 1023) << 52);
@@ -934,11 +954,15 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     }
 
     // raw prefix estimate at every tile start of the segment, and from it
-    // each tile's candidate binades of the running sum
+    // each tile's candidate binades of the running sum and its main-loop
+    // parameters
+    const float xf2 = ri.xf2;
     {
         double ct = 0.0;
+        float tmax = NEG_INF;
         if (live) {
             const TileStat ts = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
+            tmax = ts.tmax;
             ct = ts.tmax > NEG_INF ? (double)ts.tsr * (double)ex2_approx((ts.tmax - M) * c2) : 0.0;
         }
         double segtot;
@@ -946,22 +970,39 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const double Pe = Ps + ct;
         const int lo = binade_of(Ps * (1.0 - WIN_LO));
         const int hi = binade_of(Pe * (1.0 + WIN_HI));
+        const uint32_t cls = hi == lo ? CLS_SIMPLE : (hi == lo + 1 ? CLS_WINDOW : CLS_COMPLEX);
+        // SIMPLE and WINDOW tiles are counted here (WINDOW in both binades);
+        // COMPLEX tiles and tiny binades go to the exact pass.  So do the
+        // WINDOW tiles of a segment that has few of them: the exact pass
+        // stores their p, so the walker finds a binade crossing in shared
+        // memory instead of recomputing the tile from the logits
+        const uint32_t nwin_seg = __syncthreads_count(live && cls == CLS_WINDOW);
+        const bool special = cls == CLS_COMPLEX || lo < -100 || (cls == CLS_WINDOW && nwin_seg <= 32u);
+        const float K = (float)(23 - max(lo, -100));   // log2(p / u_lo) = x2 + K
+        // may hold candidates: the per-element test below is monotone in the
+        // logit, so the tile maximum decides
+        const float dm = __fsub_rn(tmax, M);
+        const float xm = (dm == 0.0f) ? 0.0f : dm * c2;
+        const bool cand = tmax > NEG_INF && xm >= xf2;
         TileParam tp;
-        tp.lo = lo;
-        tp.cls = hi == lo ? CLS_SIMPLE : (hi == lo + 1 ? CLS_WINDOW : CLS_COMPLEX);
-        tp.special = (tp.cls == CLS_COMPLEX || lo < -100) ? 1u : 0u;
-        tp.K = (float)(23 - max(lo, -100));        // log2(p / u_lo) = x2 + K
-        tp.thr = (float)(lo - 24) - 0.01f;         // p < u_lo / 2 below this
+        tp.K = K;
+        const float e = fmaxf(cert_eps(K), 0x1p-17f);
+        tp.fhi = 1.0f + e;
+        tp.flo = 1.0f - e;
+        tp.info = (special ? TP_SPECIAL : 0u) | (cand ? TP_CAND : 0u) | (cls << 2) | ((uint32_t)(lo + 128) << 8);
         tpar[tid] = tp;
     }
     __syncthreads();
 
-    const float xf2 = ri.xf2;
     const uint64_t pol = l2_policy_evict_first();
     const uint32_t sub = lane >> 3, l8 = lane & 7;
     const bool t_nan = T != T, t_inf = isinf(T);
+    const bool check_nan = ri.check_nan != 0;
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
     constexpr int ITERS = SEG_TILES / (4 * NW);   // 8
+    const bool fast = nwin == 0 && (seg + 1) * SEG_ELEMS <= P.vocab &&
+                      (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
+    const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
     uint32_t nanl = 0;
 #pragma unroll 2
     for (int it = 0; it < ITERS; it++) {
@@ -969,55 +1010,74 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const uint32_t t = seg * SEG_TILES + tl;
         const bool tlive = tl < ntile;
         const uint32_t g0 = t * TILE + 4 * l8;
-        float4 q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
-        if (tlive) q = load_quad(P, x, g0, pol, swin, nwin);
+        float4 q;
+        if (fast) {
+            q = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
+        } else {
+            q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+            if (tlive) q = load_quad(P, x, g0, pol, swin, nwin);
+        }
         const float a[4] = {q.x, q.y, q.z, q.w};
         const TileParam tp = tpar[tl < SEG_TILES ? tl : 0];
-        const int lo = tp.lo;
-        const uint32_t cls = tp.cls;
-        uint32_t special = tp.special;
-        uint32_t qlo = 0, qhi = 0, nc = 0;
-        float x2v[4];
+        // certified grid counts of binade lo: y = p / u_lo from the fast
+        // exp; y (1 - e) and y (1 + e) bracket the exact value, and the count
+        // is the common rounding of both (a tie or a value too close to one
+        // makes them differ).  The clamp makes large values differ too.
+        float d[4], y[4];
+        uint32_t acc = 0u, diff = 0u;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const float d = __fsub_rn(a[k], M);
-            if (ri.check_nan) nanl |= (g0 + k < P.vocab && ((d != d) || t_nan || (isinf(d) && t_inf))) ? 1u : 0u;
-            const float x2 = (d == 0.0f) ? 0.0f : d * c2;
-            x2v[k] = x2;
-            nc += x2 >= xf2 ? 1u : 0u;
-            // grid count from the fast exp, certified by its error bound
-            // (branch-free: evaluated for every element, used when x2 >= thr)
-            const float y = fminf(ex2_approx(x2 + tp.K), 1048576.0f);
-            const float eps = fmaf(x2, -4.8e-7f, 4.0e-6f);       // approx_p_eps(x2) + the shift's rounding
-            const float yr = y + 12582912.0f;                     // rint via 1.5 * 2^23
-            bool ok = y < 1048576.0f && fabsf(y - (yr - 12582912.0f)) < fmaf(-y, eps, 0.5f - 1e-6f);
-            uint32_t ih = 0;
-            if (cls == CLS_WINDOW) {
-                const float yh = 0.5f * y;
-                const float yhr = yh + 12582912.0f;
-                ok = ok && fabsf(yh - (yhr - 12582912.0f)) < fmaf(-yh, eps, 0.5f - 1e-6f);
-                ih = __float_as_uint(yhr) - 0x4B400000u;
-            }
-            const bool sig = x2 >= tp.thr;
-            special |= (sig && !ok) ? 1u : 0u;   // large or near a rounding boundary: exact pass
-            qlo += sig ? __float_as_uint(yr) - 0x4B400000u : 0u;
-            qhi += sig ? ih : 0u;
+            d[k] = __fsub_rn(a[k], M);
+            y[k] = ex2_approx(fminf(fmaf(d[k], c2, tp.K), 17.5f));
+            const uint32_t r1 = __float_as_uint(fmaf(y[k], tp.fhi, 12582912.0f));
+            const uint32_t r2 = __float_as_uint(fmaf(y[k], tp.flo, 12582912.0f));
+            diff |= r1 ^ r2;
+            acc += r1;
         }
-        qlo = group8_sum_u(qlo);
-        qhi = group8_sum_u(qhi);
-        special = group8_or(special);
+        // WINDOW tiles: the same for binade lo + 1 (y / 2)
+        const bool win = tlive && ((tp.info >> 2) & 3u) == CLS_WINDOW;
+        uint32_t acch = 0u;
+        if (__any_sync(0xffffffffu, win)) {
+            const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t r3 = __float_as_uint(fmaf(y[k], hh, 12582912.0f));
+                const uint32_t r4 = __float_as_uint(fmaf(y[k], hl, 12582912.0f));
+                diff |= win ? (r3 ^ r4) : 0u;
+                acch += r3;
+            }
+            acch = group8_sum_u(acch - 4u * 0x4B400000u);
+        }
+        // counts in bits 0-23 (a tile sums to < 2^22.5), uncertified lanes
+        // counted from bit 24
+        acc = acc - 4u * 0x4B400000u + (diff ? (1u << 24) : 0u);
+        acc = group8_sum_u(acc);
+        if (check_nan) {
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                nanl |= (g0 + k < P.vocab && ((d[k] != d[k]) || t_nan || (isinf(d[k]) && t_inf))) ? 1u : 0u;
+        }
         if (l8 == 0 && tlive) {
+            const bool special = (tp.info & TP_SPECIAL) || (acc >> 24) != 0u;
+            const uint32_t qs = acc & 0xFFFFFFu;
             TileRec rr;
-            rr.lo = lo;
-            rr.cls = cls;
+            rr.lo = (int32_t)(tp.info >> 8) - 128;
+            rr.cls = (tp.info >> 2) & 3u;
             rr.aux = 0xFFFFFFFFu;
-            rr.qlo = Comp{qlo, qlo};
-            rr.qhi = Comp{qhi, qhi};
+            rr.qlo = Comp{qs, qs};
+            rr.qhi = win ? Comp{acch, acch} : Comp{0u, 0u};
             rec[tl] = rr;
             if (special) wlist[atomicAdd(&nlist, 1u)] = tl;
         }
         // candidates (index, logit): warp-aggregated reservation
-        if (__any_sync(0xffffffffu, nc != 0)) {
+        if (__any_sync(0xffffffffu, tlive && (tp.info & TP_CAND))) {
+            uint32_t nc = 0;
+            float x2v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                x2v[k] = (d[k] == 0.0f) ? 0.0f : d[k] * c2;
+                nc += (tlive && (tp.info & TP_CAND) && x2v[k] >= xf2) ? 1u : 0u;
+            }
             uint32_t incl = nc;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -1026,14 +1086,16 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
             }
             const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
             uint32_t cb = 0;
-            if (lane == 31) cb = atomicAdd(&hdr->n_cand, wtot);
+            if (lane == 31 && wtot) cb = atomicAdd(&hdr->n_cand, wtot);
             cb = __shfl_sync(0xffffffffu, cb, 31);
             uint32_t pos = cb + incl - nc;
+            if (nc) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                if (x2v[k] >= xf2) {
-                    if (pos < P.cand_stride) cand[pos] = Candidate{g0 + k, a[k]};
-                    pos++;
+                for (int k = 0; k < 4; k++) {
+                    if (x2v[k] >= xf2) {
+                        if (pos < P.cand_stride) cand[pos] = Candidate{g0 + k, a[k]};
+                        pos++;
+                    }
                 }
             }
         }
@@ -1066,7 +1128,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const float p = g < P.vocab ? prob_unnorm(a, M, T) : 0.0f;
         r.qlo = warp_comp_reduce(elem_comp(p, r.lo));
         if (r.cls == CLS_WINDOW) r.qhi = warp_comp_reduce(elem_comp(p, r.lo + 1));
-        if (r.cls == CLS_COMPLEX) {
+        if (r.cls != CLS_SIMPLE) {   // several binades: the walker may need the exact p
             uint32_t slot = 0;
             if (lane == 0) slot = atomicAdd(&hdr->n_wc, 1u);
             slot = __shfl_sync(0xffffffffu, slot, 0);
@@ -1148,7 +1210,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                 }
                 if (valid && r.cls == CLS_WINDOW) {
                     const uint32_t pa = (uint32_t)min(seg_a, (uint64_t)QSAT);
-                    wpre[j] = WTile{Comp{pa, pa}, Comp{0u, 0u}, 0xFFFFFFFFu, 0u};
+                    wpre[j] = WTile{Comp{pa, pa}, Comp{0u, 0u}, r.aux, 0u};
                     sid[j] = id;
                     sb[j] = seg_b - b;   // exclusive hi prefix
                 }
@@ -1227,7 +1289,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     if (live) {
         const uint32_t id = (((uint32_t)tid + 1 < NT) ? uarr[tid + 1] : nitems) - 1u;
         const TileRec r = rec[tid];
-        if (r.cls == CLS_WINDOW) wpre[tid] = WTile{carr[tid], carr2[tid], 0xFFFFFFFFu, 0u};
+        if (r.cls == CLS_WINDOW) wpre[tid] = WTile{carr[tid], carr2[tid], r.aux, 0u};
         bool is_end = ((uint32_t)tid + 1 == NT);
         if (!is_end) {
             const uint32_t nxt2 = ((uint32_t)tid + 2 < NT) ? uarr[tid + 2] : nitems;
@@ -1375,6 +1437,9 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const RowHdr *hdr = P.hdr + hrow;
 
     __shared__ Item sitems[ITEM_CHUNK];
+    __shared__ Item sall[ITEM_SMEM];             // every item of the row, when they fit
+    __shared__ WTile swp[SEG_TILES];             // one WINDOW stretch's prefix table
+    __shared__ uint32_t s_t0[MAX_SEG], s_nit[MAX_SEG], s_ioff[MAX_SEG + 1];
     __shared__ float tilep[TILE];
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
@@ -1407,7 +1472,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     uint32_t npow = 1;
     if (tid == 0) {
         walk_flags = 0;
+        walk_items = 0;
+        walk_slow = 0;
         n_zero = 0;
+        S_sh = __int_as_float(0x7fc00000);
     }
     __syncthreads();
     uint32_t nz = 0;
@@ -1432,11 +1500,38 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         }
     }
     if (nz) atomicAdd(&n_zero, nz);
+    // the walk's inputs (segment table, items) in shared memory, fetched by
+    // all threads at once rather than segment by segment on the walk's path
+    const uint32_t nseg = min(hdr->nseg, (uint32_t)MAX_SEG);
+    if ((uint32_t)tid < nseg) {
+        const uint32_t t0 = min(hdr->seg_tile0[tid], P.ntiles_total);
+        s_t0[tid] = t0;
+        s_nit[tid] = min(hdr->seg_items[tid], P.ntiles_total - t0);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t a = lane < nseg ? s_nit[lane] : 0u, b = lane + 32 < nseg ? s_nit[lane + 32] : 0u;
+        const uint32_t ia = warp_incl_scan_u(a), ib = warp_incl_scan_u(b);
+        const uint32_t ta = __shfl_sync(0xffffffffu, ia, 31);
+        if (lane < nseg) s_ioff[lane] = ia - a;
+        if (lane + 32 < nseg) s_ioff[lane + 32] = ta + ib - b;
+        if (lane == 31) s_ioff[nseg] = ta + ib;
+    }
+    __syncthreads();
+    const bool items_fit = s_ioff[nseg] <= (uint32_t)ITEM_SMEM;
+    if (items_fit) {
+        const Item *ib = P.items + (size_t)hrow * P.ntiles_total;
+        for (uint32_t sgi = 0; sgi < nseg; sgi++)
+            for (uint32_t j = tid; j < s_nit[sgi]; j += KB_THREADS) sall[s_ioff[sgi] + j] = ib[s_t0[sgi] + j];
+    }
     __syncthreads();
     const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
 
     if (warp == 0) {
-        // ---- the exact walk of the sequential f32 sum ----
+        // ---- the exact walk of the sequential f32 sum (skipped for a NaN
+        // row, whose sum is NaN whatever the order; warp 0 must still stay
+        // out of the sort's named barrier below) ----
+        if (!(flags0 & RF_NAN)) {
         SumState st{-126, 0u};
         uint32_t wflags = 0, nitems_all = 0, nslow = 0;
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
@@ -1453,19 +1548,23 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             st.e = __shfl_sync(0xffffffffu, st.e, 0);
             st.m = __shfl_sync(0xffffffffu, st.m, 0);
         };
-        const uint32_t nseg = min(hdr->nseg, (uint32_t)MAX_SEG);
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
-            const uint32_t t0 = min(hdr->seg_tile0[sgi], P.ntiles_total);
-            const uint32_t nit = min(hdr->seg_items[sgi], P.ntiles_total - t0);
+            const uint32_t t0 = s_t0[sgi];
+            const uint32_t nit = s_nit[sgi];
             const Item *ig = P.items + (size_t)hrow * P.ntiles_total + t0;
             nitems_all += nit;
-            for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
-                const uint32_t nc = min((uint32_t)ITEM_CHUNK, nit - i0);
-                __syncwarp();
-                for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ig[i0 + j];
-                __syncwarp();
+            const uint32_t chunk = items_fit ? max(nit, 1u) : (uint32_t)ITEM_CHUNK;
+            for (uint32_t i0 = 0; i0 < nit; i0 += chunk) {
+                const uint32_t nc = min(chunk, nit - i0);
+                const Item *src = sall + (items_fit ? s_ioff[sgi] : 0u);
+                if (!items_fit) {
+                    __syncwarp();
+                    for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ig[i0 + j];
+                    __syncwarp();
+                    src = sitems;
+                }
                 for (uint32_t j = 0; j < nc; j++) {
-                    const Item it = sitems[j];
+                    const Item it = src[j];
                     const uint32_t ntl = it.kind == CLS_COMPLEX ? 1u : min(it.aux, P.ntiles_total - it.tile);
                     // 0 applied, 1 window crossing, 2 recompute every tile, 3 stored p
                     int action = 2;
@@ -1504,7 +1603,14 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                     if (action == 1) {
                         // the running sum leaves binade lo inside this stretch:
                         // first tile c whose prefix count reaches 2^24
-                        const WTile *wp = wrow + it.tile;
+                        // the stretch's prefix table in shared memory in one
+                        // round trip (a stretch lies inside one segment)
+                        const WTile *wg = wrow + it.tile;
+                        const WTile *wp = swp;
+                        __syncwarp();
+                        for (uint32_t k = lane; k < ntl && k < (uint32_t)SEG_TILES; k += 32) swp[k] = wg[k];
+                        __syncwarp();
+                        if (ntl > (uint32_t)SEG_TILES) wp = wg;
                         const uint32_t pi = par;
                         uint32_t lo_i = 0, hi_i = ntl - 1;
                         while (lo_i < hi_i) {
@@ -1567,6 +1673,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             walk_flags = wflags;
             walk_items = nitems_all;
             walk_slow = nslow;
+        }
         }
     } else if (!big) {
         // ---- candidate sort in shared memory: ascending key ----
@@ -2101,6 +2208,60 @@ extern "C" bs_status bs_last_device_status(bs_sampler *s) {
     }
     delete[] h;
     return r;
+}
+
+// Self-check of the main loop's certificate (cert_eps): random logits placed
+// so that p / u_lo falls near the rounding points; every certified count must
+// equal the exact one (elem_comp of the restated expf's p).  out[0] counts
+// violations, out[1] certified samples, out[2] samples.
+__global__ void cert_check_kernel(uint32_t n, uint64_t seed, unsigned long long *out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t h = seed ^ (0x9E3779B97F4A7C15ull * (i + 1));
+    auto nxt = [&]() {
+        h += 0x9E3779B97F4A7C15ull;
+        uint64_t z = h;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    auto unif = [&]() { return (float)((nxt() >> 40) * 0x1p-24); };
+    const int lo = -100 + (int)(nxt() % 160);   // binades -100 .. 59
+    const float K = (float)(23 - lo);
+    const float T = 0.05f + 5.0f * unif();
+    const float M = -50.0f + 100.0f * unif();
+    const float c2 = (float)(1.4426950408889634 / (double)T);
+    // target y: near k + 1/2 (half of the samples) or anywhere, 2^-3 .. 2^17.5
+    const double ly = -3.0 + 20.5 * (double)unif();
+    double y0 = exp2(ly);
+    if (nxt() & 1) y0 = floor(y0) + 0.5 + (unif() - 0.5) * 2e-4 * y0;
+    const double x2 = log2(y0) - (double)K;   // <= 0 needs y0 <= 2^K
+    if (x2 > 0.0) return;
+    const float v = __fadd_rn(M, (float)(x2 * (double)T / 1.4426950408889634));
+    const float d = __fsub_rn(v, M);
+    const float y = ex2_approx(fminf(fmaf(d, c2, K), 17.5f));
+    const float e = fmaxf(cert_eps(K), 0x1p-17f);
+    const uint32_t r1 = __float_as_uint(fmaf(y, 1.0f + e, 12582912.0f));
+    const uint32_t r2 = __float_as_uint(fmaf(y, 1.0f - e, 12582912.0f));
+    atomicAdd(&out[2], 1ull);
+    if (r1 != r2) return;
+    atomicAdd(&out[1], 1ull);
+    const Comp ex = elem_comp(prob_unnorm(v, M, T), lo);
+    if (ex.q0 != ex.q1 || ex.q0 != r1 - 0x4B400000u) atomicAdd(&out[0], 1ull);
+}
+
+extern "C" bs_status bs_debug_cert_check(uint32_t n, uint64_t seed, unsigned long long *h_out) {
+    if (!h_out || n == 0) return BS_EINVAL;
+    unsigned long long *d = nullptr;
+    BS_CUDA(cudaMalloc(&d, 3 * sizeof(unsigned long long)));
+    cudaError_t e = cudaMemset(d, 0, 3 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        cert_check_kernel<<<(n + 255) / 256, 256>>>(n, seed, d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(h_out, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return cuda_status(e);
 }
 
 // Diagnostics for the test harness: per-row RowTrace of the last call

@@ -207,3 +207,19 @@ def test_repetition_penalty(gpu_pkg, orc):
     c = w.config(repetition_window=16, repetition_penalty=1.5)
     seeds = w.seeds(8)
     assert_same(run_gpu(gpu_pkg, c, x, seeds, prev), run_oracle(orc, c, x, seeds, prev), "penalty")
+
+
+def test_certificate_bound_holds(gpu_pkg):
+    # the main pass accepts a fast-exp grid count only when it is certified;
+    # every certified count must equal the exact one (cert_eps in sampler.cu)
+    import ctypes
+    L = gpu_pkg.lib()
+    L.bs_debug_cert_check.argtypes = [ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]
+    L.bs_debug_cert_check.restype = ctypes.c_int
+    out = np.zeros(3, np.uint64)
+    for seed in range(4):
+        assert L.bs_debug_cert_check(1 << 22, seed, out.ctypes.data) == 0
+        bad, certified, total = (int(v) for v in out)
+        assert total > (1 << 20)
+        assert bad == 0, f"{bad} certified counts differ from the exact ones (seed {seed})"
+        assert certified > total // 2
