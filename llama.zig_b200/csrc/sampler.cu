@@ -169,6 +169,18 @@ __device__ __forceinline__ uint32_t warp_incl_scan_u(uint32_t v) {
     return v;
 }
 
+// s = fl(...fl(fl(s + p_0) + p_1)... + p_31) over the warp's lanes in lane
+// order.  Every lane gathers the 32 values (shuffles issue back to back) and
+// runs the same 32 dependent adds from registers, so no broadcast is needed.
+__device__ __forceinline__ float warp_seq_add32(float s, float p) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; k++) v[k] = __shfl_sync(0xffffffffu, p, k);
+#pragma unroll
+    for (int k = 0; k < 32; k++) s = __fadd_rn(s, v[k]);
+    return s;
+}
+
 // Ordered reduction of lane composites (lane 0 = first element).  Result in lane 0.
 __device__ __forceinline__ Comp warp_comp_reduce(Comp c) {
     const int lane = threadIdx.x & 31;
@@ -1004,19 +1016,31 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                       (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
     const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
     uint32_t nanl = 0;
-#pragma unroll 2
-    for (int it = 0; it < ITERS; it++) {
+    // the quads of each half of the segment are all requested before any is
+    // used (loads in flight), at a register count that keeps 5 CTAs per SM
+    constexpr int HALF = ITERS / 2;
+#pragma unroll 1
+    for (int hb = 0; hb < 2; hb++) {
+    float4 qv[HALF];
+    if (fast) {
+#pragma unroll
+        for (int i2 = 0; i2 < HALF; i2++) qv[i2] = ldg_policy(xs4 + 32 * (warp + NW * (hb * HALF + i2)), pol);
+    } else {
+#pragma unroll
+        for (int i2 = 0; i2 < HALF; i2++) {
+            const uint32_t tl = 4 * (warp + NW * (hb * HALF + i2)) + sub;
+            qv[i2] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+            if (tl < ntile) qv[i2] = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
+        }
+    }
+#pragma unroll
+    for (int i2 = 0; i2 < HALF; i2++) {
+        const int it = hb * HALF + i2;
         const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
         const uint32_t t = seg * SEG_TILES + tl;
         const bool tlive = tl < ntile;
         const uint32_t g0 = t * TILE + 4 * l8;
-        float4 q;
-        if (fast) {
-            q = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
-        } else {
-            q = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
-            if (tlive) q = load_quad(P, x, g0, pol, swin, nwin);
-        }
+        const float4 q = qv[i2];
         const float a[4] = {q.x, q.y, q.z, q.w};
         const TileParam tp = tpar[tl < SEG_TILES ? tl : 0];
         // certified grid counts of binade lo: y = p / u_lo from the fast
@@ -1099,6 +1123,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                 }
             }
         }
+    }
     }
     if (__any_sync(0xffffffffu, nanl != 0) && lane == 0) atomicOr(&nanflag, 1u);
     __syncthreads();
@@ -1437,10 +1462,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const RowHdr *hdr = P.hdr + hrow;
 
     __shared__ Item sitems[ITEM_CHUNK];
-    __shared__ Item sall[ITEM_SMEM];             // every item of the row, when they fit
-    __shared__ WTile swp[SEG_TILES];             // one WINDOW stretch's prefix table
-    __shared__ uint32_t s_t0[MAX_SEG], s_nit[MAX_SEG], s_ioff[MAX_SEG + 1];
-    __shared__ float tilep[TILE];
+    __shared__ Item sall[ITEM_SMEM];             // the first `spec` items of every segment
+    __shared__ uint32_t woff[ITEM_SMEM];         // WINDOW item: its prefix table in wpool, or ~0u
+    __shared__ WTile wpool[WPOOL];
+    __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1];
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
     __shared__ uint32_t walk_flags, walk_items, walk_slow, n_zero;
@@ -1455,6 +1480,18 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t n_cand = min(hdr->n_cand, P.cand_stride);
     const uint32_t n_wc = min(hdr->n_wc, (uint32_t)WC_CAP);
     const bool big = n_cand > (uint32_t)CAND_SMEM;
+
+    // the walk's inputs in shared memory.  Segment s's items start at tile
+    // s * SEG_TILES; its first `spec` items are fetched speculatively in the
+    // same round trip as their count
+    const uint32_t nseg = min((P.ntiles_total + SEG_TILES - 1) / SEG_TILES, (uint32_t)MAX_SEG);
+    const uint32_t spec = ITEM_SMEM / nseg;
+    const Item *ib = P.items + (size_t)hrow * P.ntiles_total;
+    if ((uint32_t)tid < nseg) s_nit[tid] = min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES));
+    for (uint32_t i = tid; i < nseg * spec; i += KB_THREADS) {
+        const uint32_t sg = i / spec, j = i - sg * spec;
+        if (sg * SEG_TILES + j < P.ntiles_total && j < (uint32_t)SEG_TILES) sall[i] = ib[sg * SEG_TILES + j];
+    }
 
     // penalty window (for the recompute path)
     uint32_t nwin = 0;
@@ -1500,29 +1537,50 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         }
     }
     if (nz) atomicAdd(&n_zero, nz);
-    // the walk's inputs (segment table, items) in shared memory, fetched by
-    // all threads at once rather than segment by segment on the walk's path
-    const uint32_t nseg = min(hdr->nseg, (uint32_t)MAX_SEG);
-    if ((uint32_t)tid < nseg) {
-        const uint32_t t0 = min(hdr->seg_tile0[tid], P.ntiles_total);
-        s_t0[tid] = t0;
-        s_nit[tid] = min(hdr->seg_items[tid], P.ntiles_total - t0);
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const uint32_t a = lane < nseg ? s_nit[lane] : 0u, b = lane + 32 < nseg ? s_nit[lane + 32] : 0u;
-        const uint32_t ia = warp_incl_scan_u(a), ib = warp_incl_scan_u(b);
-        const uint32_t ta = __shfl_sync(0xffffffffu, ia, 31);
-        if (lane < nseg) s_ioff[lane] = ia - a;
-        if (lane + 32 < nseg) s_ioff[lane + 32] = ta + ib - b;
-        if (lane == 31) s_ioff[nseg] = ta + ib;
-    }
-    __syncthreads();
-    const bool items_fit = s_ioff[nseg] <= (uint32_t)ITEM_SMEM;
-    if (items_fit) {
-        const Item *ib = P.items + (size_t)hrow * P.ntiles_total;
-        for (uint32_t sgi = 0; sgi < nseg; sgi++)
-            for (uint32_t j = tid; j < s_nit[sgi]; j += KB_THREADS) sall[s_ioff[sgi] + j] = ib[s_t0[sgi] + j];
+    // prefix tables of the WINDOW items held in shared memory (offsets by a
+    // block scan over the item slots, two per thread; tables that do not fit
+    // stay in global memory)
+    {
+        uint32_t len[2] = {0u, 0u};
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t i = 2 * tid + h;
+            if (i < nseg * spec) {
+                const uint32_t sg = i / spec;
+                if (i - sg * spec < s_nit[sg] && sall[i].kind == CLS_WINDOW)
+                    len[h] = min(sall[i].aux, P.ntiles_total - min(sall[i].tile, P.ntiles_total));
+            }
+        }
+        const uint32_t mine = len[0] + len[1];
+        const uint32_t incl = warp_incl_scan_u(mine);
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t r = 0;
+            for (int w = 0; w < KB_THREADS / 32; w++) {
+                const uint32_t v = wsum[w];
+                wsum[w] = r;
+                r += v;
+            }
+        }
+        __syncthreads();
+        uint32_t off = wsum[warp] + incl - mine;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t i = 2 * tid + h;
+            woff[i] = (len[h] && off + len[h] <= (uint32_t)WPOOL) ? off : 0xFFFFFFFFu;
+            off += len[h];
+        }
+        __syncthreads();
+        // one warp per item slot copies its table
+        const WTile *wrow_g = P.wpre + (size_t)hrow * P.ntiles_total;
+        for (uint32_t i = warp; i < nseg * spec; i += KB_THREADS / 32) {
+            const uint32_t o = woff[i];
+            if (o == 0xFFFFFFFFu) continue;
+            const Item &itm = sall[i];
+            const uint32_t n = min(itm.aux, P.ntiles_total - min(itm.tile, P.ntiles_total));
+            for (uint32_t k = lane; k < n; k += 32) wpool[o + k] = wrow_g[itm.tile + k];
+        }
     }
     __syncthreads();
     const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
@@ -1537,27 +1595,18 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
         // add one tile element by element, p recomputed from the logits
         auto add_tile = [&](uint32_t tile) {
-            tilep[lane] = exact_p_at(P, row, tile * TILE + lane, M, swin, nwin);
-            __syncwarp();
-            if (lane == 0) {
-                float s = float_of(st);
-                for (int k = 0; k < TILE; k++) s = __fadd_rn(s, tilep[k]);
-                st = state_of(s);
-            }
-            __syncwarp();
-            st.e = __shfl_sync(0xffffffffu, st.e, 0);
-            st.m = __shfl_sync(0xffffffffu, st.m, 0);
+            st = state_of(warp_seq_add32(float_of(st), exact_p_at(P, row, tile * TILE + lane, M, swin, nwin)));
         };
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
-            const uint32_t t0 = s_t0[sgi];
             const uint32_t nit = s_nit[sgi];
-            const Item *ig = P.items + (size_t)hrow * P.ntiles_total + t0;
+            const Item *ig = ib + sgi * SEG_TILES;
             nitems_all += nit;
-            const uint32_t chunk = items_fit ? max(nit, 1u) : (uint32_t)ITEM_CHUNK;
+            const bool in_smem = nit <= spec;
+            const uint32_t chunk = in_smem ? max(nit, 1u) : (uint32_t)ITEM_CHUNK;
             for (uint32_t i0 = 0; i0 < nit; i0 += chunk) {
                 const uint32_t nc = min(chunk, nit - i0);
-                const Item *src = sall + (items_fit ? s_ioff[sgi] : 0u);
-                if (!items_fit) {
+                const Item *src = sall + sgi * spec;
+                if (!in_smem) {
                     __syncwarp();
                     for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ig[i0 + j];
                     __syncwarp();
@@ -1565,6 +1614,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                 }
                 for (uint32_t j = 0; j < nc; j++) {
                     const Item it = src[j];
+                    const uint32_t wo = in_smem ? woff[sgi * spec + j] : 0xFFFFFFFFu;
                     const uint32_t ntl = it.kind == CLS_COMPLEX ? 1u : min(it.aux, P.ntiles_total - it.tile);
                     // 0 applied, 1 window crossing, 2 recompute every tile, 3 stored p
                     int action = 2;
@@ -1586,31 +1636,17 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                     }
                     if (action == 2 && it.kind == CLS_COMPLEX && it.aux < n_wc) action = 3;
                     if (action == 0) continue;
-                    if (action == 3) {
-                        tilep[lane] = wcs[it.aux * TILE + lane];   // stored exact p
-                        __syncwarp();
-                        if (lane == 0) {
-                            float s = float_of(st);
-                            for (int k = 0; k < TILE; k++) s = __fadd_rn(s, tilep[k]);
-                            st = state_of(s);
-                        }
-                        __syncwarp();
-                        st.e = __shfl_sync(0xffffffffu, st.e, 0);
-                        st.m = __shfl_sync(0xffffffffu, st.m, 0);
+                    if (action == 3) {   // stored exact p
+                        st = state_of(warp_seq_add32(float_of(st), wcs[it.aux * TILE + lane]));
                         continue;
                     }
                     uint32_t from = 0;
                     if (action == 1) {
                         // the running sum leaves binade lo inside this stretch:
                         // first tile c whose prefix count reaches 2^24
-                        // the stretch's prefix table in shared memory in one
-                        // round trip (a stretch lies inside one segment)
-                        const WTile *wg = wrow + it.tile;
-                        const WTile *wp = swp;
-                        __syncwarp();
-                        for (uint32_t k = lane; k < ntl && k < (uint32_t)SEG_TILES; k += 32) swp[k] = wg[k];
-                        __syncwarp();
-                        if (ntl > (uint32_t)SEG_TILES) wp = wg;
+                        // the stretch's prefix table (shared memory when it
+                        // was gathered)
+                        const WTile *wp = wo != 0xFFFFFFFFu ? wpool + wo : wrow + it.tile;
                         const uint32_t pi = par;
                         uint32_t lo_i = 0, hi_i = ntl - 1;
                         while (lo_i < hi_i) {
@@ -1636,17 +1672,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                             st.m += pi ? pc.q1 : pc.q0;
                         }
                         const uint32_t sl = wp[c].slot;
-                        if (sl < n_wc) {
-                            tilep[lane] = wcs[sl * TILE + lane];   // stored exact p
-                            __syncwarp();
-                            if (lane == 0) {
-                                float s = float_of(st);
-                                for (int k = 0; k < TILE; k++) s = __fadd_rn(s, tilep[k]);
-                                st = state_of(s);
-                            }
-                            __syncwarp();
-                            st.e = __shfl_sync(0xffffffffu, st.e, 0);
-                            st.m = __shfl_sync(0xffffffffu, st.m, 0);
+                        if (sl < n_wc) {   // stored exact p
+                            st = state_of(warp_seq_add32(float_of(st), wcs[sl * TILE + lane]));
                         } else {
                             add_tile(it.tile + c);
                         }

@@ -18,7 +18,8 @@ constexpr int HIST_BINS = 256;           // top-p tail-mass histogram bins
 constexpr int WC_CAP = 256;              // window/complex tiles with stored p per row
 constexpr int KSEL_MAX = 256;            // largest top_k served by the tile-max floor
 constexpr int ITEM_CHUNK = 128;          // items staged per step in Kernel B (rows with many items)
-constexpr int ITEM_SMEM = 512;           // items of a row held in shared memory at once
+constexpr int ITEM_SMEM = 512;           // items of a row held in shared memory (spread over its segments)
+constexpr int WPOOL = 256;               // WINDOW prefix-table entries of a row held in shared memory
 
 // Tile classes (running-sum binade candidates over the tile).
 enum : uint32_t { CLS_SIMPLE = 0, CLS_WINDOW = 1, CLS_COMPLEX = 2 };
