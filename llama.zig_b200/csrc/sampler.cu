@@ -470,7 +470,6 @@ struct K12Params {
     SegStat *sstat;           // per handle row: MAX_SEG
     uint32_t *khist;          // per handle row: MAX_SEG x KH_BINS tile counts
     float *mhist;             // per handle row: MAX_SEG x KH_BINS masses
-    uint32_t *done;           // per handle row: K1 segments finished
     RowInfo *rinfo;           // per handle row
     RowHdr *hdr;
     Item *items;
@@ -478,6 +477,7 @@ struct K12Params {
     float *wcdata;
     Candidate *cand;          // per handle row: cand_stride entries (idx, logit)
     uint32_t cand_stride;
+    uint32_t *kerr;           // per handle: a bounded device wait gave up
 };
 
 __device__ __forceinline__ bool penalty_active(const K12Params &P) {
@@ -631,7 +631,11 @@ __device__ __forceinline__ uint32_t group8_or(uint32_t v) {
 }
 
 // ---------------------------------------------------------------------------
-// K1: tile statistics (HBM pass), then the row reduction by the last CTA.
+// K1: tile statistics of one segment per CTA (the HBM pass).  Per tile: the
+// maximum and the sum of 2^((v - tile max) log2e / T); per segment: the
+// maximum, the sum relative to it, a non-finite flag and, for top-p without a
+// top-k floor, the tail-element histogram.  No cross-CTA step: the row
+// reduction is k1_rows.
 __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const uint32_t seg = blockIdx.x, row = blockIdx.y, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -640,24 +644,20 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const float c2 = P.c2;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
     __shared__ uint32_t swin[256];
-    __shared__ uint32_t kh[KH_BINS];
     __shared__ uint32_t mh[KH_BINS];   // tail element counts per bin
     __shared__ float stm[SEG_TILES];   // tile maxima of this segment
     __shared__ float sts[SEG_TILES];   // tile sums relative to the tile maxima
     __shared__ float wm[NW];
     __shared__ uint32_t wf[NW];
     __shared__ double wd[NW];
-    __shared__ uint32_t is_last;
     const uint32_t nwin = load_window(P, row, swin);
-    for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) {
-        kh[b] = 0u;
-        mh[b] = 0u;
-    }
     const bool k_floor = P.top_k > 0 && P.top_k < P.vocab && P.top_k <= KSEL_MAX;
     const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
     const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
     const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
-    if (nwin) __syncthreads();
+    if (p_floor)
+        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) mh[b] = 0u;
+    if (nwin || p_floor) __syncthreads();
 
     const uint64_t pol = l2_policy_evict_last();
     const uint32_t sub = lane >> 3, l8 = lane & 7;
@@ -721,17 +721,13 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         sm = fmaxf(sm, wm[w]);
         nfs |= wf[w];
     }
-    // segment sum relative to the segment maximum; tile-maximum histogram
+    // segment sum relative to the segment maximum
     double ss = 0.0;
     if ((uint32_t)tid < ntile) {
         const float tm = stm[tid];
-        if (tm > NEG_INF) {
-            const float xr = (tm - sm) * c2;
-            ss = (double)sts[tid] * (double)ex2_approx(xr);
-            if (k_floor && xr > -64.0f) atomicAdd(&kh[min(KH_BINS - 1, (int)(-xr * 4.0f))], 1u);
-        }
+        if (tm > NEG_INF) ss = (double)sts[tid] * (double)ex2_approx((tm - sm) * c2);
     }
-    // top-p without a top-k floor: tail-mass histogram relative to the
+    // top-p without a top-k floor: tail-element histogram relative to the
     // segment maximum (second read of the segment, from L2)
     if (p_floor && sm > NEG_INF) {
         const float sc = sm * c2;
@@ -751,34 +747,46 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     if (lane == 0) wd[warp] = ss;
     __syncthreads();
     if (tid == 0) {
-        double s = 0.0;
-        for (int w = 0; w < NW; w++) s += wd[w];
+        double sacc = 0.0;
+        for (int w = 0; w < NW; w++) sacc += wd[w];
         SegStat st;
         st.smax = sm;
         st.nonfin = nfs;
-        st.ssum = s;
+        st.ssum = sacc;
         st.base = 0.0;
         st.pad = 0.0;
         P.sstat[(size_t)hrow * MAX_SEG + seg] = st;
     }
-    if (k_floor)
-        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) P.khist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = kh[b];
     if (p_floor)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS)   // mass bound: count x the bin's upper edge
             P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = (float)mh[b] * exp2f(-0.25f * (float)b);
-    // the last segment of the row to finish reduces the row
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = (atomicAdd(&P.done[hrow], 1u) == P.nseg - 1) ? 1u : 0u;
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
+}
+
+// Row reduction, one CTA per row: the row maximum M, the raw prefix estimate
+// at every segment start, and the candidate floor (log2 p relative to M):
+//   top-k: from the tile maxima, binned by quarter octaves below M: the
+//     first bin edge with at least k tiles above it (so at least k logits);
+//   top-p without top-k: from the segments' tail-element histograms (a
+//     bound on the mass below each grid point);
+//   min-p: ln(min_p) in log2 units, minus a margin.
+__global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
+    const uint32_t row = blockIdx.x, hrow = P.row0 + row;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = K12_THREADS / 32;
+    const float c2 = P.c2;
+    const bool k_floor = P.top_k > 0 && P.top_k < P.vocab && P.top_k <= KSEL_MAX;
+    const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
+    const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
+    const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
 
     __shared__ float off[MAX_SEG];   // (segment max - M) log2e / T
     __shared__ float ssc[MAX_SEG];   // segment tail mass scale 2^off
     __shared__ RowInfo ri;
+    __shared__ uint32_t kh[KH_BINS];
+    __shared__ int kj_w[NW], pj_w[NW];
     const SegStat *S = P.sstat + (size_t)hrow * MAX_SEG;
     const uint32_t ns = P.nseg;
+    for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) kh[b] = 0u;
     if (warp == 0) {
         float m = NEG_INF;
         uint32_t nf = 0;
@@ -808,9 +816,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
                 const double u = __shfl_up_sync(0xffffffffu, incl, k);
                 if (lane >= k) incl += u;
             }
-            if (c < ns) {
-                P.sstat[(size_t)hrow * MAX_SEG + c].base = run + incl - sv;
-            }
+            if (c < ns) P.sstat[(size_t)hrow * MAX_SEG + c].base = run + incl - sv;
             run += __shfl_sync(0xffffffffu, incl, 31);
         }
         if (lane == 0) {
@@ -820,55 +826,59 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         }
     }
     __syncthreads();
-    // floors on the quarter-octave grid f_j = -j/4 (log2 p, relative to M).
-    // Segment c's bin b spans [off_c - (b+1)/4, off_c - b/4).  One warp per
-    // segment turns its histograms into cumulative ones in shared memory;
-    // then thread j evaluates grid point j.
-    // Segments are processed in chunks of RED_CHUNK: one warp per segment
-    // turns its histograms into cumulative ones in shared memory, then thread
-    // j accumulates grid point j.
-    __shared__ uint32_t cumk[RED_CHUNK * KH_BINS];
+    const float M = ri.M;
+    // top-k: tile maxima per quarter-octave bin below M (the same x2 as the
+    // main pass's per-logit candidate test, which is monotone in the logit)
+    uint32_t kcount = 0;   // tiles whose maximum is above the bin edge -(tid+1)/4
+    if (k_floor) {
+        const TileStat *ts = P.tstat + (size_t)hrow * P.ntiles_total;
+        for (uint32_t t = tid; t < P.ntiles_total; t += K12_THREADS) {
+            const float tm = ts[t].tmax;
+            const float d = __fsub_rn(tm, M);
+            const float x2 = (d == 0.0f) ? 0.0f : d * c2;
+            if (x2 > -64.0f) atomicAdd(&kh[min(KH_BINS - 1, (int)(-x2 * 4.0f))], 1u);
+        }
+        __syncthreads();
+        // inclusive prefix over bins 0..tid (bins hold x2 in (-(b+1)/4, -b/4])
+        const uint32_t v = kh[tid];
+        const uint32_t incl = warp_incl_scan_u(v);
+        if (lane == 31) kj_w[warp] = (int)incl;
+        __syncthreads();
+        uint32_t base = 0;
+        for (int w = 0; w < warp; w++) base += (uint32_t)kj_w[w];
+        kcount = base + incl;
+        __syncthreads();
+    }
+    // top-p without top-k: mass possibly below the grid point f_j = -j/4.
+    // Segment c's bin b spans [off_c - (b+1)/4, off_c - b/4).  Segments are
+    // processed in chunks of RED_CHUNK: one warp per segment turns its
+    // histogram into a cumulative one in shared memory, then thread j
+    // accumulates grid point j.
     __shared__ float cumm[RED_CHUNK * KH_BINS];
     __shared__ float mtot[RED_CHUNK];
-    const uint32_t *KH = P.khist + (size_t)hrow * MAX_SEG * KH_BINS;
     const float *MH = P.mhist + (size_t)hrow * MAX_SEG * KH_BINS;
-    uint32_t kcount = 0;   // tiles whose maximum is surely >= f_j (under-count)
     float mbelow = 0.0f;   // mass possibly below f_j (over-count), units of p(M)
-    if (k_floor || p_floor) {
+    if (p_floor) {
         for (uint32_t c0 = 0; c0 < ns; c0 += RED_CHUNK) {
             const uint32_t nc = min((uint32_t)RED_CHUNK, ns - c0);
             __syncthreads();
             for (uint32_t cc = warp; cc < nc; cc += NW) {
                 const uint32_t c = c0 + cc;
-                uint32_t kc[8];
                 float mc[8];
-                uint32_t ks = 0;
                 float ms = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    kc[j] = k_floor ? KH[(size_t)c * KH_BINS + lane * 8 + j] : 0u;
-                    mc[j] = p_floor ? MH[(size_t)c * KH_BINS + lane * 8 + j] : 0.0f;
-                    ks += kc[j];
-                    ms += mc[j];
-                    kc[j] = ks;
+                    ms += MH[(size_t)c * KH_BINS + lane * 8 + j];
                     mc[j] = ms;
                 }
-                uint32_t ki = ks;
                 float mi = ms;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
-                    const uint32_t u = __shfl_up_sync(0xffffffffu, ki, o);
                     const float w2 = __shfl_up_sync(0xffffffffu, mi, o);
-                    if (lane >= o) {
-                        ki += u;
-                        mi += w2;
-                    }
+                    if (lane >= o) mi += w2;
                 }
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    cumk[cc * KH_BINS + lane * 8 + j] = kc[j] + ki - ks;
-                    cumm[cc * KH_BINS + lane * 8 + j] = mc[j] + mi - ms;
-                }
+                for (int j = 0; j < 8; j++) cumm[cc * KH_BINS + lane * 8 + j] = mc[j] + mi - ms;
                 if (lane == 31) mtot[cc] = mi;
             }
             __syncthreads();
@@ -878,7 +888,6 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
                 // bins entirely above f_j: b <= floor(4 o) + j - 1
                 const float fb = floorf(4.0f * o);
                 const int bmax = fb < -1e6f ? -1 : min(KH_BINS - 1, (int)fb + tid - 1);
-                kcount += bmax >= 0 ? cumk[cc * KH_BINS + bmax] : 0u;
                 const float ma = bmax >= 0 ? cumm[cc * KH_BINS + bmax] : 0.0f;
                 // mass below -64 octaves of the segment maximum is not binned:
                 // at most SEG_ELEMS * 2^-64 of it
@@ -887,7 +896,6 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         }
     }
     const uint32_t kmask = __ballot_sync(0xffffffffu, kcount >= P.top_k);
-    __shared__ int kj_w[NW], pj_w[NW];
     const double budget = (1.0 - (double)P.top_p - p_margin) * fmax(1.0, 0.99 * ri.S_raw);
     const uint32_t pmask = __ballot_sync(0xffffffffu, (double)mbelow * 1.01 + 1e-30 <= budget);
     if (lane == 0) {
@@ -904,7 +912,8 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         float xf2 = -150.01f;   // every p > 0
         uint32_t binding = 0;
         if (k_floor && kj < KH_BINS) {
-            const float xk = -(float)kj * 0.25f - 1e-3f;
+            // at least top_k tiles have their maximum above -(kj+1)/4
+            const float xk = -(float)(kj + 1) * 0.25f - 1e-3f;
             if (xk > xf2) { xf2 = xk; binding = 1; }
         }
         if (p_floor && pj < KH_BINS) {
@@ -928,7 +937,6 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         hdr->n_wc = 0;
         hdr->flags = 0;
         hdr->nseg = ns;
-        P.done[hrow] = 0;   // ready for the next call
     }
 }
 
@@ -1375,6 +1383,7 @@ struct KBParams {
     uint32_t cand_stride;
     uint64_t *rng;       // per handle row, 4 words
     RowTrace *trace;     // per handle row
+    const uint32_t *kerr;
     uint32_t *out;       // per call row
 };
 
@@ -1763,7 +1772,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __syncthreads();
     if (tid != 0) return;
 
-    uint32_t status = ROW_OK;
+    uint32_t status = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
     uint32_t token = 0;
     uint32_t path = 0;
     uint32_t n_kept = 0;
@@ -1831,7 +1840,9 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         }
         const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || n_sel < n_pos ||
                               (k_act && P.top_k <= n_pos);
-        if (!cover_ok) {
+        if (status != ROW_OK) {
+            // a bounded device wait gave up: nothing of this call is trusted
+        } else if (!cover_ok) {
             status = ROW_EINTERNAL;
             flags |= RF_CAND_SHORT;
         } else if (P.typical_p > 0.0f && P.typical_p < 1.0f) {
@@ -1901,7 +1912,6 @@ struct bs_sampler {
     SegStat *d_sstat;
     uint32_t *d_khist;
     float *d_mhist;
-    uint32_t *d_done;
     RowInfo *d_rinfo;
     Item *d_items;
     WTile *d_wpre;
@@ -1910,6 +1920,7 @@ struct bs_sampler {
     unsigned long long *d_ctmp;
     uint32_t cand_stride;
     RowTrace *d_trace;
+    uint32_t *d_kerr;        // sticky: a bounded device wait gave up
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -1967,7 +1978,6 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_sstat);
     cudaFree(s->d_khist);
     cudaFree(s->d_mhist);
-    cudaFree(s->d_done);
     cudaFree(s->d_rinfo);
     cudaFree(s->d_items);
     cudaFree(s->d_wpre);
@@ -1975,6 +1985,7 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_cand);
     cudaFree(s->d_ctmp);
     cudaFree(s->d_trace);
+    cudaFree(s->d_kerr);
     cudaFree(s->d_logits_stage);
     cudaFree(s->d_prev_stage);
     cudaFree(s->d_out_stage);
@@ -2025,7 +2036,6 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     if (e == cudaSuccess) e = cudaMalloc(&s->d_sstat, (size_t)batch * MAX_SEG * sizeof(SegStat));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_khist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_mhist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s->d_done, (size_t)batch * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_rinfo, (size_t)batch * sizeof(RowInfo));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_items, (size_t)batch * s->ntiles_total * sizeof(Item));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_wpre, (size_t)batch * s->ntiles_total * sizeof(WTile));
@@ -2033,6 +2043,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     if (e == cudaSuccess) e = cudaMalloc(&s->d_cand, (size_t)batch * s->cand_stride * sizeof(Candidate));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_ctmp, (size_t)batch * 2 * s->cand_stride * sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_trace, (size_t)batch * sizeof(RowTrace));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_kerr, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         free_all(s);
@@ -2054,7 +2065,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     e = cudaMemcpy(s->d_rng, h, (size_t)batch * 4 * sizeof(uint64_t), cudaMemcpyHostToDevice);
     delete[] h;
     if (e == cudaSuccess) e = cudaMemset(s->d_trace, 0, (size_t)batch * sizeof(RowTrace));
-    if (e == cudaSuccess) e = cudaMemset(s->d_done, 0, (size_t)batch * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(s->d_kerr, 0, sizeof(uint32_t));
     if (e == cudaSuccess) e = raise_smem_limits(s->smem_a, s->smem_b);
     if (e != cudaSuccess) {
         fprintf(stderr, "b200_sampler: setup failed: %s\n", cudaGetErrorString(e));
@@ -2113,7 +2124,6 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.sstat = s->d_sstat;
     A.khist = s->d_khist;
     A.mhist = s->d_mhist;
-    A.done = s->d_done;
     A.rinfo = s->d_rinfo;
     A.hdr = s->d_hdr;
     A.items = s->d_items;
@@ -2121,11 +2131,13 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.wcdata = s->d_wc;
     A.cand = s->d_cand;
     A.cand_stride = s->cand_stride;
+    A.kerr = s->d_kerr;
 
     cudaEvent_t *ev = nullptr;
     if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
     if (ev) cudaEventRecord(ev[0], st);
     k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    k1_rows<<<rows, K12_THREADS, 0, st>>>(A);
     if (ev) cudaEventRecord(ev[1], st);
     k2_main<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
     if (ev) cudaEventRecord(ev[2], st);
@@ -2159,6 +2171,7 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.cand_stride = s->cand_stride;
     B.rng = s->d_rng;
     B.trace = s->d_trace;
+    B.kerr = s->d_kerr;
     B.out = d_out;
     kernel_b<<<rows, KB_THREADS, s->smem_b, st>>>(B);
     if (ev) cudaEventRecord(ev[3], st);
@@ -2231,6 +2244,7 @@ extern "C" bs_status bs_last_device_status(bs_sampler *s) {
     if (e != cudaSuccess) r = BS_ECUDA;
     for (uint32_t i = 0; r == BS_OK && i < s->batch; i++) {
         if (h[i].status == ROW_ENOTSUP) r = BS_ENOTSUP;
+        else if (h[i].status == ROW_ETIMEOUT) r = BS_ETIMEOUT;
         else if (h[i].status != ROW_OK) r = BS_EINTERNAL;
     }
     delete[] h;
@@ -2343,10 +2357,10 @@ constexpr StaticSizes static_sizes(uint32_t rows, uint32_t vocab) {
     const size_t nt = (vocab + TILE - 1) / TILE, cs = (vocab + 31u) & ~31u;
     return StaticSizes{{r256(rows * sizeof(RowHdr)), r256(rows * nt * sizeof(TileStat)),
                         r256(rows * MAX_SEG * sizeof(SegStat)), r256(rows * MAX_SEG * KH_BINS * sizeof(uint32_t)),
-                        r256(rows * MAX_SEG * KH_BINS * sizeof(float)), r256(rows * sizeof(uint32_t)),
-                        r256(rows * sizeof(RowInfo)), r256(rows * nt * sizeof(Item)), r256(rows * nt * sizeof(WTile)),
+                        r256(rows * MAX_SEG * KH_BINS * sizeof(float)), r256(rows * sizeof(RowInfo)), r256(rows * nt * sizeof(Item)), r256(rows * nt * sizeof(WTile)),
                         r256(rows * WC_CAP * TILE * sizeof(float)), r256(rows * cs * sizeof(Candidate)),
-                        r256(rows * 2 * cs * sizeof(unsigned long long)), r256(rows * sizeof(RowTrace))}};
+                        r256(rows * 2 * cs * sizeof(unsigned long long)), r256(rows * sizeof(RowTrace)),
+                        r256(sizeof(uint32_t))}};
 }
 constexpr size_t static_total(uint32_t rows, uint32_t vocab) {
     const StaticSizes s = static_sizes(rows, vocab);
@@ -2427,17 +2441,16 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     s.d_sstat = static_cast<SegStat *>(ptr[2]);
     s.d_khist = static_cast<uint32_t *>(ptr[3]);
     s.d_mhist = static_cast<float *>(ptr[4]);
-    s.d_done = static_cast<uint32_t *>(ptr[5]);
-    s.d_rinfo = static_cast<RowInfo *>(ptr[6]);
-    s.d_items = static_cast<Item *>(ptr[7]);
-    s.d_wpre = static_cast<WTile *>(ptr[8]);
-    s.d_wc = static_cast<float *>(ptr[9]);
-    s.d_cand = static_cast<Candidate *>(ptr[10]);
-    s.d_ctmp = static_cast<unsigned long long *>(ptr[11]);
-    s.d_trace = static_cast<RowTrace *>(ptr[12]);
-    // the per-row completion counters of the statistics pass must start at
-    // zero; the pass leaves them at zero, but a call that failed part-way
-    // might not have
-    BS_CUDA(cudaMemsetAsync(s.d_done, 0, (size_t)rows * sizeof(uint32_t), (cudaStream_t)stream));
+    s.d_rinfo = static_cast<RowInfo *>(ptr[5]);
+    s.d_items = static_cast<Item *>(ptr[6]);
+    s.d_wpre = static_cast<WTile *>(ptr[7]);
+    s.d_wc = static_cast<float *>(ptr[8]);
+    s.d_cand = static_cast<Candidate *>(ptr[9]);
+    s.d_ctmp = static_cast<unsigned long long *>(ptr[10]);
+    s.d_trace = static_cast<RowTrace *>(ptr[11]);
+    s.d_kerr = static_cast<uint32_t *>(ptr[12]);   // zero at load; sticky like a handle's
+    // nothing in the scratch has to start at zero: every buffer a call reads
+    // is written earlier in the same call (the error word is zero at load and
+    // only ever set)
     return bs_sample(&s, d_logits, ld, 0, rows, d_prev, n_prev, d_out, stream);
 }

@@ -34,7 +34,7 @@ enum : uint32_t {
 };
 
 // Kernel output status per row (written by Kernel B).
-enum : uint32_t { ROW_OK = 0, ROW_ENOTSUP = 6, ROW_EINTERNAL = 7 };
+enum : uint32_t { ROW_OK = 0, ROW_ETIMEOUT = 5, ROW_ENOTSUP = 6, ROW_EINTERNAL = 7 };
 
 // Row header in scratch: written by Kernel A, read by Kernel B.
 struct RowHdr {
