@@ -631,6 +631,126 @@ __device__ __forceinline__ uint32_t group8_or(uint32_t v) {
 }
 
 // ---------------------------------------------------------------------------
+// Segment staging: one bulk copy (cp.async.bulk, global -> shared, completion
+// on an mbarrier) of a CTA's 32 KB segment.  Thread t then reduces tile t from
+// shared memory, reading its eight float4 in the order j ^ (t & 7) so that the
+// eight threads of a quarter-warp hit distinct banks.
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+// Waits for phase `parity` of the barrier; false after `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (i > 64) __nanosleep(256);
+    }
+    return false;
+}
+constexpr uint32_t MBAR_POLL_LIMIT = 1u << 22;   // about a second of polling
+
+// The segment can be bulk copied: no penalised ids (they are applied while
+// loading), a 16-byte aligned start and a whole number of 16-byte chunks.
+__device__ __forceinline__ bool seg_bulk_ok(const K12Params &P, const float *xs, uint32_t n, uint32_t nwin) {
+    return nwin == 0 && (reinterpret_cast<uintptr_t>(xs) & 15u) == 0 && (n & 3u) == 0;
+}
+
+// Issues the segment's bulk copy (thread 0) if it is possible; the caller
+// waits with seg_wait.  Returns whether the copy was issued (block-uniform).
+__device__ __forceinline__ bool seg_issue(const K12Params &P, const float *xs, uint32_t n, uint32_t nwin,
+                                          float4 *sbuf, uint64_t *bar, uint64_t pol) {
+    const bool bulk = seg_bulk_ok(P, xs, n, nwin);
+    if (bulk && threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        bulk_load(sbuf, xs, n * 4u, bar, pol);
+    }
+    return bulk;
+}
+
+// Waits for the copy (bounded).  On a timeout the block loads from global
+// memory instead and the handle's error word records the failure; thread 0
+// then waits once more (bounded) so that a late copy cannot land in a later
+// CTA's shared memory.  Returns whether the shared copy is usable
+// (block-uniform).
+__device__ __forceinline__ bool seg_wait(const K12Params &P, uint64_t *bar) {
+    const bool ok = mbar_wait(bar, 0u, MBAR_POLL_LIMIT);
+    const bool all = __syncthreads_and(ok) != 0;
+    if (!all && threadIdx.x == 0) {
+        atomicOr(P.kerr, 1u);
+        mbar_wait(bar, 0u, MBAR_POLL_LIMIT);
+    }
+    return all;
+}
+
+// Tile `tl` of the segment (32 logits, -inf past the vocabulary), from the
+// shared copy or, without one, from global memory with the penalty applied.
+// The logits come back permuted: v[4 j + c] is element 4 (j ^ (tl & 7)) + c of
+// the tile (a register array must be indexed by compile-time constants).
+__device__ __forceinline__ uint32_t tile_elem(uint32_t tl, int j, int c) {
+    return 4u * ((uint32_t)j ^ (tl & 7u)) + (uint32_t)c;
+}
+__device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, uint32_t seg, uint32_t tl,
+                                            const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
+                                            uint64_t pol, float v[TILE]) {
+    const uint32_t g0 = seg * SEG_ELEMS + tl * TILE;
+    if (staged) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t jj = (uint32_t)j ^ (tl & 7u);
+            const float4 q = sbuf[tl * 8 + jj];
+            const uint32_t g = g0 + 4 * jj;
+            v[4 * j] = g < P.vocab ? q.x : NEG_INF;
+            v[4 * j + 1] = g + 1 < P.vocab ? q.y : NEG_INF;
+            v[4 * j + 2] = g + 2 < P.vocab ? q.z : NEG_INF;
+            v[4 * j + 3] = g + 3 < P.vocab ? q.w : NEG_INF;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float4 q = load_quad(P, x, g0 + tile_elem(tl, j, 0), pol, swin, nwin);
+            v[4 * j] = q.x;
+            v[4 * j + 1] = q.y;
+            v[4 * j + 2] = q.z;
+            v[4 * j + 3] = q.w;
+        }
+    }
+}
+
+// Chunk j of tile `tl` (logits 4 (j ^ (tl & 7)) .. +3, -inf past the
+// vocabulary), from the shared copy or from global memory.
+__device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, uint32_t seg, uint32_t tl, int j,
+                                            const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
+                                            uint64_t pol) {
+    const uint32_t g = seg * SEG_ELEMS + tl * TILE + tile_elem(tl, j, 0);
+    if (!staged) return load_quad(P, x, g, pol, swin, nwin);
+    float4 q = sbuf[tl * 8 + ((uint32_t)j ^ (tl & 7u))];
+    if (g + 4 > P.vocab) {
+        q.x = g < P.vocab ? q.x : NEG_INF;
+        q.y = g + 1 < P.vocab ? q.y : NEG_INF;
+        q.z = g + 2 < P.vocab ? q.z : NEG_INF;
+        q.w = g + 3 < P.vocab ? q.w : NEG_INF;
+    }
+    return q;
+}
+
+// ---------------------------------------------------------------------------
 // K1: tile statistics of one segment per CTA (the HBM pass).  Per tile: the
 // maximum and the sum of 2^((v - tile max) log2e / T); per segment: the
 // maximum, the sum relative to it, a non-finite flag and, for top-p without a
@@ -643,13 +763,17 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const float *x = P.logits + (size_t)row * P.ld;
     const float c2 = P.c2;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
+    const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
+    __shared__ __align__(8) uint64_t bar;
     __shared__ uint32_t swin[256];
     __shared__ uint32_t mh[KH_BINS];   // tail element counts per bin
-    __shared__ float stm[SEG_TILES];   // tile maxima of this segment
-    __shared__ float sts[SEG_TILES];   // tile sums relative to the tile maxima
     __shared__ float wm[NW];
     __shared__ uint32_t wf[NW];
     __shared__ double wd[NW];
+    const uint64_t pol = l2_policy_evict_last();
+    const bool pen = penalty_active(P);
+    const bool bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen ? 1u : 0u, sbuf, &bar, pol);
     const uint32_t nwin = load_window(P, row, swin);
     const bool k_floor = P.top_k > 0 && P.top_k < P.vocab && P.top_k <= KSEL_MAX;
     const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
@@ -657,57 +781,32 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
     if (p_floor)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) mh[b] = 0u;
-    if (nwin || p_floor) __syncthreads();
+    __syncthreads();   // the barrier's initialisation, the window, mh
+    const bool staged = bulk && seg_wait(P, &bar);
 
-    const uint64_t pol = l2_policy_evict_last();
-    const uint32_t sub = lane >> 3, l8 = lane & 7;
-    float smax = NEG_INF;
+    const bool live = (uint32_t)tid < ntile;
+    float v[TILE];
+    load_tile32(P, x, seg, live ? tid : 0u, sbuf, staged, swin, nwin, pol, v);
+    float tm = NEG_INF;
+#pragma unroll
+    for (int k = 0; k < TILE; k++) tm = fmaxf(tm, v[k]);
+    float s = 0.0f;
+    if (live && tm > NEG_INF) {
+        const float tc = tm * c2;
+#pragma unroll
+        for (int k = 0; k < TILE; k++) s += ex2_approx(fmaf(v[k], c2, -tc));
+    }
     uint32_t nonfin = 0;
-    constexpr int ITERS = SEG_TILES / (4 * NW);   // 8
-    // whole segment in range, 16-byte aligned and without penalised ids:
-    // plain vector loads
-    const bool fast = nwin == 0 && (seg + 1) * SEG_ELEMS <= P.vocab &&
-                      (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
-    const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
-    // all eight quads of the thread are requested before any is used: the
-    // pass streams from HBM and needs many loads in flight per SM
-    float4 qv[ITERS];
-    if (fast) {
-#pragma unroll
-        for (int it = 0; it < ITERS; it++) qv[it] = ldg_policy(xs4 + 32 * (warp + NW * it), pol);
+    if (live) {
+        // a non-finite logit may make the sum NaN: +inf shows in the tile
+        // maximum, a NaN (and -inf with T = +inf) in the tile sum
+        nonfin = (!(fabsf(tm) <= 3.4028235e38f) || s != s) ? 1u : 0u;
+        if (s != s) s = 0.0f;
+        P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid] = TileStat{tm, s};
     } else {
-#pragma unroll
-        for (int it = 0; it < ITERS; it++) {
-            const uint32_t tl = 4 * (warp + NW * it) + sub;
-            qv[it] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
-            if (tl < ntile) qv[it] = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
-        }
+        tm = NEG_INF;
     }
-#pragma unroll
-    for (int it = 0; it < ITERS; it++) {
-        const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
-        const uint32_t t = seg * SEG_TILES + tl;
-        const float4 q = qv[it];
-        const float tm = group8_max(fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
-        float s = 0.0f;
-        if (tm > NEG_INF) {
-            const float tc = tm * c2;
-            s = ex2_approx(fmaf(q.x, c2, -tc)) + ex2_approx(fmaf(q.y, c2, -tc)) +
-                ex2_approx(fmaf(q.z, c2, -tc)) + ex2_approx(fmaf(q.w, c2, -tc));
-        }
-        s = group8_sum(s);
-        if (l8 == 0 && tl < ntile) {
-            // a non-finite logit may make the sum NaN: +inf shows in the tile
-            // maximum, a NaN (and -inf with T = +inf) in the tile sum
-            nonfin |= (!(fabsf(tm) <= 3.4028235e38f) || s != s) ? 1u : 0u;
-            if (s != s) s = 0.0f;
-            stm[tl] = tm;
-            sts[tl] = s;
-            P.tstat[(size_t)hrow * P.ntiles_total + t] = TileStat{tm, s};
-        }
-        smax = fmaxf(smax, tm);
-    }
-    smax = warp_max(smax);
+    float smax = warp_max(tm);
     nonfin = __any_sync(0xffffffffu, nonfin != 0) ? 1u : 0u;
     if (lane == 0) {
         wm[warp] = smax;
@@ -723,24 +822,15 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     }
     // segment sum relative to the segment maximum
     double ss = 0.0;
-    if ((uint32_t)tid < ntile) {
-        const float tm = stm[tid];
-        if (tm > NEG_INF) ss = (double)sts[tid] * (double)ex2_approx((tm - sm) * c2);
-    }
+    if (live && tm > NEG_INF) ss = (double)s * (double)ex2_approx((tm - sm) * c2);
     // top-p without a top-k floor: tail-element histogram relative to the
-    // segment maximum (second read of the segment, from L2)
-    if (p_floor && sm > NEG_INF) {
+    // segment maximum
+    if (p_floor && sm > NEG_INF && live) {
         const float sc = sm * c2;
-        for (int it = 0; it < ITERS; it++) {
-            const uint32_t tl = 4 * (warp + NW * it) + sub;
-            if (tl >= ntile) continue;
-            const float4 q = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
-            const float a[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float xr = fmaf(a[k], c2, -sc);   // log2(p / p(segment max))
-                if (xr > -64.0f) atomicAdd(&mh[min(KH_BINS - 1, (int)(-xr * 4.0f))], 1u);
-            }
+        for (int k = 0; k < TILE; k++) {
+            const float xr = fmaf(v[k], c2, -sc);   // log2(p / p(segment max))
+            if (xr > -64.0f) atomicAdd(&mh[min(KH_BINS - 1, (int)(-xr * 4.0f))], 1u);
         }
     }
     ss = warp_sum_d(ss);
@@ -961,12 +1051,18 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     __shared__ uint32_t wtmp_u[NW + 1];
     __shared__ SegComp wtmp_s[2 * NW + 2];
     __shared__ TileRec rec[SEG_TILES];
-    __shared__ TileParam tpar[SEG_TILES];
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
+    __shared__ __align__(8) uint64_t bar;
     __shared__ uint32_t uarr[SEG_TILES], uarr2[SEG_TILES];
     __shared__ __align__(16) Comp carr[SEG_TILES];    // also read as uint64_t by the fast item path
     __shared__ __align__(16) Comp carr2[SEG_TILES];
     __shared__ uint32_t wlist[SEG_TILES];
     __shared__ uint32_t nlist, nanflag;
+    // the segment's bulk copy overlaps the prologue; it is read once more
+    // only by the exact pass, so it need not stay in L2
+    const uint64_t pol = l2_policy_evict_first();
+    const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
+    const bool bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, penalty_active(P) ? 1u : 0u, sbuf, &bar, pol);
     const uint32_t nwin = load_window(P, row, swin);
     if (tid == 0) {
         nlist = 0;
@@ -975,8 +1071,9 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
 
     // raw prefix estimate at every tile start of the segment, and from it
     // each tile's candidate binades of the running sum and its main-loop
-    // parameters
+    // parameters (thread t owns tile t)
     const float xf2 = ri.xf2;
+    TileParam tp;
     {
         double ct = 0.0;
         float tmax = NEG_INF;
@@ -1004,134 +1101,131 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const float dm = __fsub_rn(tmax, M);
         const float xm = (dm == 0.0f) ? 0.0f : dm * c2;
         const bool cand = tmax > NEG_INF && xm >= xf2;
-        TileParam tp;
         tp.K = K;
         const float e = fmaxf(cert_eps(K), 0x1p-17f);
         tp.fhi = 1.0f + e;
         tp.flo = 1.0f - e;
         tp.info = (special ? TP_SPECIAL : 0u) | (cand ? TP_CAND : 0u) | (cls << 2) | ((uint32_t)(lo + 128) << 8);
-        tpar[tid] = tp;
     }
-    __syncthreads();
 
-    const uint64_t pol = l2_policy_evict_first();
-    const uint32_t sub = lane >> 3, l8 = lane & 7;
     const bool t_nan = T != T, t_inf = isinf(T);
     const bool check_nan = ri.check_nan != 0;
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
-    constexpr int ITERS = SEG_TILES / (4 * NW);   // 8
-    const bool fast = nwin == 0 && (seg + 1) * SEG_ELEMS <= P.vocab &&
-                      (reinterpret_cast<uintptr_t>(x + seg * SEG_ELEMS) & 15u) == 0;
-    const float4 *xs4 = reinterpret_cast<const float4 *>(x + seg * SEG_ELEMS) + 8 * sub + l8;
-    uint32_t nanl = 0;
-    // the quads of each half of the segment are all requested before any is
-    // used (loads in flight), at a register count that keeps 5 CTAs per SM
-    constexpr int HALF = ITERS / 2;
-#pragma unroll 1
-    for (int hb = 0; hb < 2; hb++) {
-    float4 qv[HALF];
-    if (fast) {
+    const bool staged = bulk && seg_wait(P, &bar);
+    const uint32_t tt = live ? (uint32_t)tid : 0u;
+    auto quad = [&](int j) { return tile_quad(P, x, seg, tt, j, sbuf, staged, swin, nwin, pol); };
+    const uint32_t g0 = seg * SEG_ELEMS + (uint32_t)tid * TILE;
+    // certified grid counts of binade lo: y = p / u_lo from the fast exp;
+    // y (1 - e) and y (1 + e) bracket the exact value, and the count is the
+    // common rounding of both (a tie, or a value too close to one, makes them
+    // differ).  The clamp makes large values differ too.  The permuted order
+    // of v does not matter: without ties the counts simply add.
+    uint32_t acc = 0u, diff = 0u;
 #pragma unroll
-        for (int i2 = 0; i2 < HALF; i2++) qv[i2] = ldg_policy(xs4 + 32 * (warp + NW * (hb * HALF + i2)), pol);
-    } else {
+    for (int j = 0; j < 8; j++) {
+        const float4 q = quad(j);
+        const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int i2 = 0; i2 < HALF; i2++) {
-            const uint32_t tl = 4 * (warp + NW * (hb * HALF + i2)) + sub;
-            qv[i2] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
-            if (tl < ntile) qv[i2] = load_quad(P, x, (seg * SEG_TILES + tl) * TILE + 4 * l8, pol, swin, nwin);
-        }
-    }
-#pragma unroll
-    for (int i2 = 0; i2 < HALF; i2++) {
-        const int it = hb * HALF + i2;
-        const uint32_t tl = 4 * (warp + NW * it) + sub;   // tile within the segment
-        const uint32_t t = seg * SEG_TILES + tl;
-        const bool tlive = tl < ntile;
-        const uint32_t g0 = t * TILE + 4 * l8;
-        const float4 q = qv[i2];
-        const float a[4] = {q.x, q.y, q.z, q.w};
-        const TileParam tp = tpar[tl < SEG_TILES ? tl : 0];
-        // certified grid counts of binade lo: y = p / u_lo from the fast
-        // exp; y (1 - e) and y (1 + e) bracket the exact value, and the count
-        // is the common rounding of both (a tie or a value too close to one
-        // makes them differ).  The clamp makes large values differ too.
-        float d[4], y[4];
-        uint32_t acc = 0u, diff = 0u;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            d[k] = __fsub_rn(a[k], M);
-            y[k] = ex2_approx(fminf(fmaf(d[k], c2, tp.K), 17.5f));
-            const uint32_t r1 = __float_as_uint(fmaf(y[k], tp.fhi, 12582912.0f));
-            const uint32_t r2 = __float_as_uint(fmaf(y[k], tp.flo, 12582912.0f));
+        for (int c = 0; c < 4; c++) {
+            const float d = __fsub_rn(a4[c], M);
+            const float y = ex2_approx(fminf(fmaf(d, c2, tp.K), 17.5f));
+            const uint32_t r1 = __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
+            const uint32_t r2 = __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
             diff |= r1 ^ r2;
             acc += r1;
         }
-        // WINDOW tiles: the same for binade lo + 1 (y / 2)
-        const bool win = tlive && ((tp.info >> 2) & 3u) == CLS_WINDOW;
-        uint32_t acch = 0u;
-        if (__any_sync(0xffffffffu, win)) {
-            const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
+    }
+    acc -= (uint32_t)TILE * 0x4B400000u;   // a tile sums to < 2^22.5
+    // WINDOW tiles: the same for binade lo + 1 (y / 2)
+    const uint32_t cls_t = (tp.info >> 2) & 3u;
+    const bool win = live && cls_t == CLS_WINDOW;
+    uint32_t acch = 0u;
+    if (win) {
+        const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
+#pragma unroll 2
+        for (int j = 0; j < 8; j++) {
+            const float4 q = quad(j);
+            const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const uint32_t r3 = __float_as_uint(fmaf(y[k], hh, 12582912.0f));
-                const uint32_t r4 = __float_as_uint(fmaf(y[k], hl, 12582912.0f));
-                diff |= win ? (r3 ^ r4) : 0u;
+            for (int c = 0; c < 4; c++) {
+                const float d = __fsub_rn(a4[c], M);
+                const float y = ex2_approx(fminf(fmaf(d, c2, tp.K), 17.5f));
+                const uint32_t r3 = __float_as_uint(fmaf(y, hh, 12582912.0f));
+                const uint32_t r4 = __float_as_uint(fmaf(y, hl, 12582912.0f));
+                diff |= r3 ^ r4;
                 acch += r3;
             }
-            acch = group8_sum_u(acch - 4u * 0x4B400000u);
         }
-        // counts in bits 0-23 (a tile sums to < 2^22.5), uncertified lanes
-        // counted from bit 24
-        acc = acc - 4u * 0x4B400000u + (diff ? (1u << 24) : 0u);
-        acc = group8_sum_u(acc);
-        if (check_nan) {
+        acch -= (uint32_t)TILE * 0x4B400000u;
+    }
+    uint32_t nanl = 0;
+    if (check_nan && live) {
+#pragma unroll 1
+        for (int j = 0; j < 8; j++) {
+            const float4 q = quad(j);
+            const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-                nanl |= (g0 + k < P.vocab && ((d[k] != d[k]) || t_nan || (isinf(d[k]) && t_inf))) ? 1u : 0u;
-        }
-        if (l8 == 0 && tlive) {
-            const bool special = (tp.info & TP_SPECIAL) || (acc >> 24) != 0u;
-            const uint32_t qs = acc & 0xFFFFFFu;
-            TileRec rr;
-            rr.lo = (int32_t)(tp.info >> 8) - 128;
-            rr.cls = (tp.info >> 2) & 3u;
-            rr.aux = 0xFFFFFFFFu;
-            rr.qlo = Comp{qs, qs};
-            rr.qhi = win ? Comp{acch, acch} : Comp{0u, 0u};
-            rec[tl] = rr;
-            if (special) wlist[atomicAdd(&nlist, 1u)] = tl;
-        }
-        // candidates (index, logit): warp-aggregated reservation
-        if (__any_sync(0xffffffffu, tlive && (tp.info & TP_CAND))) {
-            uint32_t nc = 0;
-            float x2v[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                x2v[k] = (d[k] == 0.0f) ? 0.0f : d[k] * c2;
-                nc += (tlive && (tp.info & TP_CAND) && x2v[k] >= xf2) ? 1u : 0u;
+            for (int c = 0; c < 4; c++) {
+                const float d = __fsub_rn(a4[c], M);
+                nanl |= (g0 + tile_elem(tid, j, c) < P.vocab && ((d != d) || t_nan || (isinf(d) && t_inf))) ? 1u
+                                                                                                          : 0u;
             }
-            uint32_t incl = nc;
+        }
+    }
+    const bool special = live && ((tp.info & TP_SPECIAL) || diff != 0u);
+    if (live) {
+        TileRec rr;
+        rr.lo = (int32_t)(tp.info >> 8) - 128;
+        rr.cls = cls_t;
+        rr.aux = 0xFFFFFFFFu;
+        rr.qlo = Comp{acc, acc};
+        rr.qhi = win ? Comp{acch, acch} : Comp{0u, 0u};
+        rec[tid] = rr;
+    }
+    {   // special tiles to the exact pass: one reservation per warp
+        const uint32_t m = __ballot_sync(0xffffffffu, special);
+        uint32_t base = 0;
+        if (lane == 0 && m) base = atomicAdd(&nlist, (uint32_t)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (special) wlist[base + __popc(m & ((1u << lane) - 1u))] = tid;
+    }
+    // candidates (index, logit): warp-aggregated reservation
+    const bool tc = live && (tp.info & TP_CAND);
+    if (__any_sync(0xffffffffu, tc)) {
+        uint32_t nc = 0;
+        if (tc) {
+#pragma unroll 1
+            for (int j = 0; j < 8; j++) {
+                const float4 q = quad(j);
+                const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += u;
+                for (int c = 0; c < 4; c++) {
+                    const float d = __fsub_rn(a4[c], M);
+                    nc += ((d == 0.0f ? 0.0f : d * c2) >= xf2) ? 1u : 0u;
+                }
             }
-            const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
-            uint32_t cb = 0;
-            if (lane == 31 && wtot) cb = atomicAdd(&hdr->n_cand, wtot);
-            cb = __shfl_sync(0xffffffffu, cb, 31);
-            uint32_t pos = cb + incl - nc;
-            if (nc) {
+        }
+        const uint32_t incl = warp_incl_scan_u(nc);
+        const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t cb = 0;
+        if (lane == 31 && wtot) cb = atomicAdd(&hdr->n_cand, wtot);
+        cb = __shfl_sync(0xffffffffu, cb, 31);
+        uint32_t pos = cb + incl - nc;
+        if (nc) {
+#pragma unroll 1
+            for (int j = 0; j < 8; j++) {
+                const float4 q = quad(j);
+                const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    if (x2v[k] >= xf2) {
-                        if (pos < P.cand_stride) cand[pos] = Candidate{g0 + k, a[k]};
+                for (int c = 0; c < 4; c++) {
+                    const float d = __fsub_rn(a4[c], M);
+                    if ((d == 0.0f ? 0.0f : d * c2) >= xf2) {
+                        if (pos < P.cand_stride) cand[pos] = Candidate{g0 + tile_elem(tid, j, c), a4[c]};
                         pos++;
                     }
                 }
             }
         }
-    }
     }
     if (__any_sync(0xffffffffu, nanl != 0) && lane == 0) atomicOr(&nanflag, 1u);
     __syncthreads();
@@ -1147,7 +1241,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         TileRec r = rec[lt];
         const uint32_t g = tt * TILE + lane;
         float a = NEG_INF;
-        if (g < P.vocab) a = x[g];
+        if (g < P.vocab) a = staged ? reinterpret_cast<const float *>(sbuf)[lt * TILE + lane] : x[g];
         // the penalty, as in load_tile
         for (uint32_t j = 0; j < nwin; j++) {
             if (swin[j] == g) {
