@@ -1279,110 +1279,129 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const bool ties = __syncthreads_or(live && (rec[tid].qlo.q0 != rec[tid].qlo.q1 ||
                                                 rec[tid].qhi.q0 != rec[tid].qhi.q1)) != 0;
     if (!ties) {
-        if (warp == 0) {
-            uint32_t nitems = 0;
-            uint64_t carry_a = 0, carry_b = 0;
-            uint32_t carry_start = 0;
-            uint32_t *sid = uarr;                                   // item of each WINDOW tile
-            uint64_t *sb = reinterpret_cast<uint64_t *>(carr);      // hi prefix of each WINDOW tile
-            uint64_t *itb = reinterpret_cast<uint64_t *>(carr2);    // hi total of each item
-            for (uint32_t c0 = 0; c0 < NT; c0 += 32) {
-                const uint32_t j = c0 + lane;
-                const bool valid = j < NT;
-                TileRec r;
-                r.lo = 0;
-                r.cls = CLS_SIMPLE;
-                r.aux = 0u;
-                r.qlo = Comp{0u, 0u};
-                r.qhi = Comp{0u, 0u};
-                if (valid) r = rec[j];
-                bool h = valid, e = valid;
-                if (valid && j > 0) {
-                    const TileRec q = rec[j - 1];
-                    h = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
-                }
-                if (valid && j + 1 < NT) {
-                    const TileRec q = rec[j + 1];
-                    e = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
-                }
-                const uint32_t heads = __ballot_sync(0xffffffffu, h);
-                const uint64_t a = r.qlo.q0, b = r.qhi.q0;
-                uint64_t Pa = a, Pb = b;
+        // each warp builds the items of its chunk of 32 tiles; a stretch that
+        // runs into a chunk from before is carried from the chunk summaries
+        __shared__ uint64_t ch_a[NW], ch_b[NW];   // counts from the chunk's last head (or start) to its end
+        __shared__ uint32_t ch_heads[NW], ch_start[NW];
+        uint32_t *sid = uarr;                                   // item of each WINDOW tile
+        uint64_t *sb = reinterpret_cast<uint64_t *>(carr);      // hi prefix of each WINDOW tile
+        uint64_t *itb = reinterpret_cast<uint64_t *>(carr2);    // hi total of each item
+        const uint32_t c0 = (uint32_t)warp * 32u;
+        const uint32_t j = c0 + lane;
+        const bool valid = j < NT;
+        TileRec r;
+        r.lo = 0;
+        r.cls = CLS_SIMPLE;
+        r.aux = 0u;
+        r.qlo = Comp{0u, 0u};
+        r.qhi = Comp{0u, 0u};
+        if (valid) r = rec[j];
+        bool h = valid, e = valid;
+        if (valid && j > 0) {
+            const TileRec q = rec[j - 1];
+            h = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
+        }
+        if (valid && j + 1 < NT) {
+            const TileRec q = rec[j + 1];
+            e = r.cls == CLS_COMPLEX || q.cls != r.cls || q.lo != r.lo;
+        }
+        const uint32_t heads = __ballot_sync(0xffffffffu, h);
+        const uint64_t a = r.qlo.q0, b = r.qhi.q0;
+        uint64_t Pa = a, Pb = b;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const uint64_t ua = __shfl_up_sync(0xffffffffu, Pa, o);
-                    const uint64_t ub = __shfl_up_sync(0xffffffffu, Pb, o);
-                    if (lane >= o) {
-                        Pa += ua;
-                        Pb += ub;
-                    }
-                }
-                const uint32_t upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
-                const uint32_t m = heads & upto;
-                const int sl = m ? 31 - __clz(m) : 0;
-                const uint64_t pa0 = __shfl_sync(0xffffffffu, Pa, sl > 0 ? sl - 1 : 0);
-                const uint64_t pb0 = __shfl_sync(0xffffffffu, Pb, sl > 0 ? sl - 1 : 0);
-                uint64_t seg_a, seg_b;
-                uint32_t start, id;
-                if (m) {
-                    seg_a = Pa - (sl > 0 ? pa0 : 0);
-                    seg_b = Pb - (sl > 0 ? pb0 : 0);
-                    start = c0 + (uint32_t)sl;
-                    id = nitems + __popc(m) - 1u;
-                } else {   // continues the stretch open at the chunk start
-                    seg_a = carry_a + Pa;
-                    seg_b = carry_b + Pb;
-                    start = carry_start;
-                    id = nitems - 1u;
-                }
-                if (valid && r.cls == CLS_WINDOW) {
-                    const uint32_t pa = (uint32_t)min(seg_a, (uint64_t)QSAT);
-                    wpre[j] = WTile{Comp{pa, pa}, Comp{0u, 0u}, r.aux, 0u};
-                    sid[j] = id;
-                    sb[j] = seg_b - b;   // exclusive hi prefix
-                }
-                if (valid && e) {
-                    Item it;
-                    it.kind = r.cls;
-                    it.lo = r.lo;
-                    it.tile = tile0 + start;
-                    const uint32_t qa = (uint32_t)min(seg_a, (uint64_t)QSAT);
-                    const uint32_t qb = (uint32_t)min(seg_b, (uint64_t)QSAT);
-                    if (r.cls == CLS_COMPLEX) {
-                        it.q[0] = r.qlo.q0;
-                        it.q[1] = r.qlo.q1;
-                        it.q[2] = 0u;
-                        it.q[3] = 0u;
-                        it.aux = r.aux;
-                    } else {
-                        it.q[0] = qa;
-                        it.q[1] = qa;
-                        it.q[2] = r.cls == CLS_WINDOW ? qb : 0u;
-                        it.q[3] = r.cls == CLS_WINDOW ? qb : 0u;
-                        it.aux = j - start + 1u;
-                    }
-                    items[id] = it;
-                    itb[id] = seg_b;
-                }
-                carry_a = __shfl_sync(0xffffffffu, seg_a, 31);
-                carry_b = __shfl_sync(0xffffffffu, seg_b, 31);
-                carry_start = __shfl_sync(0xffffffffu, start, 31);
-                nitems += __popc(heads);
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t ua = __shfl_up_sync(0xffffffffu, Pa, o);
+            const uint64_t ub = __shfl_up_sync(0xffffffffu, Pb, o);
+            if (lane >= o) {
+                Pa += ua;
+                Pb += ub;
             }
-            __syncwarp();
-            // suffix counts (binade lo+1) of the WINDOW tiles
-            for (uint32_t j = lane; j < NT; j += 32) {
-                const TileRec r = rec[j];
-                if (r.cls == CLS_WINDOW) {
-                    const uint64_t suf = itb[sid[j]] - sb[j];
-                    const uint32_t qs = (uint32_t)min(suf, (uint64_t)QSAT);
-                    wpre[j].suf_hi = Comp{qs, qs};
-                }
+        }
+        const uint32_t upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+        const uint32_t m = heads & upto;
+        const int sl = m ? 31 - __clz(m) : 0;
+        const uint64_t pa0 = __shfl_sync(0xffffffffu, Pa, sl > 0 ? sl - 1 : 0);
+        const uint64_t pb0 = __shfl_sync(0xffffffffu, Pb, sl > 0 ? sl - 1 : 0);
+        const uint64_t loc_a = m ? Pa - (sl > 0 ? pa0 : 0) : Pa;
+        const uint64_t loc_b = m ? Pb - (sl > 0 ? pb0 : 0) : Pb;
+        if (lane == 31) {
+            ch_a[warp] = loc_a;
+            ch_b[warp] = loc_b;
+            ch_heads[warp] = __popc(heads);
+            ch_start[warp] = heads ? c0 + (31u - __clz(heads)) : 0xFFFFFFFFu;
+        }
+        __syncthreads();
+        // the stretch open at this chunk's start: back to the nearest chunk
+        // with a head (chunk 0 always starts with one)
+        uint32_t nbefore = 0;
+        for (int w2 = 0; w2 < warp; w2++) nbefore += ch_heads[w2];
+        uint64_t carry_a = 0, carry_b = 0;
+        uint32_t carry_start = 0;
+        for (int w2 = warp - 1; w2 >= 0; w2--) {
+            carry_a += ch_a[w2];
+            carry_b += ch_b[w2];
+            if (ch_heads[w2]) {
+                carry_start = ch_start[w2];
+                break;
             }
-            if (lane == 0) {
-                hdr->seg_items[seg] = nitems;
-                hdr->seg_tile0[seg] = tile0;
+        }
+        uint64_t seg_a, seg_b;
+        uint32_t start, id;
+        if (m) {
+            seg_a = loc_a;
+            seg_b = loc_b;
+            start = c0 + (uint32_t)sl;
+            id = nbefore + __popc(m) - 1u;
+        } else {   // continues the stretch open at the chunk start
+            seg_a = carry_a + Pa;
+            seg_b = carry_b + Pb;
+            start = carry_start;
+            id = nbefore - 1u;
+        }
+        if (valid && r.cls == CLS_WINDOW) {
+            const uint32_t pa = (uint32_t)min(seg_a, (uint64_t)QSAT);
+            wpre[j] = WTile{Comp{pa, pa}, Comp{0u, 0u}, r.aux, 0u};
+            sid[j] = id;
+            sb[j] = seg_b - b;   // exclusive hi prefix
+        }
+        if (valid && e) {
+            Item it;
+            it.kind = r.cls;
+            it.lo = r.lo;
+            it.tile = tile0 + start;
+            const uint32_t qa = (uint32_t)min(seg_a, (uint64_t)QSAT);
+            const uint32_t qb = (uint32_t)min(seg_b, (uint64_t)QSAT);
+            if (r.cls == CLS_COMPLEX) {
+                it.q[0] = r.qlo.q0;
+                it.q[1] = r.qlo.q1;
+                it.q[2] = 0u;
+                it.q[3] = 0u;
+                it.aux = r.aux;
+            } else {
+                it.q[0] = qa;
+                it.q[1] = qa;
+                it.q[2] = r.cls == CLS_WINDOW ? qb : 0u;
+                it.q[3] = r.cls == CLS_WINDOW ? qb : 0u;
+                it.aux = j - start + 1u;
             }
+            items[id] = it;
+            itb[id] = seg_b;
+        }
+        __syncthreads();
+        // suffix counts (binade lo+1) of the WINDOW tiles
+        if (live) {
+            const TileRec rr = rec[tid];
+            if (rr.cls == CLS_WINDOW) {
+                const uint64_t suf = itb[sid[tid]] - sb[tid];
+                const uint32_t qs = (uint32_t)min(suf, (uint64_t)QSAT);
+                wpre[tid].suf_hi = Comp{qs, qs};
+            }
+        }
+        if (tid == 0) {
+            uint32_t nitems = 0;
+            for (int w2 = 0; w2 < NW; w2++) nitems += ch_heads[w2];
+            hdr->seg_items[seg] = nitems;
+            hdr->seg_tile0[seg] = tile0;
         }
         return;
     }
