@@ -1053,9 +1053,12 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     __shared__ TileRec rec[SEG_TILES];
     __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ __align__(8) uint64_t bar;
-    __shared__ uint32_t uarr[SEG_TILES], uarr2[SEG_TILES];
-    __shared__ __align__(16) Comp carr[SEG_TILES];    // also read as uint64_t by the fast item path
-    __shared__ __align__(16) Comp carr2[SEG_TILES];
+    // the item phase's arrays reuse the segment copy, which is dead by then
+    // (6 KB less shared memory per CTA: five CTAs fit an SM instead of four)
+    uint32_t *const uarr = reinterpret_cast<uint32_t *>(sbuf);
+    uint32_t *const uarr2 = uarr + SEG_TILES;
+    Comp *const carr = reinterpret_cast<Comp *>(uarr2 + SEG_TILES);   // 8-byte aligned: read as uint64_t too
+    Comp *const carr2 = carr + SEG_TILES;
     __shared__ uint32_t wlist[SEG_TILES];
     __shared__ uint32_t nlist, nanflag;
     // the segment's bulk copy overlaps the prologue; it is read once more
