@@ -169,15 +169,21 @@ __device__ __forceinline__ uint32_t warp_incl_scan_u(uint32_t v) {
     return v;
 }
 
-// s = fl(...fl(fl(s + p_0) + p_1)... + p_31) over the warp's lanes in lane
-// order.  Every lane gathers the 32 values (shuffles issue back to back) and
-// runs the same 32 dependent adds from registers, so no broadcast is needed.
-__device__ __forceinline__ float warp_seq_add32(float s, float p) {
-    float v[32];
+// s = fl(...fl(fl(s + p[0]) + p[1])... + p[31]) for 32 values in shared
+// memory (16-byte aligned).  Every lane reads them with eight broadcast
+// float4 loads and runs the same 32 dependent adds from registers.
+__device__ __forceinline__ float seq_add32_smem(float s, const float *p) {
+    const float4 *p4 = reinterpret_cast<const float4 *>(p);
+    float4 q[8];
 #pragma unroll
-    for (int k = 0; k < 32; k++) v[k] = __shfl_sync(0xffffffffu, p, k);
+    for (int k = 0; k < 8; k++) q[k] = p4[k];
 #pragma unroll
-    for (int k = 0; k < 32; k++) s = __fadd_rn(s, v[k]);
+    for (int k = 0; k < 8; k++) {
+        s = __fadd_rn(s, q[k].x);
+        s = __fadd_rn(s, q[k].y);
+        s = __fadd_rn(s, q[k].z);
+        s = __fadd_rn(s, q[k].w);
+    }
     return s;
 }
 
@@ -1591,6 +1597,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __shared__ uint32_t woff[ITEM_SMEM];         // WINDOW item: its prefix table in wpool, or ~0u
     __shared__ WTile wpool[WPOOL];
     __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1];
+    __shared__ __align__(16) float tilep[TILE];   // a recomputed tile's p, for the walker
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
     __shared__ uint32_t walk_flags, walk_items, walk_slow, n_zero;
@@ -1720,7 +1727,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
         // add one tile element by element, p recomputed from the logits
         auto add_tile = [&](uint32_t tile) {
-            st = state_of(warp_seq_add32(float_of(st), exact_p_at(P, row, tile * TILE + lane, M, swin, nwin)));
+            tilep[lane] = exact_p_at(P, row, tile * TILE + lane, M, swin, nwin);
+            __syncwarp();
+            st = state_of(seq_add32_smem(float_of(st), tilep));
+            __syncwarp();
         };
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
             const uint32_t nit = s_nit[sgi];
@@ -1762,7 +1772,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                     if (action == 2 && it.kind == CLS_COMPLEX && it.aux < n_wc) action = 3;
                     if (action == 0) continue;
                     if (action == 3) {   // stored exact p
-                        st = state_of(warp_seq_add32(float_of(st), wcs[it.aux * TILE + lane]));
+                        st = state_of(seq_add32_smem(float_of(st), wcs + it.aux * TILE));
                         continue;
                     }
                     uint32_t from = 0;
@@ -1798,7 +1808,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                         }
                         const uint32_t sl = wp[c].slot;
                         if (sl < n_wc) {   // stored exact p
-                            st = state_of(warp_seq_add32(float_of(st), wcs[sl * TILE + lane]));
+                            st = state_of(seq_add32_smem(float_of(st), wcs + sl * TILE));
                         } else {
                             add_tile(it.tile + c);
                         }
