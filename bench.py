@@ -187,10 +187,11 @@ def main():
 
     B, V = w.rows, w.vocab
     # this rank's rows; seeds keyed by the global row
-    host = [pkg.workloads.make_logits(w, step=s, rows=B, row_offset=rank * B) for s in range(ROTATE)]
+    shard = pkg.sharding.shard_for(rank, world, B)
+    host = [pkg.workloads.make_logits(w, step=s, rows=B, row_offset=shard.row0) for s in range(ROTATE)]
     dev = [torch.from_numpy(h).cuda() for h in host]
     cfg = pkg.SamplerConfig(**w.config())
-    smp = pkg.Sampler(cfg, batch=B, vocab=V, device=local, seeds=w.seeds(B, offset=rank * B))
+    smp = pkg.Sampler(cfg, batch=B, vocab=V, device=local, seeds=shard.seeds(w.seed))
     out = torch.empty(B, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
 
@@ -215,11 +216,7 @@ def main():
         torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    ms = start.elapsed_time(end)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
     if smp.last_status() != 0:
         raise RuntimeError(f"sampler status {smp.last_status()}")
     launches_per_step = 1 if greedy else 3
@@ -238,15 +235,11 @@ def main():
     t0 = time.perf_counter()
     for i in range(args.e2e_steps):
         smp.sample(pin_np[i % 2])
-    e2e_s = time.perf_counter() - t0
-    e2e_rows = B * args.e2e_steps * world / e2e_s
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_rows = B * args.e2e_steps * world / float(t.item())
+    e2e_s = pkg.sharding.max_over_ranks(time.perf_counter() - t0, dist, device="cuda")
+    e2e_rows = pkg.sharding.aggregate_rows_per_s(shard, args.e2e_steps, e2e_s)
 
     if rank == 0:
-        rows_per_s = B * args.steps * world / (ms / 1e3)
+        rows_per_s = pkg.sharding.aggregate_rows_per_s(shard, args.steps, ms / 1e3)
         peak, peak_kind = peaks()
         alg_bytes = 4.0 * V * B
         roof = None

@@ -3,7 +3,8 @@
 The product is ``libb200_sampler.so`` (CUDA kernels for sm_100a behind the C
 ABI in include/b200_sampler.h).  This package holds its sources (csrc/), the
 build step (build.py), the Python mirror of the reference interface
-(sampler.py) and the benchmark workloads (workloads.py).
+(sampler.py), the batch sharding across ranks (sharding.py) and the benchmark
+workloads (workloads.py).
 
 The directory name contains a dot, so it is loaded by path, e.g.::
 
@@ -14,7 +15,7 @@ The directory name contains a dot, so it is loaded by path, e.g.::
     pkg = importlib.util.module_from_spec(spec); sys.modules["llama_zig_b200"] = pkg
     spec.loader.exec_module(pkg)
 """
-from . import build, workloads  # noqa: F401
+from . import build, sharding, workloads  # noqa: F401
 from .sampler import (  # noqa: F401
     EXPORTS, Sampler, SamplerConfig, SamplerError, lib, sample_argmax, status_string,
 )

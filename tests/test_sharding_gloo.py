@@ -1,0 +1,75 @@
+"""The N>1 batch-sharding host logic on CPU: two gloo ranks each sample their
+block of a batch with the checker, seeded by global row; the gathered tokens
+and RNG states must equal one process sampling the whole batch, and the
+timing reduction must return the slowest rank's value."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, rows_per_rank, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as graft
+    pkg = graft.load_package()
+    orc = graft.load_oracle()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = pkg.workloads.WORKLOADS["c1"]
+        sh = pkg.sharding.shard_for(rank, world, rows_per_rank)
+        x = pkg.workloads.make_logits(w, rows=rows_per_rank, row_offset=sh.row0, vocab=4096)
+        tok, _, st = orc.sample_batch(orc.make_config(**w.config()), x, seeds=sh.seeds(w.seed))
+        # gather every rank's block (test only: the data path has no collective)
+        t_all = [torch.zeros(rows_per_rank, dtype=torch.int64) for _ in range(world)]
+        s_all = [torch.zeros(rows_per_rank * 4, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(t_all, torch.from_numpy(tok.astype(np.int64)))
+        dist.all_gather(s_all, torch.from_numpy(st.reshape(-1).view(np.int64).copy()))
+        slowest = pkg.sharding.max_over_ranks(10.0 + rank, dist)
+        if rank == 0:
+            np.savez(os.path.join(out_dir, "shards.npz"),
+                     tokens=torch.cat(t_all).numpy(), states=torch.cat(s_all).numpy().view(np.uint64),
+                     slowest=np.float64(slowest))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_match_one_process(tmp_path, pkg, orc):
+    world, rpr = 2, 6
+    mp.start_processes(_rank_main, args=(world, _free_port(), rpr, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    got = np.load(tmp_path / "shards.npz")
+    w = pkg.workloads.WORKLOADS["c1"]
+    x = pkg.workloads.make_logits(w, rows=world * rpr, vocab=4096)
+    tok, _, st = orc.sample_batch(orc.make_config(**w.config()), x, seeds=w.seeds(world * rpr))
+    assert np.array_equal(got["tokens"], tok.astype(np.int64))
+    assert np.array_equal(got["states"].reshape(-1, 4), st)
+    assert float(got["slowest"]) == 11.0
+
+
+def test_shard_layout():
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as graft
+    sh = graft.load_package().sharding
+    blocks = [list(sh.shard_for(r, 4, 3).rows()) for r in range(4)]
+    assert sum(blocks, []) == list(range(12))
+    assert list(sh.shard_for(2, 4, 3).seeds(42)) == [48, 49, 50]
+    assert sh.aggregate_rows_per_s(sh.shard_for(0, 4, 3), steps=10, seconds=2.0) == 60.0
+    assert sh.max_over_ranks(3.5) == 3.5
+    with pytest.raises(ValueError):
+        sh.shard_for(4, 4, 3)
