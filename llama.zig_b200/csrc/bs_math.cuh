@@ -184,6 +184,15 @@ __device__ __forceinline__ float log_ref(float x) {
 __device__ __forceinline__ float prob_unnorm(float v, float m, float t) {
     return exp_ref(__fdiv_rn(__fsub_rn(v, m), t));
 }
+
+// The entropy term of sampler.zig:131-133 for logit v: with P = fl(p / S),
+// `entropy -= P * @log(P)` adds fl(P * -logf(P)) (negation is exact and the
+// rounding symmetric); 0 when P is not positive.
+__device__ __forceinline__ float entropy_term(float v, float m, float t, float S) {
+    const float P = __fdiv_rn(prob_unnorm(v, m, t), S);
+    if (!(P > 0.0f)) return 0.0f;
+    return __fmul_rn(P, -log_ref(P));
+}
 #endif  // __CUDACC__
 
 }  // namespace bs

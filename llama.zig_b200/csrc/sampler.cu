@@ -415,6 +415,18 @@ constexpr int RED_CHUNK = 4;                 // segments per step of the row red
 constexpr double WIN_LO = 4e-3;
 constexpr double WIN_HI = 3e-5;
 
+// Typical-p band (sampler.zig:128-154 with typical-p alone): the dev bound is
+// chosen on a 1/32-nat grid from the statistics pass's mass histograms,
+// assuming |H_raw - H| <= TB_H_REL |H| + TB_H_ABS; the walk checks that
+// assumption against the exact H and reports BS_ENOTSUP when it fails.
+constexpr int TB_CELLS = 1024;
+constexpr double TB_PER_NAT = 32.0;
+constexpr double TB_H_REL = 4e-3;
+constexpr double TB_H_ABS = 1e-3;
+constexpr float TB_MASS_REL = 0.01f;
+constexpr float TB_MASS_ABS = 0.005f;
+constexpr float TB_D_PAD = 0.01f;
+
 // Relative error bound, for the main loop's certificate, between
 // y = ex2.approx(min(fma(d, c2, K), 17.5)) and the exact p / u_lo, where
 // p = exp_ref(fdiv_rn(d, T)), d = fsub_rn(v, M), c2 = fl(log2(e) / T).
@@ -430,30 +442,67 @@ __host__ __device__ __forceinline__ float cert_eps(float K) {
     return 2.0f * ((K + 1.0f) * 8.27e-8f + 1.2e-7f + 7.3e-7f + 2.4e-7f);
 }
 
+// The same for the entropy term h = P (-ln P), P = p / S, approximated as
+// y = min(ex2.approx(min(z + K, 40)) * (-z ln2), 2^17.5) with
+// z = fma(d, c2, -log2 S) ~ log2 P.  zmin: the tile's smallest |z| (its
+// largest P; tiles with zmin < 1/16 go to the exact pass), l2s = |log2 S|.
+// Elements that can count (y >= 1/2) have |z| <= K + 8, so |x2| <= K + 8 + l2s.
+//   reference: P's error eP = (|x| + 3) 2^-24 (divide by T, expf, divide by
+//     S) also moves -logf(P) by eP / (zmin ln2) relative; logf's ulp 2^-23;
+//     the product's rounding 2^-24;
+//   approximation: z's error dz = (|x2| + 2 l2s + K + 8) 2^-24 (log2 units)
+//     moves 2^z by ln2 dz and -z by dz / zmin; the add's rounding 40 ln2
+//     2^-24; ex2.approx 2^-22; two multiplies and ln2 3 2^-24.
+// The bound is doubled; the caller floors it at 2^-17 like cert_eps.
+__host__ __device__ __forceinline__ float cert_eps_h(float K, float zmin, float l2s) {
+    const float u = 5.9604645e-8f;   // 2^-24
+    const float x2m = K + 8.0f + l2s;
+    const float eP = (x2m * 0.6931472f + 3.0f) * u;
+    const float dz = (x2m + 2.0f * l2s + K + 8.0f) * u;
+    const float inv = 1.0f / (zmin * 0.6931472f);
+    const float ref = eP * (1.0f + inv) + 2.0f * u + u;
+    const float apx = 0.6931472f * dz + dz / zmin + 40.0f * 0.6931472f * u + 4.0f * u + 3.0f * u;
+    return 2.0f * (ref + apx);
+}
+
 __device__ __forceinline__ double pow2d(int k) {   // 2^k, -1022 <= k <= 1023
     return __longlong_as_double((long long)(k + 1023) << 52);
 }
 
 struct TileStat {
     float tmax;   // tile maximum (penalised logits)
-    float tsr;    // sum of 2^((v - tmax) log2e / T) over the tile
+    float tsr;    // sum of 2^r over the tile, r = (v - tmax) log2e / T
+    float tsr2;   // sum of 2^r r (the entropy estimate's second moment)
+    float pad;
 };
 
 struct SegStat {
     float smax;        // segment maximum
     uint32_t nonfin;   // a non-finite logit in the segment
-    double ssum;       // sum of tile sums relative to smax
+    double ssum;       // sum of 2^x over the segment, x = (v - smax) log2e / T
     double base;       // (row reduction) raw prefix estimate at the segment start
-    double pad;
+    double ssum2;      // sum of 2^x x
 };
 
-struct RowInfo {   // written by K1's row reduction, read by K2 and K3
+struct RowInfo {   // written by the row reduction, read by the main and walk passes
     float M;
     float xf2;         // candidate floor, log2 p units
-    uint32_t binding;  // 0 none (all p > 0), 1 top-k, 2 top-p, 3 min-p
+    uint32_t binding;  // 0 none (all p > 0), 1 top-k, 2 top-p, 3 min-p, 4 typical top ties
     uint32_t check_nan;
     double S_raw;
+    double H_raw;      // typical-p: entropy estimate from the tile statistics
+    float dband;       // TYP_BAND: dev bound of the candidate band
+    uint32_t tmode;    // TYP_*
 };
+
+// Typical-p mode of the configuration (sampler.zig:128-154): off, over a
+// selected set bounded by another filter, or alone (band candidates).
+__host__ __device__ __forceinline__ uint32_t typical_mode(float typical_p, uint32_t top_k, uint32_t vocab,
+                                                          float top_p, float min_p) {
+    if (!(typical_p > 0.0f && typical_p < 1.0f)) return TYP_OFF;
+    const bool other = (top_k > 0 && top_k < vocab) || (top_p > 0.0f && top_p < 1.0f) || min_p > 0.0f;
+    return other ? TYP_SELECTED : TYP_BAND;
+}
 
 struct K12Params {
     const float *logits;
@@ -470,6 +519,8 @@ struct K12Params {
     float min_p;
     uint32_t rep_window;
     float rep_penalty;
+    float typical_p;
+    uint32_t tmode;           // TYP_*
     uint32_t nseg;
     uint32_t ntiles_total;
     TileStat *tstat;          // per handle row: ntiles_total
@@ -785,9 +836,13 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
     const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
     const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
+    const bool t_band = P.tmode == TYP_BAND;
+    __shared__ float th[KH_BINS];      // typical band: mass per bin
     if (p_floor)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) mh[b] = 0u;
-    __syncthreads();   // the barrier's initialisation, the window, mh
+    if (t_band)
+        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) th[b] = 0.0f;
+    __syncthreads();   // the barrier's initialisation, the window, mh, th
     const bool staged = bulk && seg_wait(P, &bar);
 
     const bool live = (uint32_t)tid < ntile;
@@ -796,11 +851,16 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     float tm = NEG_INF;
 #pragma unroll
     for (int k = 0; k < TILE; k++) tm = fmaxf(tm, v[k]);
-    float s = 0.0f;
+    float s = 0.0f, s2 = 0.0f;
     if (live && tm > NEG_INF) {
         const float tc = tm * c2;
 #pragma unroll
-        for (int k = 0; k < TILE; k++) s += ex2_approx(fmaf(v[k], c2, -tc));
+        for (int k = 0; k < TILE; k++) {
+            const float r = fmaf(v[k], c2, -tc);
+            const float e = ex2_approx(r);
+            s += e;
+            s2 = fmaf(e, fmaxf(r, -1e30f), s2);   // 2^r r (0 for -inf logits)
+        }
     }
     uint32_t nonfin = 0;
     if (live) {
@@ -808,7 +868,8 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         // maximum, a NaN (and -inf with T = +inf) in the tile sum
         nonfin = (!(fabsf(tm) <= 3.4028235e38f) || s != s) ? 1u : 0u;
         if (s != s) s = 0.0f;
-        P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid] = TileStat{tm, s};
+        if (s2 != s2) s2 = 0.0f;
+        P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid] = TileStat{tm, s, s2, 0.0f};
     } else {
         tm = NEG_INF;
     }
@@ -826,9 +887,23 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         sm = fmaxf(sm, wm[w]);
         nfs |= wf[w];
     }
-    // segment sum relative to the segment maximum
-    double ss = 0.0;
-    if (live && tm > NEG_INF) ss = (double)s * (double)ex2_approx((tm - sm) * c2);
+    // segment sums relative to the segment maximum
+    double ss = 0.0, ss2 = 0.0;
+    if (live && tm > NEG_INF) {
+        const float o = (tm - sm) * c2;
+        const double et = (double)ex2_approx(o);
+        ss = (double)s * et;
+        ss2 = et * ((double)s2 + (double)o * (double)s);
+    }
+    // typical-p alone: mass per quarter-octave below the segment maximum
+    if (t_band && sm > NEG_INF && live) {
+        const float sc = sm * c2;
+#pragma unroll
+        for (int k = 0; k < TILE; k++) {
+            const float xr = fmaf(v[k], c2, -sc);
+            if (xr > -64.0f) atomicAdd(&th[min(KH_BINS - 1, (int)(-xr * 4.0f))], ex2_approx(xr));
+        }
+    }
     // top-p without a top-k floor: tail-element histogram relative to the
     // segment maximum
     if (p_floor && sm > NEG_INF && live) {
@@ -840,22 +915,32 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         }
     }
     ss = warp_sum_d(ss);
-    if (lane == 0) wd[warp] = ss;
+    ss2 = warp_sum_d(ss2);
+    __shared__ double wd2[NW];
+    if (lane == 0) {
+        wd[warp] = ss;
+        wd2[warp] = ss2;
+    }
     __syncthreads();
     if (tid == 0) {
-        double sacc = 0.0;
-        for (int w = 0; w < NW; w++) sacc += wd[w];
+        double sacc = 0.0, sacc2 = 0.0;
+        for (int w = 0; w < NW; w++) {
+            sacc += wd[w];
+            sacc2 += wd2[w];
+        }
         SegStat st;
         st.smax = sm;
         st.nonfin = nfs;
         st.ssum = sacc;
         st.base = 0.0;
-        st.pad = 0.0;
+        st.ssum2 = sacc2;
         P.sstat[(size_t)hrow * MAX_SEG + seg] = st;
     }
     if (p_floor)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS)   // mass bound: count x the bin's upper edge
             P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = (float)mh[b] * exp2f(-0.25f * (float)b);
+    if (t_band)
+        for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = th[b];
 }
 
 // Row reduction, one CTA per row: the row maximum M, the raw prefix estimate
@@ -915,14 +1000,72 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
             if (c < ns) P.sstat[(size_t)hrow * MAX_SEG + c].base = run + incl - sv;
             run += __shfl_sync(0xffffffffu, incl, 31);
         }
+        // entropy estimate: H = ln S - ln2 sum(e x) / S, e = 2^x, x = (v - M) log2e / T
+        double e2 = 0.0;
+        for (uint32_t c = lane; c < ns; c += 32) {
+            const SegStat st = S[c];
+            if (st.smax > NEG_INF) {
+                const double o = (double)((st.smax - m) * c2);
+                e2 += (double)ex2_approx((float)o) * (st.ssum2 + o * st.ssum);
+            }
+        }
+        e2 = warp_sum_d(e2);
         if (lane == 0) {
             ri.M = m;
             ri.check_nan = nf | ((P.T != P.T) ? 1u : 0u);
             ri.S_raw = run;
+            ri.H_raw = run > 0.0 ? log(run) - 0.6931471805599453 * e2 / run : 0.0;
+            ri.dband = __int_as_float(0x7f800000);
+            ri.tmode = P.tmode;
         }
     }
     __syncthreads();
     const float M = ri.M;
+    // typical-p alone: the smallest dev bound d whose band [H - d, H + d] of
+    // surprise surely holds more than typical_p of the mass.  Each source bin
+    // (segment c, quarter-octave b) lies wholly inside the band once
+    // d >= max(H_hi - s_lo, s_hi - H_lo); those d are histogrammed by mass.
+    if (P.tmode == TYP_BAND && ri.S_raw > 0.0) {
+        __shared__ float dh[TB_CELLS];
+        for (uint32_t j = tid; j < TB_CELLS; j += K12_THREADS) dh[j] = 0.0f;
+        __syncthreads();
+        const double lnS = log(ri.S_raw), H = ri.H_raw;
+        const double dH = TB_H_REL * fabs(H) + TB_H_ABS;   // assumed bound on |H_raw - H|
+        const float *TH = P.mhist + (size_t)hrow * MAX_SEG * KH_BINS;
+        for (uint32_t i = tid; i < ns * KH_BINS; i += K12_THREADS) {
+            const uint32_t c = i / KH_BINS, b = i - c * KH_BINS;
+            const float o = off[c];
+            const float mass = TH[i];
+            if (!(o > NEG_INF) || !(mass > 0.0f)) continue;
+            const double xs_hi = (double)o - 0.25 * (double)b, xs_lo = (double)o - 0.25 * (double)(b + 1);
+            const double s_lo = lnS - xs_hi * 0.6931471805599453, s_hi = lnS - xs_lo * 0.6931471805599453;
+            const double d = fmax(fmax((H + dH) - s_lo, s_hi - (H - dH)), 0.0);
+            const int cell = (int)fmin(ceil(d * TB_PER_NAT), (double)(TB_CELLS - 1));
+            atomicAdd(&dh[cell], (float)((double)mass * (double)ssc[c] / ri.S_raw));
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // first cell whose cumulative (lower-bound) mass reaches the target
+            const float target = P.typical_p * (1.0f + TB_MASS_REL) + TB_MASS_ABS;
+            float run2 = 0.0f;
+            int found = -1;
+            for (uint32_t j0 = 0; j0 < TB_CELLS && found < 0; j0 += 32) {
+                const float v = dh[j0 + lane];
+                float incl = v;
+#pragma unroll
+                for (int o2 = 1; o2 < 32; o2 <<= 1) {
+                    const float t = __shfl_up_sync(0xffffffffu, incl, o2);
+                    if (lane >= o2) incl += t;
+                }
+                const uint32_t hit = __ballot_sync(0xffffffffu, run2 + incl >= target);
+                if (hit) found = (int)(j0 + __ffs(hit) - 1);
+                run2 += __shfl_sync(0xffffffffu, incl, 31);
+            }
+            if (lane == 0 && found >= 0 && found < TB_CELLS - 1)
+                ri.dband = (float)(found + 1) / (float)TB_PER_NAT + TB_D_PAD;
+        }
+        __syncthreads();
+    }
     // top-k: tile maxima per quarter-octave bin below M (the same x2 as the
     // main pass's per-logit candidate test, which is monotone in the logit)
     uint32_t kcount = 0;   // tiles whose maximum is above the bin edge -(tid+1)/4
@@ -1020,6 +1163,11 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
             const float xm = fminf(0.0f, log2f(P.min_p)) - 0.01f;
             if (xm > xf2) { xf2 = xm; binding = 3; }
         }
+        if (P.tmode == TYP_BAND) {
+            // the probability order only matters for indices[0] (ties at the top)
+            xf2 = -0.01f;
+            binding = 4;
+        }
         RowInfo r = ri;
         r.xf2 = xf2;
         r.binding = binding;
@@ -1038,6 +1186,12 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
 
 // ---------------------------------------------------------------------------
 // K2: classification, certified grid counts, candidates, walk items.
+// TERM_P: the terms p_i of the normaliser S (sampler.zig:83-88).
+// TERM_H: the terms h_i of the entropy H (sampler.zig:130-133), after S is
+// known; only for typical-p rows whose token is not yet final.
+enum : int { TERM_P = 0, TERM_H = 1 };
+
+template <int TERM>
 __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // rows in reverse order: the rows K1 streamed last are still in L2; the
     // first segments (most of the exact-pass tiles) start first
@@ -1051,9 +1205,15 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const RowInfo ri = P.rinfo[hrow];
     const float M = ri.M;
     RowHdr *hdr = P.hdr + hrow;
+    if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
+    // the entropy pass: S exact, log2 S for the terms' exponents
+    const float S = TERM == TERM_H ? hdr->S_exact : 1.0f;
+    const double lnS = TERM == TERM_H ? log((double)S) : 0.0;
+    const float l2S = (float)(lnS * 1.4426950408889634);
 
     __shared__ uint32_t swin[256];
     __shared__ double wtmp_d[NW + 1];
+    __shared__ double hbase;
     __shared__ uint32_t wtmp_u[NW + 1];
     __shared__ SegComp wtmp_s[2 * NW + 2];
     __shared__ TileRec rec[SEG_TILES];
@@ -1082,6 +1242,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // each tile's candidate binades of the running sum and its main-loop
     // parameters (thread t owns tile t)
     const float xf2 = ri.xf2;
+    const bool band = TERM == TERM_H && ri.tmode == TYP_BAND;
+    const float Hr = (float)ri.H_raw, dband = ri.dband;
     TileParam tp;
     {
         double ct = 0.0;
@@ -1089,10 +1251,41 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         if (live) {
             const TileStat ts = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
             tmax = ts.tmax;
-            ct = ts.tmax > NEG_INF ? (double)ts.tsr * (double)ex2_approx((ts.tmax - M) * c2) : 0.0;
+            if (ts.tmax > NEG_INF) {
+                const float o = (ts.tmax - M) * c2;
+                const double et = (double)ex2_approx(o);
+                if (TERM == TERM_P) {
+                    ct = (double)ts.tsr * et;
+                } else {   // sum of P (-ln P) = 2^o (ln S tsr - ln2 (tsr2 + o tsr)) / S
+                    ct = fmax(0.0, et * (lnS * ts.tsr - 0.6931471805599453 * ((double)ts.tsr2 + (double)o * ts.tsr)) /
+                                       (double)S);
+                }
+            }
+        }
+        double base;
+        if (TERM == TERM_P) {
+            base = P.sstat[(size_t)hrow * MAX_SEG + seg].base;
+        } else {
+            // entropy mass of the earlier segments, from their statistics
+            if (warp == 0) {
+                double hb = 0.0;
+                for (uint32_t c = lane; c < seg; c += 32) {
+                    const SegStat st = P.sstat[(size_t)hrow * MAX_SEG + c];
+                    if (st.smax > NEG_INF) {
+                        const double o = (double)((st.smax - M) * c2);
+                        hb += fmax(0.0, (double)ex2_approx((float)o) *
+                                            (lnS * st.ssum - 0.6931471805599453 * (st.ssum2 + o * st.ssum)) /
+                                            (double)S);
+                    }
+                }
+                hb = warp_sum_d(hb);
+                if (lane == 0) hbase = hb;
+            }
+            __syncthreads();
+            base = hbase;
         }
         double segtot;
-        const double Ps = P.sstat[(size_t)hrow * MAX_SEG + seg].base + block_exscan1_d(ct, wtmp_d, &segtot);
+        const double Ps = base + block_exscan1_d(ct, wtmp_d, &segtot);
         const double Pe = Ps + ct;
         const int lo = binade_of(Ps * (1.0 - WIN_LO));
         const int hi = binade_of(Pe * (1.0 + WIN_HI));
@@ -1103,15 +1296,26 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         // stores their p, so the walker finds a binade crossing in shared
         // memory instead of recomputing the tile from the logits
         const uint32_t nwin_seg = __syncthreads_count(live && cls == CLS_WINDOW);
-        const bool special = cls == CLS_COMPLEX || lo < -100 || (cls == CLS_WINDOW && nwin_seg <= 32u);
-        const float K = (float)(23 - max(lo, -100));   // log2(p / u_lo) = x2 + K
+        bool special = cls == CLS_COMPLEX || lo < -100 || (cls == CLS_WINDOW && nwin_seg <= 32u);
+        const float K = (float)(23 - max(lo, -100));   // log2(term / u_lo) = exponent + K
         // may hold candidates: the per-element test below is monotone in the
         // logit, so the tile maximum decides
         const float dm = __fsub_rn(tmax, M);
         const float xm = (dm == 0.0f) ? 0.0f : dm * c2;
-        const bool cand = tmax > NEG_INF && xm >= xf2;
+        bool cand = tmax > NEG_INF && xm >= xf2;
+        float e;
+        if (TERM == TERM_P) {
+            e = fmaxf(cert_eps(K), 0x1p-17f);
+        } else {
+            // the tile's largest P: a P near 1 has a tiny -ln P whose relative
+            // error the certificate cannot bound, so its tile is exact
+            const float zt = xm - l2S;
+            special = special || zt > -0.0625f;
+            e = fmaxf(cert_eps_h(K, fmaxf(-zt, 0.0625f), fabsf(l2S)), 0x1p-17f);
+            // band candidates: surprises of the tile are at least -zt ln2
+            cand = band && tmax > NEG_INF && -zt * 0.6931472f <= Hr + dband + 0.01f;
+        }
         tp.K = K;
-        const float e = fmaxf(cert_eps(K), 0x1p-17f);
         tp.fhi = 1.0f + e;
         tp.flo = 1.0f - e;
         tp.info = (special ? TP_SPECIAL : 0u) | (cand ? TP_CAND : 0u) | (cls << 2) | ((uint32_t)(lo + 128) << 8);
@@ -1129,6 +1333,14 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // common rounding of both (a tie, or a value too close to one, makes them
     // differ).  The clamp makes large values differ too.  The permuted order
     // of v does not matter: without ties the counts simply add.
+    // the term over u_lo: p / u_lo = 2^(x2 + K), or for the entropy
+    // P (-ln P) / u_lo = 2^(z + K) (-z ln2) with z = x2 - log2 S
+    auto term_y = [&](float d) {
+        if (TERM == TERM_P) return ex2_approx(fminf(fmaf(d, c2, tp.K), 17.5f));
+        const float z = fmaf(d, c2, -l2S);
+        const float w = fminf(z * -0.6931472f, 1e30f);   // -ln P (finite for P = 0)
+        return fminf(ex2_approx(fminf(z + tp.K, 40.0f)) * w, 185363.8f);   // 2^17.5
+    };
     uint32_t acc = 0u, diff = 0u;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -1136,8 +1348,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-            const float d = __fsub_rn(a4[c], M);
-            const float y = ex2_approx(fminf(fmaf(d, c2, tp.K), 17.5f));
+            const float y = term_y(__fsub_rn(a4[c], M));
             const uint32_t r1 = __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
             const uint32_t r2 = __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
             diff |= r1 ^ r2;
@@ -1157,8 +1368,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
             const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                const float d = __fsub_rn(a4[c], M);
-                const float y = ex2_approx(fminf(fmaf(d, c2, tp.K), 17.5f));
+                const float y = term_y(__fsub_rn(a4[c], M));
                 const uint32_t r3 = __float_as_uint(fmaf(y, hh, 12582912.0f));
                 const uint32_t r4 = __float_as_uint(fmaf(y, hl, 12582912.0f));
                 diff |= r3 ^ r4;
@@ -1168,7 +1378,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         acch -= (uint32_t)TILE * 0x4B400000u;
     }
     uint32_t nanl = 0;
-    if (check_nan && live) {
+    if (TERM == TERM_P && check_nan && live) {
 #pragma unroll 1
         for (int j = 0; j < 8; j++) {
             const float4 q = quad(j);
@@ -1198,7 +1408,15 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         base = __shfl_sync(0xffffffffu, base, 0);
         if (special) wlist[base + __popc(m & ((1u << lane) - 1u))] = tid;
     }
-    // candidates (index, logit): warp-aggregated reservation
+    // candidates (index, logit): warp-aggregated reservation.  The
+    // normaliser pass takes every token above the floor; the entropy pass,
+    // for typical-p alone, every token whose approximate dev = |-ln P - H|
+    // is inside the band
+    auto is_cand = [&](float d) {
+        if (TERM == TERM_P) return (d == 0.0f ? 0.0f : d * c2) >= xf2;
+        const float w = fminf(fmaf(d, c2, -l2S) * -0.6931472f, 1e30f);
+        return fabsf(w - Hr) <= dband;
+    };
     const bool tc = live && (tp.info & TP_CAND);
     if (__any_sync(0xffffffffu, tc)) {
         uint32_t nc = 0;
@@ -1208,10 +1426,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                 const float4 q = quad(j);
                 const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const float d = __fsub_rn(a4[c], M);
-                    nc += ((d == 0.0f ? 0.0f : d * c2) >= xf2) ? 1u : 0u;
-                }
+                for (int c = 0; c < 4; c++) nc += is_cand(__fsub_rn(a4[c], M)) ? 1u : 0u;
             }
         }
         const uint32_t incl = warp_incl_scan_u(nc);
@@ -1227,8 +1442,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                 const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    const float d = __fsub_rn(a4[c], M);
-                    if ((d == 0.0f ? 0.0f : d * c2) >= xf2) {
+                    if (is_cand(__fsub_rn(a4[c], M))) {
                         if (pos < P.cand_stride) cand[pos] = Candidate{g0 + tile_elem(tid, j, c), a4[c]};
                         pos++;
                     }
@@ -1261,7 +1475,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
                 break;
             }
         }
-        const float p = g < P.vocab ? prob_unnorm(a, M, T) : 0.0f;
+        const float p = g < P.vocab ? (TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S)) : 0.0f;
         r.qlo = warp_comp_reduce(elem_comp(p, r.lo));
         if (r.cls == CLS_WINDOW) r.qhi = warp_comp_reduce(elem_comp(p, r.lo + 1));
         if (r.cls != CLS_SIMPLE) {   // several binades: the walker may need the exact p
@@ -1506,6 +1720,8 @@ struct KBParams {
     uint64_t *rng;       // per handle row, 4 words
     RowTrace *trace;     // per handle row
     const uint32_t *kerr;
+    const RowInfo *rinfo;   // per handle row
+    uint32_t tmode;      // TYP_*
     uint32_t *out;       // per call row
 };
 
@@ -1521,6 +1737,38 @@ __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M
         }
     }
     return prob_unnorm(v, M, P.T);
+}
+
+// The term of element g for the recompute path: p (TERM_P) or the entropy
+// term h (TERM_H, with the normaliser S).
+template <int TERM>
+__device__ __forceinline__ float exact_term_at(const KBParams &P, uint32_t row, uint32_t g, float M,
+                                               const uint32_t *win, uint32_t nwin, float S) {
+    const float p = exact_p_at(P, row, g, M, win, nwin);
+    if (TERM == TERM_P) return p;
+    const float Pn = __fdiv_rn(p, S);
+    return Pn > 0.0f ? __fmul_rn(Pn, -log_ref(Pn)) : 0.0f;
+}
+
+// Block-wide bitonic sort (ascending) of npow (a power of two) keys in shared
+// memory; every thread of the block takes part.
+__device__ void block_bitonic(unsigned long long *k, uint32_t npow) {
+    for (uint32_t size = 2; size <= npow; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (uint32_t i = threadIdx.x; i < npow / 2; i += blockDim.x) {
+                const uint32_t a = 2 * i - (i & (stride - 1));
+                const uint32_t b = a + stride;
+                const bool up = ((a & size) == 0);
+                const unsigned long long ka = k[a], kb = k[b];
+                if (up ? (ka > kb) : (ka < kb)) {
+                    k[a] = kb;
+                    k[b] = ka;
+                }
+            }
+        }
+    }
+    __syncthreads();
 }
 
 // Candidate key: ascending key order == (p descending, index ascending).
@@ -1586,11 +1834,146 @@ __device__ unsigned long long *cta_radix_sort(unsigned long long *a, unsigned lo
     return a;
 }
 
+// Typical-p (sampler.zig:128-154) and the draw (:156-168), after the entropy
+// walk.  The list is the selected set from the normaliser pass (TYP_SELECTED:
+// (index, P) pairs) or the band candidates of the entropy pass (TYP_BAND:
+// (index, logit)).  Exact dev = |fl(-logf P) - H| gives the stable dev order;
+// cum_typ over it deselects the crossing token and everything after it; the
+// kept tokens are then taken in probability order (stable) for the mass and
+// the inverse-CDF draw.  In band mode the kept set is trusted only when every
+// token up to the crossing's dev is surely inside the band.
+__device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, float H, const uint32_t *swin,
+                             uint32_t nwin, unsigned long long *skeys, float *sprobs, unsigned long long *red2) {
+    const int tid = threadIdx.x;
+    RowHdr *hdr = P.hdr + hrow;
+    const RowInfo ri = P.rinfo[hrow];
+    const float M = hdr->M, S = hdr->S_exact;
+    const uint32_t mode = P.tmode;
+    const Candidate *cl = P.cand + (size_t)hrow * P.cand_stride;
+    unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
+    unsigned long long *gk1 = gk0 + P.cand_stride;
+    const uint32_t n = min(mode == TYP_SELECTED ? hdr->n_sel : hdr->n_cand, P.cand_stride);
+    const bool big = n > (uint32_t)CAND_SMEM;
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // radix scratch (big lists keep P in global memory)
+    __shared__ uint32_t n_keep_sh, status_sh, nk_pow_sh;
+
+    // 1. keys (dev, index), ascending
+    uint32_t npow = 1;
+    while (npow < n) npow <<= 1;
+    unsigned long long *keys = big ? gk0 : skeys;
+    for (uint32_t i = tid; i < (big ? n : npow); i += KB_THREADS) {
+        unsigned long long k = ~0ull;
+        if (i < n) {
+            const Candidate c = cl[i];
+            const float Pi = mode == TYP_SELECTED ? c.v : __fdiv_rn(prob_unnorm(c.v, M, P.T), S);
+            const float sur = Pi > 0.0f ? -log_ref(Pi) : __int_as_float(0x7f800000);
+            const float dev = fabsf(__fsub_rn(sur, H));
+            k = ((unsigned long long)__float_as_uint(dev) << 32) | c.idx;
+        }
+        keys[i] = k;
+    }
+    __syncthreads();
+    if (big) {
+        keys = cta_radix_sort(gk0, gk1, n, cnt, red2);
+    } else {
+        block_bitonic(keys, npow);
+    }
+    // 2. P in dev order, recomputed from the logits as the normaliser pass did
+    float *pd = big ? reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0) : sprobs;
+    for (uint32_t i = tid; i < n; i += KB_THREADS)
+        pd[i] = __fdiv_rn(exact_p_at(P, row, (uint32_t)keys[i], M, swin, nwin), S);
+    __syncthreads();
+    // 3. cum_typ (sequential f32 in dev order)
+    if (tid == 0) {
+        uint32_t nk = n, st = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+        float cum = 0.0f;
+        bool crossed = false;
+        for (uint32_t i = 0; i < n; i++) {
+            cum = __fadd_rn(cum, pd[i]);
+            if (cum > P.typical_p) {
+                nk = i;
+                crossed = true;
+                break;
+            }
+        }
+        if (mode == TYP_BAND && st == ROW_OK) {
+            // the band held every token with approximate dev <= dband, where
+            // the approximation used H_raw: tokens with exact dev up to
+            // dband - |H_raw - H| - (surprise error) are surely in it
+            const float dcross = crossed ? __uint_as_float((uint32_t)(keys[nk] >> 32)) : __int_as_float(0x7f800000);
+            const float herr = fabsf((float)ri.H_raw - H);
+            const float safe = ri.dband - herr - (1e-4f * (fabsf(H) + dcross) + 1e-4f);
+            if (!crossed || !(dcross <= safe)) st = ROW_ENOTSUP;
+        }
+        uint32_t np2 = 1;
+        while (np2 < nk) np2 <<= 1;
+        n_keep_sh = nk;
+        status_sh = st;
+        nk_pow_sh = np2;
+    }
+    __syncthreads();
+    const uint32_t nk = n_keep_sh, nkp = nk_pow_sh;
+    // 4. the kept tokens by (P descending, index ascending): each thread
+    // rewrites its own entries in place
+    for (uint32_t i = tid; i < (big ? nk : nkp); i += KB_THREADS)
+        keys[i] = i < nk ? cand_key((uint32_t)keys[i], pd[i]) : ~0ull;
+    __syncthreads();
+    if (big) {
+        keys = cta_radix_sort(keys, keys == gk0 ? gk1 : gk0, nk, cnt, red2);
+    } else {
+        block_bitonic(keys, nkp);
+    }
+    if (tid != 0) return;
+    // 5. kept mass (sorted order) and the draw
+    uint32_t status = status_sh;
+    uint32_t token = hdr->top_idx, path = 2;
+    float total = 0.0f, u = __int_as_float(0x7fc00000);
+    uint64_t *rng = P.rng + (size_t)hrow * 4;
+    uint64_t s4[4] = {rng[0], rng[1], rng[2], rng[3]};
+    if (status == ROW_OK) {
+        for (uint32_t j = 0; j < nk; j++) total = __fadd_rn(total, key_p(keys[j]));
+        if (total > 0.0f) {   // else indices[0] without a draw (sampler.zig:160)
+            u = rng_float(s4);
+            float r = __fmul_rn(u, total);
+            path = 4;
+            for (uint32_t j = 0; j < nk; j++) {
+                r = __fsub_rn(r, key_p(keys[j]));
+                if (r <= 0.0f) {
+                    token = (uint32_t)keys[j];
+                    path = 3;
+                    break;
+                }
+            }
+        }
+        rng[0] = s4[0]; rng[1] = s4[1]; rng[2] = s4[2]; rng[3] = s4[3];
+        P.out[row] = token;
+    } else {
+        P.out[row] = 0xFFFFFFFFu;
+    }
+    RowTrace tr;
+    tr.S = S;
+    tr.total = total;
+    tr.u = u;
+    tr.n_kept = nk;
+    tr.path = path;
+    tr.flags = hdr->flags | (status == ROW_ENOTSUP ? RF_TYP_BAND : 0u);
+    tr.n_cand = n;
+    tr.status = status;
+    tr.n_items = 0;
+    tr.n_wc = hdr->n_wc;
+    tr.n_slow = 0;
+    tr.H = H;
+    P.trace[hrow] = tr;
+}
+
+template <int TERM>
 __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t row = blockIdx.x;
     const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const RowHdr *hdr = P.hdr + hrow;
+    RowHdr *hdr = P.hdr + hrow;
+    if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
+    const float Sx = TERM == TERM_H ? hdr->S_exact : 1.0f;
 
     __shared__ Item sitems[ITEM_CHUNK];
     __shared__ Item sall[ITEM_SMEM];             // the first `spec` items of every segment
@@ -1611,7 +1994,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t flags0 = hdr->flags;
     const uint32_t n_cand = min(hdr->n_cand, P.cand_stride);
     const uint32_t n_wc = min(hdr->n_wc, (uint32_t)WC_CAP);
-    const bool big = n_cand > (uint32_t)CAND_SMEM;
+    const bool big = TERM == TERM_P && n_cand > (uint32_t)CAND_SMEM;
 
     // the walk's inputs in shared memory.  Segment s's items start at tile
     // s * SEG_TILES; its first `spec` items are fetched speculatively in the
@@ -1648,7 +2031,9 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     }
     __syncthreads();
     uint32_t nz = 0;
-    if (!big) {
+    if (TERM == TERM_H) {
+        // no candidate keys: the typical tail builds its own list
+    } else if (!big) {
         while (npow < n_cand) npow <<= 1;
         for (uint32_t i = tid; i < npow; i += KB_THREADS) {
             unsigned long long k = ~0ull;
@@ -1727,7 +2112,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
         // add one tile element by element, p recomputed from the logits
         auto add_tile = [&](uint32_t tile) {
-            tilep[lane] = exact_p_at(P, row, tile * TILE + lane, M, swin, nwin);
+            tilep[lane] = exact_term_at<TERM>(P, row, tile * TILE + lane, M, swin, nwin, Sx);
             __syncwarp();
             st = state_of(seq_add32_smem(float_of(st), tilep));
             __syncwarp();
@@ -1837,7 +2222,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             walk_slow = nslow;
         }
         }
-    } else if (!big) {
+    } else if (TERM == TERM_P && !big) {
         // ---- candidate sort in shared memory: ascending key ----
         const int t2 = tid - 32, nthr = KB_THREADS - 32;
         for (uint32_t size = 2; size <= npow; size <<= 1) {
@@ -1858,6 +2243,10 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         asm volatile("bar.sync 1, %0;" ::"r"(nthr));
     }
     __syncthreads();
+    if (TERM == TERM_H) {
+        typical_tail(P, row, hrow, S_sh, swin, nwin, skeys, sprobs, red2);
+        return;
+    }
 
     // large candidate sets: stable radix sort in global memory (whole CTA)
     unsigned long long *keys = skeys;
@@ -1899,6 +2288,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     if (tid != 0) return;
 
     uint32_t status = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+    bool pending = false;
     uint32_t token = 0;
     uint32_t path = 0;
     uint32_t n_kept = 0;
@@ -1964,15 +2354,22 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             while (j < n_sel && !(probs[j] < thr)) j++;
             n_sel = j;
         }
-        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || n_sel < n_pos ||
+        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || binding == 4 || n_sel < n_pos ||
                               (k_act && P.top_k <= n_pos);
         if (status != ROW_OK) {
             // a bounded device wait gave up: nothing of this call is trusted
         } else if (!cover_ok) {
             status = ROW_EINTERNAL;
             flags |= RF_CAND_SHORT;
-        } else if (P.typical_p > 0.0f && P.typical_p < 1.0f) {
-            status = ROW_ENOTSUP;  // typical-p runs in its own pass (not in this build)
+        } else if (P.tmode != TYP_OFF) {
+            // typical-p follows in the entropy passes (sampler.zig:128-154):
+            // hand over S, indices[0] and the selected set (index, P)
+            pending = true;
+            Candidate *cw = P.cand + (size_t)hrow * P.cand_stride;
+            if (P.tmode == TYP_SELECTED)
+                for (uint32_t j = 0; j < n_sel; j++) cw[j] = Candidate{idxs[2 * j], probs[j]};
+            hdr->n_sel = P.tmode == TYP_SELECTED ? n_sel : 0u;
+            hdr->top_idx = n_pos > 0 ? idxs[0] : 0u;
         } else {
             // kept mass in sorted order (sampler.zig:156-159)
             for (uint32_t j = 0; j < n_sel; j++) total = __fadd_rn(total, probs[j]);
@@ -1996,6 +2393,13 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             }
         }
     }
+    if (P.tmode != TYP_OFF) {
+        hdr->S_exact = S;
+        hdr->tdone = pending ? 0u : 1u;
+        hdr->n_cand = 0;   // the entropy pass appends its own candidates
+        hdr->n_wc = 0;
+        if (pending) return;   // the typical tail writes token, state and trace
+    }
     if (status == ROW_OK) {
         rng[0] = s4[0]; rng[1] = s4[1]; rng[2] = s4[2]; rng[3] = s4[3];
         P.out[row] = token;
@@ -2014,7 +2418,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     tr.n_items = walk_items;
     tr.n_wc = hdr->n_wc;
     tr.n_slow = walk_slow;
-    tr.pad = 0;
+    tr.H = __int_as_float(0x7fc00000);
     P.trace[hrow] = tr;
 }
 
@@ -2130,7 +2534,8 @@ static cudaError_t raise_smem_limits(size_t a, size_t b) {
         if (e == cudaSuccess) g_smem_a = a;
     }
     if (e == cudaSuccess && b > g_smem_b) {
-        e = cudaFuncSetAttribute(kernel_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
+        e = cudaFuncSetAttribute(kernel_b<TERM_P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel_b<TERM_H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
         if (e == cudaSuccess) g_smem_b = b;
     }
     return e;
@@ -2258,20 +2663,8 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.cand = s->d_cand;
     A.cand_stride = s->cand_stride;
     A.kerr = s->d_kerr;
-
-    cudaEvent_t *ev = nullptr;
-    if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
-    if (ev) cudaEventRecord(ev[0], st);
-    k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
-    k1_rows<<<rows, K12_THREADS, 0, st>>>(A);
-    if (ev) cudaEventRecord(ev[1], st);
-    k2_main<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
-    if (ev) cudaEventRecord(ev[2], st);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        fprintf(stderr, "b200_sampler: pass launch failed: %s\n", cudaGetErrorString(e));
-        return BS_ECUDA;
-    }
+    A.typical_p = c.typical_p;
+    A.tmode = typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p);
 
     KBParams B;
     B.logits = d_logits;
@@ -2298,10 +2691,34 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.rng = s->d_rng;
     B.trace = s->d_trace;
     B.kerr = s->d_kerr;
+    B.rinfo = s->d_rinfo;
+    B.tmode = A.tmode;
     B.out = d_out;
-    kernel_b<<<rows, KB_THREADS, s->smem_b, st>>>(B);
+
+    // statistics, row reduction | main pass | walk and draw.  With typical-p
+    // the normaliser's walk hands over to a second main pass and walk over
+    // the entropy terms (profiled with the main pass | the final walk).
+    cudaEvent_t *ev = nullptr;
+    if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
+    if (ev) cudaEventRecord(ev[0], st);
+    k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    k1_rows<<<rows, K12_THREADS, 0, st>>>(A);
+    if (ev) cudaEventRecord(ev[1], st);
+    k2_main<TERM_P><<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    if (A.tmode != TYP_OFF) {
+        kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
+        k2_main<TERM_H><<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    }
+    if (ev) cudaEventRecord(ev[2], st);
+    if (A.tmode != TYP_OFF) {
+        kernel_b<TERM_H><<<rows, KB_THREADS, s->smem_b, st>>>(B);
+    } else {
+        kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
+    }
     if (ev) cudaEventRecord(ev[3], st);
-    return cuda_status(cudaGetLastError());
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
+    return cuda_status(e);
 }
 
 extern "C" bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t ld, uint32_t row0,
@@ -2417,13 +2834,72 @@ __global__ void cert_check_kernel(uint32_t n, uint64_t seed, unsigned long long 
     if (ex.q0 != ex.q1 || ex.q0 != r1 - 0x4B400000u) atomicAdd(&out[0], 1ull);
 }
 
+// The same for the entropy terms (cert_eps_h): the certified count of
+// y = min(ex2.approx(min(z + K, 40)) (-z ln2), 2^17.5), z = fma(d, c2, -log2 S),
+// against elem_comp of the exact term fl(P * -logf(P)), P = fl(p / S).
+__global__ void cert_check_h_kernel(uint32_t n, uint64_t seed, unsigned long long *out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t h = seed ^ (0xD1B54A32D192ED03ull * (i + 1));
+    auto nxt = [&]() {
+        h += 0x9E3779B97F4A7C15ull;
+        uint64_t z = h;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    auto unif = [&]() { return (double)(nxt() >> 11) * 0x1p-53; };
+    const int lo = -60 + (int)(nxt() % 70);   // binades -60 .. 9
+    const float K = (float)(23 - lo);
+    const float T = (float)(0.05 + 5.0 * unif());
+    const float M = (float)(-50.0 + 100.0 * unif());
+    const float S = (float)exp2(10.0 * unif());   // 1 .. 1024
+    const float c2 = (float)(1.4426950408889634 / (double)T);
+    const float l2S = (float)(log((double)S) * 1.4426950408889634);
+    // target y = P (-ln P) / u_lo: near k + 1/2 (half of the samples) or anywhere
+    double ly = -3.0 + 20.0 * unif();
+    double y0 = exp2(ly);
+    if (nxt() & 1) y0 = floor(y0) + 0.5 + (unif() - 0.5) * 2e-4 * y0;
+    // solve 2^(z + K) (-z ln2) = y0 for z < -1/16 (Newton on the branch below
+    // the maximum at z = -1/ln2)
+    double z = -2.0 - 30.0 * unif();
+    for (int it = 0; it < 60; it++) {
+        const double f = exp2(z + K) * (-z * 0.6931471805599453) - y0;
+        const double fp = exp2(z + K) * 0.6931471805599453 * (-z * 0.6931471805599453 - 1.0);
+        if (fp == 0.0) break;
+        const double zn = z - f / fp;
+        z = fmin(zn, -1.4426950408889634 - 1e-3);
+    }
+    if (!(z < -0.0625) || z + l2S > 0.0) return;
+    const double x2 = z + (double)l2S;
+    const float v = __fadd_rn(M, (float)(x2 * (double)T / 1.4426950408889634));
+    const float d = __fsub_rn(v, M);
+    const float zz = fmaf(d, c2, -l2S);
+    if (!(zz < -0.0625f)) return;
+    const float w = fminf(zz * -0.6931472f, 1e30f);
+    const float y = fminf(ex2_approx(fminf(zz + K, 40.0f)) * w, 185363.8f);
+    const float e = fmaxf(cert_eps_h(K, fmaxf(-zz, 0.0625f), fabsf(l2S)), 0x1p-17f);
+    const uint32_t r1 = __float_as_uint(fmaf(y, 1.0f + e, 12582912.0f));
+    const uint32_t r2 = __float_as_uint(fmaf(y, 1.0f - e, 12582912.0f));
+    atomicAdd(&out[2], 1ull);
+    if (r1 != r2) return;
+    atomicAdd(&out[1], 1ull);
+    const Comp ex = elem_comp(entropy_term(v, M, T, S), lo);
+    if (ex.q0 != ex.q1 || ex.q0 != r1 - 0x4B400000u) atomicAdd(&out[0], 1ull);
+}
+
 extern "C" bs_status bs_debug_cert_check(uint32_t n, uint64_t seed, unsigned long long *h_out) {
     if (!h_out || n == 0) return BS_EINVAL;
+    const bool entropy = (seed >> 63) != 0;   // the entropy terms' certificate
     unsigned long long *d = nullptr;
     BS_CUDA(cudaMalloc(&d, 3 * sizeof(unsigned long long)));
     cudaError_t e = cudaMemset(d, 0, 3 * sizeof(unsigned long long));
     if (e == cudaSuccess) {
-        cert_check_kernel<<<(n + 255) / 256, 256>>>(n, seed, d);
+        if (entropy) {
+            cert_check_h_kernel<<<(n + 255) / 256, 256>>>(n, seed, d);
+        } else {
+            cert_check_kernel<<<(n + 255) / 256, 256>>>(n, seed, d);
+        }
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaMemcpy(h_out, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
@@ -2513,7 +2989,8 @@ static cudaError_t static_scratch_base(int dev, unsigned char **base) {
         cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess) return e;
         const size_t smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
-        e = cudaFuncSetAttribute(kernel_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
+        e = cudaFuncSetAttribute(kernel_b<TERM_P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel_b<TERM_H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
         if (e != cudaSuccess) return e;
         g_static_base[dev] = static_cast<unsigned char *>(p);
     }
@@ -2532,7 +3009,6 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
                 rows, vocab, (unsigned)BS_STATIC_MAX_ROWS, (unsigned)BS_STATIC_MAX_VOCAB);
         return BS_EINVAL;
     }
-    if (cfg->typical_p > 0.0f && cfg->typical_p < 1.0f) return BS_ENOTSUP;
     if (rows == 0) return BS_OK;
     if (cfg->temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, vocab, d_out, stream);
     int dev = 0;

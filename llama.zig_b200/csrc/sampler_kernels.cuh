@@ -6,15 +6,9 @@
 
 namespace bs {
 
-constexpr int TILE = 32;                 // elements per tile (one warp, one lane each)
-constexpr int KA_THREADS = 512;          // Kernel A block size
-constexpr int KA_WARPS = KA_THREADS / 32;
-constexpr int KB_THREADS = 256;          // Kernel B block size
-constexpr int MAX_CLUSTER = 8;           // portable cluster size
-constexpr int SEG_TARGET = 16384;        // target elements per CTA segment
-constexpr int SEG_MAX = 32768;           // hard cap (128 KB of shared memory)
+constexpr int TILE = 32;                 // elements per tile
+constexpr int KB_THREADS = 256;          // walk/draw kernel block size
 constexpr int CAND_SMEM = 4096;          // candidates sorted in shared memory (fast path)
-constexpr int HIST_BINS = 256;           // top-p tail-mass histogram bins
 constexpr int WC_CAP = 256;              // window/complex tiles with stored p per row
 constexpr int KSEL_MAX = 256;            // largest top_k served by the tile-max floor
 constexpr int ITEM_CHUNK = 128;          // items staged per step in Kernel B (rows with many items)
@@ -30,13 +24,21 @@ enum : uint32_t {
     RF_CAND_BIG = 1u << 1,      // more than CAND_SMEM candidates (global-memory path)
     RF_CAND_SHORT = 1u << 2,    // candidate set did not cover the kept prefix
     RF_SLOW_WALK = 1u << 3,     // walker needed the recompute path (diagnostic)
-    RF_BAD_CONFIG = 1u << 4,
+    RF_TYP_BAND = 1u << 4,      // typical-p: the dev band did not cover the kept set
 };
 
-// Kernel output status per row (written by Kernel B).
+// Typical-p modes of a row (sampler.zig:128-154).
+enum : uint32_t {
+    TYP_OFF = 0,       // typical_p outside (0, 1)
+    TYP_SELECTED = 1,  // another filter bounds the selected set: typical-p runs over it
+    TYP_BAND = 2,      // typical-p alone: candidates from a band of dev = |surprise - H|
+};
+
+// Per-row status (written by the walk/draw pass).
 enum : uint32_t { ROW_OK = 0, ROW_ETIMEOUT = 5, ROW_ENOTSUP = 6, ROW_EINTERNAL = 7 };
 
-// Row header in scratch: written by Kernel A, read by Kernel B.
+// Row header in scratch: written by the statistics and main passes, read by
+// the walk/draw pass.
 struct RowHdr {
     float M;             // max of penalised logits (sampler.zig:80-81)
     float raw_max;       // sampleArgmax of the raw logits, value ...
@@ -49,8 +51,12 @@ struct RowHdr {
     uint32_t seg_items[64];   // walk items per segment (MAX_SEG)
     uint32_t seg_tile0[64];
     uint32_t nseg;
-    uint32_t binding;    // which filter set the candidate floor (0 none, 1 k, 2 p, 3 min-p)
-    uint32_t pad[2];
+    uint32_t binding;    // which filter set the candidate floor (0 none, 1 k, 2 p, 3 min-p, 4 typical)
+    // typical-p (written by the normaliser's walk, read by the entropy passes)
+    float S_exact;       // the sequential f32 normaliser
+    uint32_t top_idx;    // indices[0]: the first token of the probability order
+    uint32_t n_sel;      // TYP_SELECTED: size of the selected set
+    uint32_t tdone;      // the row's token is final (NaN row, sum <= 0, ...)
 };
 
 // One walk item: a stretch of SIMPLE tiles with one binade, or one
@@ -76,7 +82,7 @@ struct RowTrace {
     uint32_t n_items;  // walk items of the row
     uint32_t n_wc;     // window/complex tiles
     uint32_t n_slow;   // tiles the walk recomputed from the logits
-    uint32_t pad;
+    float H;           // typical-p: the sequential f32 entropy (NaN otherwise)
 };
 
 struct Candidate {

@@ -60,7 +60,8 @@ class BsConfig(ctypes.Structure):
 
 
 class RowTrace(ctypes.Structure):
-    """Per-row diagnostics of the last call (S, kept mass, draw, path)."""
+    """Per-row diagnostics of the last call (S, kept mass, draw, path, and
+    with typical-p the entropy H)."""
 
     _fields_ = [
         ("S", ctypes.c_float),
@@ -74,7 +75,7 @@ class RowTrace(ctypes.Structure):
         ("n_items", ctypes.c_uint32),
         ("n_wc", ctypes.c_uint32),
         ("n_slow", ctypes.c_uint32),
-        ("pad", ctypes.c_uint32),
+        ("H", ctypes.c_float),
     ]
 
 

@@ -86,14 +86,11 @@ def test_reference_tests_through_c_abi(gpu_pkg):
 
 
 GOLDEN = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
-GPU_UNSUPPORTED = {"typical", "typical_combo"}   # typical-p: separate pass, not in this build
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
 def test_golden_fixtures_on_gpu(gpu_pkg, path):
     name = os.path.basename(path)[:-4]
-    if name in GPU_UNSUPPORTED:
-        pytest.skip("typical-p pass not built yet")
     f = np.load(path)
     c = json.loads(str(f["config"]))
     prev = f["prev"] if "prev" in f.files else None
@@ -223,3 +220,57 @@ def test_certificate_bound_holds(gpu_pkg):
         assert total > (1 << 20)
         assert bad == 0, f"{bad} certified counts differ from the exact ones (seed {seed})"
         assert certified > total // 2
+
+
+def test_entropy_certificate_bound_holds(gpu_pkg):
+    # the entropy pass's certificate (cert_eps_h): seeds with the top bit set
+    # select the entropy-term check
+    import ctypes
+    L = gpu_pkg.lib()
+    L.bs_debug_cert_check.argtypes = [ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]
+    L.bs_debug_cert_check.restype = ctypes.c_int
+    out = np.zeros(3, np.uint64)
+    for seed in range(4):
+        assert L.bs_debug_cert_check(1 << 22, (1 << 63) | seed, out.ctypes.data) == 0
+        bad, certified, total = (int(v) for v in out)
+        assert total > (1 << 20)
+        assert bad == 0, f"{bad} certified entropy counts differ from the exact ones (seed {seed})"
+        assert certified > total // 4
+
+
+def _typical_case(gpu_pkg, orc, c, x, seeds, what):
+    """Tokens, RNG states, S and the entropy H bit for bit."""
+    rows, V = x.shape
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=rows, vocab=V, seeds=seeds)
+    tok = s.sample(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.uint32)
+    torch.cuda.synchronize()
+    tr = s.traces()
+    st = s.rng_state
+    s.close()
+    exp, otr, ost = orc.sample_batch(orc.make_config(**c), x, seeds=seeds)
+    for r in range(rows):
+        assert tr[r].status == 0, f"{what}: row {r} status {tr[r].status} flags {tr[r].flags}"
+    bad = np.flatnonzero(tok != exp)
+    assert len(bad) == 0, f"{what}: rows {bad[:8]} gpu {tok[bad[:8]]} ref {exp[bad[:8]]}"
+    assert np.array_equal(st, ost), f"{what}: RNG states differ"
+    for r in range(rows):
+        if otr[r].path >= 2 and np.isfinite(otr[r].entropy):
+            assert f32bits(tr[r].H) == f32bits(otr[r].entropy), (what, r, tr[r].H, otr[r].entropy)
+            assert f32bits(tr[r].S) == f32bits(otr[r].sum), (what, r)
+
+
+@pytest.mark.parametrize("rows,vocab", [(16, 151936), (8, 40000)])
+def test_typical_alone_matches_checker(gpu_pkg, orc, rows, vocab):
+    # config 2: typical_p = 0.9 alone (the dev band path)
+    w = gpu_pkg.workloads.WORKLOADS["c2"]
+    x = gpu_pkg.workloads.make_logits(w, rows=rows, vocab=vocab)
+    _typical_case(gpu_pkg, orc, w.config(), x, w.seeds(rows), f"c2 V={vocab}")
+
+
+@pytest.mark.parametrize("extra", [dict(top_k=40), dict(top_p=0.95), dict(min_p=0.05),
+                                   dict(top_k=200, top_p=0.9, min_p=0.01)])
+def test_typical_with_other_filters(gpu_pkg, orc, extra):
+    # typical-p over the selected set of another filter
+    w = gpu_pkg.workloads.WORKLOADS["c2"]
+    x = gpu_pkg.workloads.make_logits(w, rows=8, vocab=50000)
+    _typical_case(gpu_pkg, orc, w.config(**extra), x, w.seeds(8), str(extra))
