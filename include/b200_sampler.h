@@ -119,7 +119,7 @@ bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uint32_t *n_ca
  * static device array of this library (about 14 MB per device), so at most
  * BS_STATIC_MAX_ROWS rows of at most BS_STATIC_MAX_VOCAB logits per call;
  * larger calls return BS_EINVAL with a message on stderr.
- *   cfg    : the sampler settings (typical_p in (0,1) -> BS_ENOTSUP)
+ *   cfg    : the sampler settings
  *   d_rng  : device buffer of rows x 4 u64 xoshiro256++ states, in the layout
  *            bs_get_rng_state returns; advanced in place like bs_sample's
  * Other arguments as bs_sample (row i of this call uses d_rng[4i..4i+3]).
