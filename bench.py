@@ -154,6 +154,75 @@ def run_reference(args, pkg, w):
     return 0
 
 
+def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
+    """Config 4: all B rows, vocab split over the ranks (a tensor-parallel LM
+    head).  One step = the all-to-all transpose, sampling this rank's B/G rows
+    and the all-gather of the B token ids (replicated on every rank)."""
+    B, V = w.rows, w.vocab
+    cfg = pkg.SamplerConfig(**w.config())
+    vs = pkg.sharding.VocabShardedSampler(cfg, B, V, dist if world > 1 else None, device=local)
+    lay = vs.lay
+    host = [np.ascontiguousarray(lay.shard_of(pkg.workloads.make_logits(w, step=s, rows=B))) for s in range(ROTATE)]
+    dev = [torch.from_numpy(h).cuda() for h in host]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        vs.sample(dev[i % ROTATE])
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            vs.sample(dev[i % ROTATE])
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
+    if vs.local.last_status() != 0:
+        raise RuntimeError(f"sampler status {vs.local.last_status()}")
+    # end to end: pinned host shard -> device, sample, B token ids -> host
+    pinned = [torch.from_numpy(h).pin_memory() for h in host[:2]]
+    d_in = torch.empty_like(dev[0])
+    for i in range(3):
+        d_in.copy_(pinned[i % 2], non_blocking=True)
+        vs.sample(d_in).cpu()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        d_in.copy_(pinned[i % 2], non_blocking=True)
+        vs.sample(d_in).cpu()
+    e2e_s = pkg.sharding.max_over_ranks(time.perf_counter() - t0, dist, device="cuda")
+    if rank == 0:
+        peak, peak_kind = peaks()
+        step_s = ms / args.steps / 1e3
+        per_gpu_bytes = 4.0 * V * B / world
+        ach = per_gpu_bytes / step_s / 1e9
+        line = {
+            "metric": "rows sampled/sec", "value": B / step_s, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": workload_desc(w), "rows": B, "vocab": V,
+                       "parallelism": f"vocab-sharded x{world}: all-to-all transpose, B/G rows per rank, "
+                                      "all-gather of the token ids",
+                       "l2": f"{ROTATE} rotating shard batches ({ROTATE * per_gpu_bytes / 1e6:.0f} MB per GPU)"},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole step per GPU (its 4 V B / G bytes of shard over the step time)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": B * args.e2e_steps / e2e_s, "unit": "rows/s",
+                    "h2d_bytes_per_step": int(per_gpu_bytes), "d2h_bytes_per_step": 4 * B,
+                    "api": "VocabShardedSampler.sample (pinned host shard)"},
+            "gpu_launches": 4 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    vs.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -184,6 +253,9 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+
+    if w.name == "c4":
+        return run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local)
 
     B, V = w.rows, w.vocab
     # this rank's rows; seeds keyed by the global row

@@ -105,11 +105,12 @@ bs_status bs_last_device_status(bs_sampler *s);
 
 /* Profiling (the counterpart of the engine's --report-json timers,
  * src/engine.zig:14-26 and :457-462): when enabled, each of the next
- * `max_calls` bs_sample calls records CUDA events around its three kernels.
+ * `max_calls` bs_sample calls records CUDA events around its kernel groups.
  * bs_profile_read synchronises and writes, for up to `cap` calls, the
  * durations in ms: ms[3i] the statistics pass (the one HBM read of the
- * logits), ms[3i+1] the main pass, ms[3i+2] the walk/draw pass; then it
- * resets the ring. */
+ * logits, and the per-row reduction), ms[3i+1] the main pass (with typical-p
+ * also the normaliser walk and the entropy main pass), ms[3i+2] the final
+ * walk/draw pass; then it resets the ring. */
 bs_status bs_profile_enable(bs_sampler *s, uint32_t max_calls);
 bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uint32_t *n_calls);
 

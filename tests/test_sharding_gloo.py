@@ -73,3 +73,50 @@ def test_shard_layout():
     assert sh.max_over_ranks(3.5) == 3.5
     with pytest.raises(ValueError):
         sh.shard_for(4, 4, 3)
+
+
+def _vocab_rank_main(rank, world, port, rows, vocab, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as graft
+    pkg = graft.load_package()
+    orc = graft.load_oracle()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = pkg.workloads.WORKLOADS["c4"]
+        full = torch.from_numpy(pkg.workloads.make_logits(w, rows=rows, vocab=vocab))
+        lay = pkg.sharding.VocabShard(rank, world, rows, vocab)
+        shard = lay.shard_of(full).contiguous()
+        mine = pkg.sharding.rows_from_vocab_shards(lay, shard, dist)
+        assert torch.equal(mine, full[lay.row0:lay.row0 + lay.rows_per_rank])
+        tok, _, st = orc.sample_batch(orc.make_config(**w.config()), mine.numpy(), seeds=lay.seeds(w.seed))
+        allt = pkg.sharding.gather_tokens(lay, torch.from_numpy(tok.astype(np.int64)), dist)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "vocab_tokens.npy"), allt.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_vocab_sharded_transpose_matches_one_process(tmp_path, pkg, orc, world):
+    rows, vocab = 8, 4096
+    mp.start_processes(_vocab_rank_main, args=(world, _free_port(), rows, vocab, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    got = np.load(tmp_path / "vocab_tokens.npy")
+    w = pkg.workloads.WORKLOADS["c4"]
+    x = pkg.workloads.make_logits(w, rows=rows, vocab=vocab)
+    tok, _, _ = orc.sample_batch(orc.make_config(**w.config()), x, seeds=w.seeds(rows))
+    assert np.array_equal(got, tok.astype(np.int64))
+
+
+def test_vocab_shard_layout():
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as graft
+    sh = graft.load_package().sharding
+    lay = sh.VocabShard(2, 4, 512, 128256)
+    assert (lay.cols, lay.col0, lay.rows_per_rank, lay.row0) == (32064, 64128, 128, 256)
+    assert list(lay.seeds(7)[:2]) == [263, 264]
+    with pytest.raises(ValueError):
+        sh.VocabShard(0, 3, 512, 128256)
