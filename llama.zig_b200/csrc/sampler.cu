@@ -688,6 +688,15 @@ __device__ __forceinline__ uint32_t group8_or(uint32_t v) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch: the kernels after the statistics pass are
+// launched so that their CTAs may start while the previous kernel drains;
+// each waits for its producer's results (all of its memory operations) before
+// reading them.  Every kernel lets its dependents launch once all of its CTAs
+// have started.  Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------
 // Segment staging: one bulk copy (cp.async.bulk, global -> shared, completion
 // on an mbarrier) of a CTA's 32 KB segment.  Thread t then reduces tile t from
 // shared memory, reading its eight float4 in the order j ^ (t & 7) so that the
@@ -768,15 +777,16 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
                                             uint64_t pol, float v[TILE]) {
     const uint32_t g0 = seg * SEG_ELEMS + tl * TILE;
     if (staged) {
+        const bool full = g0 + TILE <= P.vocab;   // only the row's last tile is partial
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const uint32_t jj = (uint32_t)j ^ (tl & 7u);
             const float4 q = sbuf[tl * 8 + jj];
             const uint32_t g = g0 + 4 * jj;
-            v[4 * j] = g < P.vocab ? q.x : NEG_INF;
-            v[4 * j + 1] = g + 1 < P.vocab ? q.y : NEG_INF;
-            v[4 * j + 2] = g + 2 < P.vocab ? q.z : NEG_INF;
-            v[4 * j + 3] = g + 3 < P.vocab ? q.w : NEG_INF;
+            v[4 * j] = full || g < P.vocab ? q.x : NEG_INF;
+            v[4 * j + 1] = full || g + 1 < P.vocab ? q.y : NEG_INF;
+            v[4 * j + 2] = full || g + 2 < P.vocab ? q.z : NEG_INF;
+            v[4 * j + 3] = full || g + 3 < P.vocab ? q.w : NEG_INF;
         }
     } else {
 #pragma unroll
@@ -814,6 +824,7 @@ __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, 
 // top-k floor, the tail-element histogram.  No cross-CTA step: the row
 // reduction is k1_rows.
 __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
+    grid_dep_launch();
     const uint32_t seg = blockIdx.x, row = blockIdx.y, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
@@ -854,12 +865,17 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
     float s = 0.0f, s2 = 0.0f;
     if (live && tm > NEG_INF) {
         const float tc = tm * c2;
+        if (P.tmode == TYP_OFF) {
 #pragma unroll
-        for (int k = 0; k < TILE; k++) {
-            const float r = fmaf(v[k], c2, -tc);
-            const float e = ex2_approx(r);
-            s += e;
-            s2 = fmaf(e, fmaxf(r, -1e30f), s2);   // 2^r r (0 for -inf logits)
+            for (int k = 0; k < TILE; k++) s += ex2_approx(fmaf(v[k], c2, -tc));
+        } else {
+#pragma unroll
+            for (int k = 0; k < TILE; k++) {
+                const float r = fmaf(v[k], c2, -tc);
+                const float e = ex2_approx(r);
+                s += e;
+                s2 = fmaf(e, fmaxf(r, -1e30f), s2);   // 2^r r (0 for -inf logits)
+            }
         }
     }
     uint32_t nonfin = 0;
@@ -951,6 +967,8 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
 //     bound on the mass below each grid point);
 //   min-p: ln(min_p) in log2 units, minus a margin.
 __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
+    grid_dep_launch();
+    grid_dep_wait();   // the statistics pass's results
     const uint32_t row = blockIdx.x, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
@@ -1071,11 +1089,21 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     uint32_t kcount = 0;   // tiles whose maximum is above the bin edge -(tid+1)/4
     if (k_floor) {
         const TileStat *ts = P.tstat + (size_t)hrow * P.ntiles_total;
-        for (uint32_t t = tid; t < P.ntiles_total; t += K12_THREADS) {
-            const float tm = ts[t].tmax;
-            const float d = __fsub_rn(tm, M);
-            const float x2 = (d == 0.0f) ? 0.0f : d * c2;
-            if (x2 > -64.0f) atomicAdd(&kh[min(KH_BINS - 1, (int)(-x2 * 4.0f))], 1u);
+        // all of a thread's tile maxima are requested before the first atomic
+        constexpr int KT = 16;
+        for (uint32_t t0 = 0; t0 < P.ntiles_total; t0 += KT * K12_THREADS) {
+            float tmv[KT];
+#pragma unroll
+            for (int k = 0; k < KT; k++) {
+                const uint32_t t = t0 + (uint32_t)k * K12_THREADS + tid;
+                tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+            }
+#pragma unroll
+            for (int k = 0; k < KT; k++) {
+                const float d = __fsub_rn(tmv[k], M);
+                const float x2 = (d == 0.0f) ? 0.0f : d * c2;
+                if (x2 > -64.0f) atomicAdd(&kh[min(KH_BINS - 1, (int)(-x2 * 4.0f))], 1u);
+            }
         }
         __syncthreads();
         // inclusive prefix over bins 0..tid (bins hold x2 in (-(b+1)/4, -b/4])
@@ -1200,16 +1228,10 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     constexpr int NW = K12_THREADS / 32;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
     const bool live = (uint32_t)tid < ntile;   // thread-per-tile phases below
+    grid_dep_launch();
     const float *x = P.logits + (size_t)row * P.ld;
     const float c2 = P.c2, T = P.T;
-    const RowInfo ri = P.rinfo[hrow];
-    const float M = ri.M;
     RowHdr *hdr = P.hdr + hrow;
-    if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
-    // the entropy pass: S exact, log2 S for the terms' exponents
-    const float S = TERM == TERM_H ? hdr->S_exact : 1.0f;
-    const double lnS = TERM == TERM_H ? log((double)S) : 0.0;
-    const float l2S = (float)(lnS * 1.4426950408889634);
 
     __shared__ uint32_t swin[256];
     __shared__ double wtmp_d[NW + 1];
@@ -1227,11 +1249,23 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     Comp *const carr2 = carr + SEG_TILES;
     __shared__ uint32_t wlist[SEG_TILES];
     __shared__ uint32_t nlist, nanflag;
-    // the segment's bulk copy overlaps the prologue; it is read once more
-    // only by the exact pass, so it need not stay in L2
+    // the segment's bulk copy overlaps the prologue (and, for the normaliser,
+    // the wait for the row reduction: it needs only the logits); it is read
+    // once more only by the exact pass, so it need not stay in L2
     const uint64_t pol = l2_policy_evict_first();
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
-    const bool bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, penalty_active(P) ? 1u : 0u, sbuf, &bar, pol);
+    const uint32_t pen = penalty_active(P) ? 1u : 0u;
+    bool bulk = false;
+    if (TERM == TERM_P) bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen, sbuf, &bar, pol);
+    grid_dep_wait();   // the row reduction (and, for the entropy, the normaliser's walk)
+    const RowInfo ri = P.rinfo[hrow];
+    const float M = ri.M;
+    if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
+    if (TERM == TERM_H) bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen, sbuf, &bar, pol);
+    // the entropy pass: S exact, log2 S for the terms' exponents
+    const float S = TERM == TERM_H ? hdr->S_exact : 1.0f;
+    const double lnS = TERM == TERM_H ? log((double)S) : 0.0;
+    const float l2S = (float)(lnS * 1.4426950408889634);
     const uint32_t nwin = load_window(P, row, swin);
     if (tid == 0) {
         nlist = 0;
@@ -1497,8 +1531,44 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const uint32_t tile0 = seg * SEG_TILES;
     Item *items = P.items + (size_t)hrow * P.ntiles_total + tile0;
     WTile *wpre = P.wpre + (size_t)hrow * P.ntiles_total + tile0;
+    // the common segment (past the row start): every tile SIMPLE in one
+    // binade with parity-free counts -- a single item, from a block sum
+    {
+        __shared__ int32_t lo0;
+        __shared__ uint32_t wsum_u[NW];
+        if (tid == 0) lo0 = rec[0].lo;
+        __syncthreads();
+        const TileRec rt = live ? rec[tid] : rec[0];
+        const bool uni = __syncthreads_and(rt.cls == CLS_SIMPLE && rt.lo == lo0 && rt.qlo.q0 == rt.qlo.q1) != 0;
+        if (uni) {
+            // a tile counts < 2^22.5, so 256 of them fit 32 bits
+            uint32_t q = live ? rt.qlo.q0 : 0u;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            if (lane == 0) wsum_u[warp] = q;
+            __syncthreads();
+            if (tid == 0) {
+                uint32_t tot = 0;
+                for (int w = 0; w < NW; w++) tot += wsum_u[w];
+                const uint32_t qa = min(tot, QSAT);
+                Item it;
+                it.kind = CLS_SIMPLE;
+                it.lo = lo0;
+                it.q[0] = qa;
+                it.q[1] = qa;
+                it.q[2] = 0u;
+                it.q[3] = 0u;
+                it.tile = tile0;
+                it.aux = NT;
+                items[0] = it;
+                hdr->seg_items[seg] = 1u;
+                hdr->seg_tile0[seg] = tile0;
+            }
+            return;
+        }
+    }
     // counts that depend on the entry parity (ties) need ordered composition;
-    // otherwise plain sums suffice and one warp builds the items
+    // otherwise plain sums suffice and the warps build the items in parallel
     const bool ties = __syncthreads_or(live && (rec[tid].qlo.q0 != rec[tid].qlo.q1 ||
                                                 rec[tid].qhi.q0 != rec[tid].qhi.q1)) != 0;
     if (!ties) {
@@ -1971,6 +2041,8 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t row = blockIdx.x;
     const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    grid_dep_launch();
+    grid_dep_wait();   // the main pass's results
     RowHdr *hdr = P.hdr + hrow;
     if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
     const float Sx = TERM == TERM_H ? hdr->S_exact : 1.0f;
@@ -2623,6 +2695,24 @@ extern "C" bs_status bs_argmax(const float *d_logits, size_t ld, uint32_t rows, 
     return cuda_status(cudaGetLastError());
 }
 
+// A launch that may overlap the previous kernel of the stream (the kernel
+// waits for it with griddepcontrol.wait before reading its results).
+template <typename... Args>
+static cudaError_t launch_dependent(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                    Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, uint32_t row0,
                                uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out,
                                void *stream) {
@@ -2700,23 +2790,25 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     // the entropy terms (profiled with the main pass | the final walk).
     cudaEvent_t *ev = nullptr;
     if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
+    // (with profiling on, the event records between the groups keep them
+    // from overlapping; the unprofiled step overlaps every boundary after the
+    // statistics pass)
+    const dim3 g12(s->nseg, rows);
     if (ev) cudaEventRecord(ev[0], st);
-    k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
-    k1_rows<<<rows, K12_THREADS, 0, st>>>(A);
+    k1_stats<<<g12, K12_THREADS, 0, st>>>(A);
+    cudaError_t e = launch_dependent(k1_rows, dim3(rows), dim3(K12_THREADS), 0, st, A);
     if (ev) cudaEventRecord(ev[1], st);
-    k2_main<TERM_P><<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+    if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_P>, g12, dim3(K12_THREADS), 0, st, A);
     if (A.tmode != TYP_OFF) {
-        kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
-        k2_main<TERM_H><<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(A);
+        if (e == cudaSuccess) e = launch_dependent(kernel_b<TERM_P>, dim3(rows), dim3(KB_THREADS), s->smem_b, st, B);
+        if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_H>, g12, dim3(K12_THREADS), 0, st, A);
     }
     if (ev) cudaEventRecord(ev[2], st);
-    if (A.tmode != TYP_OFF) {
-        kernel_b<TERM_H><<<rows, KB_THREADS, s->smem_b, st>>>(B);
-    } else {
-        kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
-    }
+    if (e == cudaSuccess)
+        e = launch_dependent(A.tmode != TYP_OFF ? kernel_b<TERM_H> : kernel_b<TERM_P>, dim3(rows), dim3(KB_THREADS),
+                             s->smem_b, st, B);
     if (ev) cudaEventRecord(ev[3], st);
-    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
     return cuda_status(e);
 }
