@@ -2088,12 +2088,14 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         for (uint32_t j = tid; j < win; j += KB_THREADS) swin[j] = P.prev[(size_t)row * P.n_prev + start + j];
         nwin = win;
     }
+    // the stored exact terms (their loads overlap the item-table set-up below)
     const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
     for (uint32_t i = tid; i < n_wc * TILE; i += KB_THREADS) wcs[i] = wcg[i];
     const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
     unsigned long long *gk1 = gk0 + P.cand_stride;
     uint32_t npow = 1;
+    while (npow < n_cand) npow <<= 1;
     if (tid == 0) {
         walk_flags = 0;
         walk_items = 0;
@@ -2102,30 +2104,6 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         S_sh = __int_as_float(0x7fc00000);
     }
     __syncthreads();
-    uint32_t nz = 0;
-    if (TERM == TERM_H) {
-        // no candidate keys: the typical tail builds its own list
-    } else if (!big) {
-        while (npow < n_cand) npow <<= 1;
-        for (uint32_t i = tid; i < npow; i += KB_THREADS) {
-            unsigned long long k = ~0ull;
-            if (i < n_cand) {
-                const Candidate c = cg_[i];
-                const float p = prob_unnorm(c.v, M, P.T);
-                k = cand_key(c.idx, p);
-                nz += p > 0.0f ? 0u : 1u;
-            }
-            skeys[i] = k;
-        }
-    } else {
-        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) {
-            const Candidate c = cg_[i];
-            const float p = prob_unnorm(c.v, M, P.T);
-            gk0[i] = cand_key(c.idx, p);
-            nz += p > 0.0f ? 0u : 1u;
-        }
-    }
-    if (nz) atomicAdd(&n_zero, nz);
     // prefix tables of the WINDOW items held in shared memory (offsets by a
     // block scan over the item slots, two per thread; tables that do not fit
     // stay in global memory)
@@ -2172,7 +2150,6 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         }
     }
     __syncthreads();
-    const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
 
     if (warp == 0) {
         // ---- the exact walk of the sequential f32 sum (skipped for a NaN
@@ -2295,8 +2272,21 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         }
         }
     } else if (TERM == TERM_P && !big) {
-        // ---- candidate sort in shared memory: ascending key ----
+        // ---- candidate keys (exact p), then the sort in shared memory,
+        // ascending key, while warp 0 walks ----
         const int t2 = tid - 32, nthr = KB_THREADS - 32;
+        uint32_t nz = 0;
+        for (uint32_t i = t2; i < npow; i += nthr) {
+            unsigned long long k = ~0ull;
+            if (i < n_cand) {
+                const Candidate c = cg_[i];
+                const float p = prob_unnorm(c.v, M, P.T);
+                k = cand_key(c.idx, p);
+                nz += p > 0.0f ? 0u : 1u;
+            }
+            skeys[i] = k;
+        }
+        if (nz) atomicAdd(&n_zero, nz);
         for (uint32_t size = 2; size <= npow; size <<= 1) {
             for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
                 asm volatile("bar.sync 1, %0;" ::"r"(nthr));
@@ -2320,10 +2310,19 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         return;
     }
 
-    // large candidate sets: stable radix sort in global memory (whole CTA)
+    // large candidate sets: keys, then a stable radix sort in global memory
+    // (whole CTA)
     unsigned long long *keys = skeys;
     float *probs = sprobs;
     if (big) {
+        uint32_t nz = 0;
+        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) {
+            const Candidate c = cg_[i];
+            const float p = prob_unnorm(c.v, M, P.T);
+            gk0[i] = cand_key(c.idx, p);
+            nz += p > 0.0f ? 0u : 1u;
+        }
+        if (nz) atomicAdd(&n_zero, nz);
         __syncthreads();
         uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // 16 * KB_THREADS words
         keys = cta_radix_sort(gk0, gk1, n_cand, cnt, red2);
@@ -2331,6 +2330,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         __syncthreads();
     }
 
+    const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
     const float S = S_sh;
     const bool nan_row = (flags0 & RF_NAN) != 0;
     __shared__ uint32_t rawarg_sh;
