@@ -967,8 +967,8 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
 //     bound on the mass below each grid point);
 //   min-p: ln(min_p) in log2 units, minus a margin.
 __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
-    grid_dep_launch();
-    grid_dep_wait();   // the statistics pass's results
+    grid_dep_wait();     // the statistics pass's results
+    grid_dep_launch();   // after the wait: the main pass may read the statistics before its own wait
     const uint32_t row = blockIdx.x, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
@@ -1257,6 +1257,11 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const uint32_t pen = penalty_active(P) ? 1u : 0u;
     bool bulk = false;
     if (TERM == TERM_P) bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen, sbuf, &bar, pol);
+    // the tile statistics come from the statistics pass, complete before this
+    // grid could start (the row reduction lets it launch only after its own
+    // wait): load them before waiting for the row reduction
+    TileStat ts_pre = TileStat{NEG_INF, 0.0f, 0.0f, 0.0f};
+    if (live) ts_pre = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
     grid_dep_wait();   // the row reduction (and, for the entropy, the normaliser's walk)
     const RowInfo ri = P.rinfo[hrow];
     const float M = ri.M;
@@ -1283,7 +1288,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         double ct = 0.0;
         float tmax = NEG_INF;
         if (live) {
-            const TileStat ts = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
+            const TileStat ts = ts_pre;
             tmax = ts.tmax;
             if (ts.tmax > NEG_INF) {
                 const float o = (ts.tmax - M) * c2;
