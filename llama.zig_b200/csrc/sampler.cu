@@ -426,6 +426,7 @@ constexpr double TB_H_ABS = 1e-3;
 constexpr float TB_MASS_REL = 0.01f;
 constexpr float TB_MASS_ABS = 0.005f;
 constexpr float TB_D_PAD = 0.01f;
+constexpr float TB_OCTAVES = 12.0f;   // band histogram depth below each segment maximum
 
 // Relative error bound, for the main loop's certificate, between
 // y = ex2.approx(min(fma(d, c2, K), 17.5)) and the exact p / u_lo, where
@@ -911,13 +912,17 @@ __global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
         ss = (double)s * et;
         ss2 = et * ((double)s2 + (double)o * (double)s);
     }
-    // typical-p alone: mass per quarter-octave below the segment maximum
-    if (t_band && sm > NEG_INF && live) {
+    // typical-p alone: mass per quarter-octave below the segment maximum.
+    // The band needs only a lower bound of mass, so logits more than
+    // TB_OCTAVES below the segment maximum are left out (their mass is at
+    // most 2^-TB_OCTAVES of the maximum's each); a tile whose maximum is that
+    // low is skipped whole
+    if (t_band && sm > NEG_INF && live && (tm - sm) * c2 > -TB_OCTAVES) {
         const float sc = sm * c2;
 #pragma unroll
         for (int k = 0; k < TILE; k++) {
             const float xr = fmaf(v[k], c2, -sc);
-            if (xr > -64.0f) atomicAdd(&th[min(KH_BINS - 1, (int)(-xr * 4.0f))], ex2_approx(xr));
+            if (xr > -TB_OCTAVES) atomicAdd(&th[min(KH_BINS - 1, (int)(-xr * 4.0f))], ex2_approx(xr));
         }
     }
     // top-p without a top-k floor: tail-element histogram relative to the
