@@ -1914,6 +1914,55 @@ __device__ unsigned long long *cta_radix_sort(unsigned long long *a, unsigned lo
     return a;
 }
 
+// Sequential f32 scans by one thread over long lists (top-p and cum_typ,
+// kept mass, draw walk).  The adds stay strictly in list order; only the
+// loads are issued eight ahead, so the loop runs at the add chain's latency
+// instead of a load round trip per element.  `get(i)` returns element i.
+template <typename Get>
+__device__ __forceinline__ uint32_t seq_first_exceed(Get get, uint32_t n, float thr, float &cum) {
+    for (uint32_t i0 = 0; i0 < n; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = i0 + k < n ? get(i0 + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (i0 + k >= n) return n;
+            cum = __fadd_rn(cum, v[k]);
+            if (cum > thr) return i0 + k;
+        }
+    }
+    return n;
+}
+template <typename Get>
+__device__ __forceinline__ float seq_sum(Get get, uint32_t n) {
+    float t = 0.0f;
+    for (uint32_t i0 = 0; i0 < n; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = i0 + k < n ? get(i0 + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (i0 + k < n) t = __fadd_rn(t, v[k]);
+    }
+    return t;
+}
+// r -= a[i] in order; the first i with r <= 0, or n.
+template <typename Get>
+__device__ __forceinline__ uint32_t seq_draw(Get get, uint32_t n, float r) {
+    for (uint32_t i0 = 0; i0 < n; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = i0 + k < n ? get(i0 + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (i0 + k >= n) return n;
+            r = __fsub_rn(r, v[k]);
+            if (r <= 0.0f) return i0 + k;
+        }
+    }
+    return n;
+}
+
 // Typical-p (sampler.zig:128-154) and the draw (:156-168), after the entropy
 // walk.  The list is the selected set from the normaliser pass (TYP_SELECTED:
 // (index, P) pairs) or the band candidates of the entropy pass (TYP_BAND:
@@ -1967,15 +2016,8 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
     if (tid == 0) {
         uint32_t nk = n, st = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
         float cum = 0.0f;
-        bool crossed = false;
-        for (uint32_t i = 0; i < n; i++) {
-            cum = __fadd_rn(cum, pd[i]);
-            if (cum > P.typical_p) {
-                nk = i;
-                crossed = true;
-                break;
-            }
-        }
+        nk = seq_first_exceed([&](uint32_t i) { return pd[i]; }, n, P.typical_p, cum);
+        const bool crossed = nk < n;
         if (mode == TYP_BAND && st == ROW_OK) {
             // the band held every token with approximate dev <= dband, where
             // the approximation used H_raw: tokens with exact dev up to
@@ -2011,18 +2053,14 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
     uint64_t *rng = P.rng + (size_t)hrow * 4;
     uint64_t s4[4] = {rng[0], rng[1], rng[2], rng[3]};
     if (status == ROW_OK) {
-        for (uint32_t j = 0; j < nk; j++) total = __fadd_rn(total, key_p(keys[j]));
+        total = seq_sum([&](uint32_t j) { return key_p(keys[j]); }, nk);
         if (total > 0.0f) {   // else indices[0] without a draw (sampler.zig:160)
             u = rng_float(s4);
-            float r = __fmul_rn(u, total);
+            const uint32_t j = seq_draw([&](uint32_t i) { return key_p(keys[i]); }, nk, __fmul_rn(u, total));
             path = 4;
-            for (uint32_t j = 0; j < nk; j++) {
-                r = __fsub_rn(r, key_p(keys[j]));
-                if (r <= 0.0f) {
-                    token = (uint32_t)keys[j];
-                    path = 3;
-                    break;
-                }
+            if (j < nk) {
+                token = (uint32_t)keys[j];
+                path = 3;
             }
         }
         rng[0] = s4[0]; rng[1] = s4[1]; rng[2] = s4[2]; rng[3] = s4[3];
@@ -2367,6 +2405,16 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     // exact probs in sorted order (sampler.zig:90)
     for (uint32_t i = tid; i < n_pos; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
     __syncthreads();
+    // distinct p can round to equal probs; the stable sort then wants index
+    // order among them.  Rare: the block checks adjacent pairs first
+    bool tie_fix = false;
+    {
+        const uint32_t *ix = reinterpret_cast<const uint32_t *>(keys);
+        bool mine = false;
+        for (uint32_t i = tid + 1; i < n_pos; i += KB_THREADS)
+            mine |= probs[i] == probs[i - 1] && ix[2 * (i - 1)] > ix[2 * i];
+        tie_fix = __syncthreads_or(mine) != 0;
+    }
     if (tid != 0) return;
 
     uint32_t status = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
@@ -2397,7 +2445,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         // idxs[2*i] aliases the low word of keys[i]
         uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);
         // ties: equal probs from distinct p keep index order (stable sort)
-        for (uint32_t i = 1; i < n_pos; i++) {
+        for (uint32_t i = 1; tie_fix && i < n_pos; i++) {
             if (probs[i] == probs[i - 1] && idxs[2 * (i - 1)] > idxs[2 * i]) {
                 uint32_t j = i;
                 const uint32_t id = idxs[2 * j];
@@ -2421,13 +2469,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         // top-p (sampler.zig:111-118): the crossing token is deselected too
         if (P.top_p > 0.0f && P.top_p < 1.0f) {
             float cum = 0.0f;
-            for (uint32_t j = 0; j < n_sel; j++) {
-                cum = __fadd_rn(cum, probs[j]);
-                if (cum > P.top_p) {
-                    n_sel = j;
-                    break;
-                }
-            }
+            n_sel = seq_first_exceed([&](uint32_t j) { return probs[j]; }, n_sel, P.top_p, cum);
         }
         // min-p (sampler.zig:120-126) against probs[indices[0]]
         if (P.min_p > 0.0f && n_pos > 0) {
@@ -2454,23 +2496,19 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             hdr->top_idx = n_pos > 0 ? idxs[0] : 0u;
         } else {
             // kept mass in sorted order (sampler.zig:156-159)
-            for (uint32_t j = 0; j < n_sel; j++) total = __fadd_rn(total, probs[j]);
+            total = seq_sum([&](uint32_t j) { return probs[j]; }, n_sel);
             n_kept = n_sel;
             if (!(total > 0.0f)) {
                 token = n_pos > 0 ? idxs[0] : 0u;  // sampler.zig:160
                 path = 2;
             } else {
                 u = rng_float(s4);
-                float r = __fmul_rn(u, total);
+                const uint32_t j = seq_draw([&](uint32_t i) { return probs[i]; }, n_sel, __fmul_rn(u, total));
                 token = idxs[0];
                 path = 4;
-                for (uint32_t j = 0; j < n_sel; j++) {
-                    r = __fsub_rn(r, probs[j]);
-                    if (r <= 0.0f) {
-                        token = idxs[2 * j];
-                        path = 3;
-                        break;
-                    }
+                if (j < n_sel) {
+                    token = idxs[2 * j];
+                    path = 3;
                 }
             }
         }
