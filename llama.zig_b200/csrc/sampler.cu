@@ -1226,9 +1226,10 @@ enum : int { TERM_P = 0, TERM_H = 1 };
 
 template <int TERM>
 __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
-    // rows in reverse order: the rows K1 streamed last are still in L2; the
-    // first segments (most of the exact-pass tiles) start first
-    const uint32_t seg = blockIdx.x, row = P.rows - 1 - blockIdx.y, hrow = P.row0 + row;
+    // segment-major order over a 1-D grid: every row's segment 0 first (the
+    // row start holds most exact-pass tiles, so those CTAs live several times
+    // longer), the last segments last, so the kernel's tail is short CTAs
+    const uint32_t seg = blockIdx.x / P.rows, row = blockIdx.x - seg * P.rows, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
@@ -2841,15 +2842,15 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     // (with profiling on, the event records between the groups keep them
     // from overlapping; the unprofiled step overlaps every boundary after the
     // statistics pass)
-    const dim3 g12(s->nseg, rows);
+    const dim3 g12(s->nseg, rows), g2(s->nseg * rows);
     if (ev) cudaEventRecord(ev[0], st);
     k1_stats<<<g12, K12_THREADS, 0, st>>>(A);
     cudaError_t e = launch_dependent(k1_rows, dim3(rows), dim3(K12_THREADS), 0, st, A);
     if (ev) cudaEventRecord(ev[1], st);
-    if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_P>, g12, dim3(K12_THREADS), 0, st, A);
+    if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_P>, g2, dim3(K12_THREADS), 0, st, A);
     if (A.tmode != TYP_OFF) {
         if (e == cudaSuccess) e = launch_dependent(kernel_b<TERM_P>, dim3(rows), dim3(KB_THREADS), s->smem_b, st, B);
-        if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_H>, g12, dim3(K12_THREADS), 0, st, A);
+        if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_H>, g2, dim3(K12_THREADS), 0, st, A);
     }
     if (ev) cudaEventRecord(ev[2], st);
     if (e == cudaSuccess)
