@@ -2215,101 +2215,114 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             st = state_of(seq_add32_smem(float_of(st), tilep));
             __syncwarp();
         };
+        // everything but the common case: a WINDOW crossing, a stored or
+        // recomputed tile, a running sum outside the item's binades
+        auto slow_item = [&](const Item &it, uint32_t wo) {
+            const uint32_t ntl = it.kind == CLS_COMPLEX ? 1u : min(it.aux, P.ntiles_total - it.tile);
+            // 0 applied, 1 window crossing, 2 recompute every tile, 3 stored p
+            int action = 2;
+            const uint32_t par = st.m & 1u;
+            if (st.e == it.lo) {
+                const uint32_t q = par ? it.q[1] : it.q[0];
+                if (st.m + q < QLIM && q < QSAT) {
+                    st.m += q;
+                    action = 0;
+                } else if (it.kind == CLS_WINDOW) {
+                    action = 1;
+                }
+            } else if (it.kind == CLS_WINDOW && st.e == it.lo + 1) {
+                const uint32_t q = par ? it.q[3] : it.q[2];
+                if (st.m + q < QLIM && q < QSAT) {
+                    st.m += q;
+                    action = 0;
+                }
+            }
+            if (action == 2 && it.kind == CLS_COMPLEX && it.aux < n_wc) action = 3;
+            if (action == 0) return;
+            if (action == 3) {   // stored exact p
+                st = state_of(seq_add32_smem(float_of(st), wcs + it.aux * TILE));
+                return;
+            }
+            uint32_t from = 0;
+            if (action == 1) {
+                // the running sum leaves binade lo inside this stretch: first
+                // tile c whose prefix count reaches 2^24, from the stretch's
+                // prefix table (shared memory when it was gathered)
+                const WTile *wp = wo != 0xFFFFFFFFu ? wpool + wo : wrow + it.tile;
+                const uint32_t pi = par;
+                uint32_t lo_i = 0, hi_i = ntl - 1;
+                while (lo_i < hi_i) {
+                    const uint32_t step = (hi_i - lo_i + 32) / 32;
+                    const uint32_t pos = lo_i + lane * step;
+                    bool pr = false;
+                    if (pos <= hi_i) {
+                        const Comp c = wp[pos].pre_lo;
+                        pr = st.m + (pi ? c.q1 : c.q0) >= QLIM;
+                    }
+                    const uint32_t mask = __ballot_sync(0xffffffffu, pr);
+                    if (mask == 0) {
+                        lo_i = lo_i + 31 * step + 1;
+                    } else {
+                        const uint32_t f = __ffs(mask) - 1;
+                        hi_i = lo_i + f * step;
+                        if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
+                    }
+                }
+                const uint32_t c = lo_i;
+                if (c > 0) {
+                    const Comp pc = wp[c - 1].pre_lo;
+                    st.m += pi ? pc.q1 : pc.q0;
+                }
+                const uint32_t sl = wp[c].slot;
+                if (sl < n_wc) {   // stored exact p
+                    st = state_of(seq_add32_smem(float_of(st), wcs + sl * TILE));
+                } else {
+                    add_tile(it.tile + c);
+                }
+                from = c + 1;
+                if (from < ntl && st.e == it.lo + 1) {
+                    const Comp sh = wp[from].suf_hi;
+                    const uint32_t q = (st.m & 1u) ? sh.q1 : sh.q0;
+                    if (st.m + q < QLIM && q < QSAT) {
+                        st.m += q;
+                        from = ntl;
+                    }
+                }
+            }
+            if (from < ntl) {
+                wflags |= RF_SLOW_WALK;
+                nslow += ntl - from;
+                for (uint32_t tt = from; tt < ntl; tt++) add_tile(it.tile + tt);
+            }
+        };
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
             const uint32_t nit = s_nit[sgi];
-            const Item *ig = ib + sgi * SEG_TILES;
             nitems_all += nit;
-            const bool in_smem = nit <= spec;
-            const uint32_t chunk = in_smem ? max(nit, 1u) : (uint32_t)ITEM_CHUNK;
-            for (uint32_t i0 = 0; i0 < nit; i0 += chunk) {
-                const uint32_t nc = min(chunk, nit - i0);
+            if (nit <= spec) {
+                // the common case stays in this loop: the running sum is in
+                // the item's binade and stays there (a SIMPLE stretch, or a
+                // WINDOW stretch that does not cross)
                 const Item *src = sall + sgi * spec;
-                if (!in_smem) {
+                for (uint32_t j = 0; j < nit; j++) {
+                    const Item it = src[j];
+                    if (st.e == it.lo) {
+                        const uint32_t q = (st.m & 1u) ? it.q[1] : it.q[0];
+                        if (st.m + q < QLIM && q < QSAT) {
+                            st.m += q;
+                            continue;
+                        }
+                    }
+                    slow_item(it, woff[sgi * spec + j]);
+                }
+            } else {
+                // more items than the shared copy holds: chunks from global memory
+                const Item *ig = ib + sgi * SEG_TILES;
+                for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
+                    const uint32_t nc = min((uint32_t)ITEM_CHUNK, nit - i0);
                     __syncwarp();
                     for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ig[i0 + j];
                     __syncwarp();
-                    src = sitems;
-                }
-                for (uint32_t j = 0; j < nc; j++) {
-                    const Item it = src[j];
-                    const uint32_t wo = in_smem ? woff[sgi * spec + j] : 0xFFFFFFFFu;
-                    const uint32_t ntl = it.kind == CLS_COMPLEX ? 1u : min(it.aux, P.ntiles_total - it.tile);
-                    // 0 applied, 1 window crossing, 2 recompute every tile, 3 stored p
-                    int action = 2;
-                    const uint32_t par = st.m & 1u;
-                    if (st.e == it.lo) {
-                        const uint32_t q = par ? it.q[1] : it.q[0];
-                        if (st.m + q < QLIM && q < QSAT) {
-                            st.m += q;
-                            action = 0;
-                        } else if (it.kind == CLS_WINDOW) {
-                            action = 1;
-                        }
-                    } else if (it.kind == CLS_WINDOW && st.e == it.lo + 1) {
-                        const uint32_t q = par ? it.q[3] : it.q[2];
-                        if (st.m + q < QLIM && q < QSAT) {
-                            st.m += q;
-                            action = 0;
-                        }
-                    }
-                    if (action == 2 && it.kind == CLS_COMPLEX && it.aux < n_wc) action = 3;
-                    if (action == 0) continue;
-                    if (action == 3) {   // stored exact p
-                        st = state_of(seq_add32_smem(float_of(st), wcs + it.aux * TILE));
-                        continue;
-                    }
-                    uint32_t from = 0;
-                    if (action == 1) {
-                        // the running sum leaves binade lo inside this stretch:
-                        // first tile c whose prefix count reaches 2^24
-                        // the stretch's prefix table (shared memory when it
-                        // was gathered)
-                        const WTile *wp = wo != 0xFFFFFFFFu ? wpool + wo : wrow + it.tile;
-                        const uint32_t pi = par;
-                        uint32_t lo_i = 0, hi_i = ntl - 1;
-                        while (lo_i < hi_i) {
-                            const uint32_t step = (hi_i - lo_i + 32) / 32;
-                            const uint32_t pos = lo_i + lane * step;
-                            bool pr = false;
-                            if (pos <= hi_i) {
-                                const Comp c = wp[pos].pre_lo;
-                                pr = st.m + (pi ? c.q1 : c.q0) >= QLIM;
-                            }
-                            const uint32_t mask = __ballot_sync(0xffffffffu, pr);
-                            if (mask == 0) {
-                                lo_i = lo_i + 31 * step + 1;
-                            } else {
-                                const uint32_t f = __ffs(mask) - 1;
-                                hi_i = lo_i + f * step;
-                                if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
-                            }
-                        }
-                        const uint32_t c = lo_i;
-                        if (c > 0) {
-                            const Comp pc = wp[c - 1].pre_lo;
-                            st.m += pi ? pc.q1 : pc.q0;
-                        }
-                        const uint32_t sl = wp[c].slot;
-                        if (sl < n_wc) {   // stored exact p
-                            st = state_of(seq_add32_smem(float_of(st), wcs + sl * TILE));
-                        } else {
-                            add_tile(it.tile + c);
-                        }
-                        from = c + 1;
-                        if (from < ntl && st.e == it.lo + 1) {
-                            const Comp sh = wp[from].suf_hi;
-                            const uint32_t q = (st.m & 1u) ? sh.q1 : sh.q0;
-                            if (st.m + q < QLIM && q < QSAT) {
-                                st.m += q;
-                                from = ntl;
-                            }
-                        }
-                    }
-                    if (from < ntl) {
-                        wflags |= RF_SLOW_WALK;
-                        nslow += ntl - from;
-                        for (uint32_t tt = from; tt < ntl; tt++) add_tile(it.tile + tt);
-                    }
+                    for (uint32_t j = 0; j < nc; j++) slow_item(sitems[j], 0xFFFFFFFFu);
                 }
             }
         }
