@@ -187,6 +187,19 @@ __device__ __forceinline__ float seq_add32_smem(float s, const float *p) {
     return s;
 }
 
+// The composite of a warp's 32 lane composites in lane order.  Without ties
+// (every count parity-free) and with every count below 2^24, it is a plain
+// sum (one warp reduction, below 2^29); otherwise the ordered composition.
+// The result is valid in lane 0.
+__device__ __forceinline__ Comp warp_comp_reduce(Comp c);
+__device__ __forceinline__ Comp warp_tile_comp(Comp c) {
+    if (__all_sync(0xffffffffu, c.q0 == c.q1 && c.q0 < QLIM)) {
+        const uint32_t q = __reduce_add_sync(0xffffffffu, c.q0);
+        return Comp{q, q};
+    }
+    return warp_comp_reduce(c);
+}
+
 // Ordered reduction of lane composites (lane 0 = first element).  Result in lane 0.
 __device__ __forceinline__ Comp warp_comp_reduce(Comp c) {
     const int lane = threadIdx.x & 31;
@@ -1521,8 +1534,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
             }
         }
         const float p = g < P.vocab ? (TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S)) : 0.0f;
-        r.qlo = warp_comp_reduce(elem_comp(p, r.lo));
-        if (r.cls == CLS_WINDOW) r.qhi = warp_comp_reduce(elem_comp(p, r.lo + 1));
+        r.qlo = warp_tile_comp(elem_comp(p, r.lo));
+        if (r.cls == CLS_WINDOW) r.qhi = warp_tile_comp(elem_comp(p, r.lo + 1));
         if (r.cls != CLS_SIMPLE) {   // several binades: the walker may need the exact p
             uint32_t slot = 0;
             if (lane == 0) slot = atomicAdd(&hdr->n_wc, 1u);
