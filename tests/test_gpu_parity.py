@@ -274,3 +274,22 @@ def test_typical_with_other_filters(gpu_pkg, orc, extra):
     w = gpu_pkg.workloads.WORKLOADS["c2"]
     x = gpu_pkg.workloads.make_logits(w, rows=8, vocab=50000)
     _typical_case(gpu_pkg, orc, w.config(**extra), x, w.seeds(8), str(extra))
+
+
+def test_config0_thousand_sequential_steps(gpu_pkg, orc):
+    # config 0 as the CLI runs it: B=1, 1000 steps of fresh logits, one
+    # persistent RNG state; every token and the final state bit-exact
+    w = gpu_pkg.workloads.WORKLOADS["c0"]
+    c = w.config()
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=1, vocab=w.vocab, seeds=w.seeds(1))
+    oc = orc.make_config(**c)
+    states = None
+    d = torch.empty((1, w.vocab), dtype=torch.float32, device="cuda")
+    for step in range(w.steps):
+        x = gpu_pkg.workloads.make_logits(w, step=step, rows=1)
+        d.copy_(torch.from_numpy(x))
+        got = int(s.sample(d).cpu().numpy()[0])
+        exp, _, states = orc.sample_batch(oc, x, seeds=w.seeds(1) if states is None else None, states=states)
+        assert got == int(exp[0]), f"step {step}: gpu {got} ref {int(exp[0])}"
+    assert np.array_equal(s.rng_state, states)
+    s.close()
