@@ -730,21 +730,30 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
-// Waits for phase `parity` of the barrier; false after `limit` polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit) {
-    for (uint32_t i = 0; i < limit; i++) {
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits for phase `parity` of the barrier; false once `limit_ns` have passed
+// (or after 2^20 tries).  Each try lets the hardware suspend the thread until
+// the phase completes or a microsecond passes, so waiting threads do not
+// spin on the issue slots the SM's other CTAs need.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < (1u << 20); i++) {
         uint32_t done;
         asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
             : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
             : "memory");
         if (done) return true;
-        if (i > 64) __nanosleep(256);
+        if (global_ns() - t0 > limit_ns) return false;
     }
     return false;
 }
-constexpr uint32_t MBAR_POLL_LIMIT = 1u << 22;   // about a second of polling
+constexpr uint64_t MBAR_WAIT_NS = 1000000000ull;   // one second
 
 // The segment can be bulk copied: no penalised ids (they are applied while
 // loading), a 16-byte aligned start and a whole number of 16-byte chunks.
@@ -770,11 +779,11 @@ __device__ __forceinline__ bool seg_issue(const K12Params &P, const float *xs, u
 // CTA's shared memory.  Returns whether the shared copy is usable
 // (block-uniform).
 __device__ __forceinline__ bool seg_wait(const K12Params &P, uint64_t *bar) {
-    const bool ok = mbar_wait(bar, 0u, MBAR_POLL_LIMIT);
+    const bool ok = mbar_wait(bar, 0u, MBAR_WAIT_NS);
     const bool all = __syncthreads_and(ok) != 0;
     if (!all && threadIdx.x == 0) {
         atomicOr(P.kerr, 1u);
-        mbar_wait(bar, 0u, MBAR_POLL_LIMIT);
+        mbar_wait(bar, 0u, MBAR_WAIT_NS);
     }
     return all;
 }
@@ -790,17 +799,25 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
                                             const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
                                             uint64_t pol, float v[TILE]) {
     const uint32_t g0 = seg * SEG_ELEMS + tl * TILE;
-    if (staged) {
-        const bool full = g0 + TILE <= P.vocab;   // only the row's last tile is partial
+    if (staged && g0 + TILE <= P.vocab) {   // every tile but the row's last
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float4 q = sbuf[tl * 8 + ((uint32_t)j ^ (tl & 7u))];
+            v[4 * j] = q.x;
+            v[4 * j + 1] = q.y;
+            v[4 * j + 2] = q.z;
+            v[4 * j + 3] = q.w;
+        }
+    } else if (staged) {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const uint32_t jj = (uint32_t)j ^ (tl & 7u);
             const float4 q = sbuf[tl * 8 + jj];
             const uint32_t g = g0 + 4 * jj;
-            v[4 * j] = full || g < P.vocab ? q.x : NEG_INF;
-            v[4 * j + 1] = full || g + 1 < P.vocab ? q.y : NEG_INF;
-            v[4 * j + 2] = full || g + 2 < P.vocab ? q.z : NEG_INF;
-            v[4 * j + 3] = full || g + 3 < P.vocab ? q.w : NEG_INF;
+            v[4 * j] = g < P.vocab ? q.x : NEG_INF;
+            v[4 * j + 1] = g + 1 < P.vocab ? q.y : NEG_INF;
+            v[4 * j + 2] = g + 2 < P.vocab ? q.z : NEG_INF;
+            v[4 * j + 3] = g + 3 < P.vocab ? q.w : NEG_INF;
         }
     } else {
 #pragma unroll
