@@ -755,6 +755,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
 }
 constexpr uint64_t MBAR_WAIT_NS = 1000000000ull;   // one second
 
+// Per-thread asynchronous global -> shared copies (cp.async).  A thread
+// issues all of its copies and then waits once, so a table gathered from many
+// places costs one memory latency instead of one per load/store pair.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // The segment can be bulk copied: no penalised ids (they are applied while
 // loading), a 16-byte aligned start and a whole number of 16-byte chunks.
 __device__ __forceinline__ bool seg_bulk_ok(const K12Params &P, const float *xs, uint32_t n, uint32_t nwin) {
@@ -2127,9 +2141,9 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const float Sx = TERM == TERM_H ? hdr->S_exact : 1.0f;
 
     __shared__ Item sitems[ITEM_CHUNK];
-    __shared__ Item sall[ITEM_SMEM];             // the first `spec` items of every segment
+    __shared__ __align__(16) Item sall[ITEM_SMEM];   // the first `spec` items of every segment
     __shared__ uint32_t woff[ITEM_SMEM];         // WINDOW item: its prefix table in wpool, or ~0u
-    __shared__ WTile wpool[WPOOL];
+    __shared__ __align__(8) WTile wpool[WPOOL];
     __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1];
     __shared__ __align__(16) float tilep[TILE];   // a recomputed tile's p, for the walker
     __shared__ uint32_t swin[256];
@@ -2147,29 +2161,32 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     const uint32_t n_wc = min(hdr->n_wc, (uint32_t)WC_CAP);
     const bool big = TERM == TERM_P && n_cand > (uint32_t)CAND_SMEM;
 
-    // the walk's inputs in shared memory.  Segment s's items start at tile
+    // the walk's inputs in shared memory, gathered with asynchronous copies
+    // (one wait for all of them).  Segment s's items start at tile
     // s * SEG_TILES; its first `spec` items are fetched speculatively in the
     // same round trip as their count
     const uint32_t nseg = min((P.ntiles_total + SEG_TILES - 1) / SEG_TILES, (uint32_t)MAX_SEG);
     const uint32_t spec = ITEM_SMEM / nseg;
     const Item *ib = P.items + (size_t)hrow * P.ntiles_total;
-    if ((uint32_t)tid < nseg) s_nit[tid] = min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES));
-    for (uint32_t i = tid; i < nseg * spec; i += KB_THREADS) {
-        const uint32_t sg = i / spec, j = i - sg * spec;
-        if (sg * SEG_TILES + j < P.ntiles_total && j < (uint32_t)SEG_TILES) sall[i] = ib[sg * SEG_TILES + j];
+    static_assert(sizeof(Item) == 32, "an item is two 16-byte chunks");
+    for (uint32_t i = tid; i < 2 * nseg * spec; i += KB_THREADS) {
+        const uint32_t it = i >> 1, sg = it / spec, j = it - sg * spec;
+        if (sg * SEG_TILES + j < P.ntiles_total && j < (uint32_t)SEG_TILES)
+            cp_async16(reinterpret_cast<uint4 *>(sall) + i, reinterpret_cast<const uint4 *>(ib + sg * SEG_TILES + j) + (i & 1u));
     }
-
+    // the stored exact terms (rows of WC_CAP * TILE floats, 16-byte aligned)
+    const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
+    for (uint32_t i = tid; i < n_wc * (TILE / 4); i += KB_THREADS) cp_async16(wcs + 4 * i, wcg + 4 * i);
     // penalty window (for the recompute path)
     uint32_t nwin = 0;
     if (P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0) {
         const uint32_t win = min(min(P.n_prev, P.rep_window), 256u);
         const uint32_t start = P.n_prev - win;
-        for (uint32_t j = tid; j < win; j += KB_THREADS) swin[j] = P.prev[(size_t)row * P.n_prev + start + j];
+        for (uint32_t j = tid; j < win; j += KB_THREADS) cp_async4(swin + j, P.prev + (size_t)row * P.n_prev + start + j);
         nwin = win;
     }
-    // the stored exact terms (their loads overlap the item-table set-up below)
-    const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
-    for (uint32_t i = tid; i < n_wc * TILE; i += KB_THREADS) wcs[i] = wcg[i];
+    if ((uint32_t)tid < nseg) s_nit[tid] = min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES));
+    cp_async_wait_all();
     const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
     unsigned long long *gk1 = gk0 + P.cand_stride;
@@ -2218,15 +2235,19 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             off += len[h];
         }
         __syncthreads();
-        // one warp per item slot copies its table
+        // one warp per item slot issues its table's copies (8-byte chunks)
+        static_assert(sizeof(WTile) == 24, "a prefix-table entry is three 8-byte chunks");
         const WTile *wrow_g = P.wpre + (size_t)hrow * P.ntiles_total;
         for (uint32_t i = warp; i < nseg * spec; i += KB_THREADS / 32) {
             const uint32_t o = woff[i];
             if (o == 0xFFFFFFFFu) continue;
             const Item &itm = sall[i];
             const uint32_t n = min(itm.aux, P.ntiles_total - min(itm.tile, P.ntiles_total));
-            for (uint32_t k = lane; k < n; k += 32) wpool[o + k] = wrow_g[itm.tile + k];
+            const uint2 *src = reinterpret_cast<const uint2 *>(wrow_g + itm.tile);
+            uint2 *dst = reinterpret_cast<uint2 *>(wpool + o);
+            for (uint32_t k = lane; k < 3 * n; k += 32) cp_async8(dst + k, src + k);
         }
+        cp_async_wait_all();
     }
     __syncthreads();
 
