@@ -2144,7 +2144,7 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __shared__ __align__(16) Item sall[ITEM_SMEM];   // the first `spec` items of every segment
     __shared__ uint32_t woff[ITEM_SMEM];         // WINDOW item: its prefix table in wpool, or ~0u
     __shared__ __align__(8) WTile wpool[WPOOL];
-    __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1];
+    __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1], wcnt[KB_THREADS / 32], n_fit;
     __shared__ __align__(16) float tilep[TILE];   // a recomputed tile's p, for the walker
     __shared__ uint32_t swin[256];
     __shared__ float S_sh;
@@ -2202,8 +2202,12 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
     __syncthreads();
     // prefix tables of the WINDOW items held in shared memory (offsets by a
     // block scan over the item slots, two per thread; tables that do not fit
-    // stay in global memory)
+    // stay in global memory).  Slots are scanned in order, so the tables that
+    // fit are the first ones; their slots are listed (in sitems, unused
+    // until the walk) and one warp per listed table issues its copies.
     {
+        uint32_t *tlist = reinterpret_cast<uint32_t *>(sitems);
+        static_assert(sizeof(sitems) >= ITEM_SMEM * sizeof(uint32_t), "the table list fits the item chunk");
         uint32_t len[2] = {0u, 0u};
 #pragma unroll
         for (int h = 0; h < 2; h++) {
@@ -2215,36 +2219,50 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
             }
         }
         const uint32_t mine = len[0] + len[1];
+        const uint32_t nmine = (len[0] != 0u) + (len[1] != 0u);
         const uint32_t incl = warp_incl_scan_u(mine);
-        if (lane == 31) wsum[warp] = incl;
-        __syncthreads();
-        if (tid == 0) {
-            uint32_t r = 0;
-            for (int w = 0; w < KB_THREADS / 32; w++) {
-                const uint32_t v = wsum[w];
-                wsum[w] = r;
-                r += v;
-            }
+        const uint32_t nincl = warp_incl_scan_u(nmine);
+        if (lane == 31) {
+            wsum[warp] = incl;
+            wcnt[warp] = nincl;
         }
         __syncthreads();
-        uint32_t off = wsum[warp] + incl - mine;
+        if (tid == 0) {
+            uint32_t r = 0, c = 0;
+            for (int w = 0; w < KB_THREADS / 32; w++) {
+                const uint32_t v = wsum[w], n = wcnt[w];
+                wsum[w] = r;
+                wcnt[w] = c;
+                r += v;
+                c += n;
+            }
+            n_fit = 0;
+        }
+        __syncthreads();
+        uint32_t off = wsum[warp] + incl - mine, t = wcnt[warp] + nincl - nmine;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const uint32_t i = 2 * tid + h;
-            woff[i] = (len[h] && off + len[h] <= (uint32_t)WPOOL) ? off : 0xFFFFFFFFu;
+            const bool fits = len[h] && off + len[h] <= (uint32_t)WPOOL;
+            woff[i] = fits ? off : 0xFFFFFFFFu;
+            if (fits) {
+                tlist[t] = i;
+                atomicAdd(&n_fit, 1u);
+            }
+            t += len[h] ? 1u : 0u;
             off += len[h];
         }
         __syncthreads();
-        // one warp per item slot issues its table's copies (8-byte chunks)
+        // one warp per listed table issues its copies (8-byte chunks)
         static_assert(sizeof(WTile) == 24, "a prefix-table entry is three 8-byte chunks");
         const WTile *wrow_g = P.wpre + (size_t)hrow * P.ntiles_total;
-        for (uint32_t i = warp; i < nseg * spec; i += KB_THREADS / 32) {
-            const uint32_t o = woff[i];
-            if (o == 0xFFFFFFFFu) continue;
+        const uint32_t nf = n_fit;
+        for (uint32_t t2 = warp; t2 < nf; t2 += KB_THREADS / 32) {
+            const uint32_t i = tlist[t2];
             const Item &itm = sall[i];
             const uint32_t n = min(itm.aux, P.ntiles_total - min(itm.tile, P.ntiles_total));
             const uint2 *src = reinterpret_cast<const uint2 *>(wrow_g + itm.tile);
-            uint2 *dst = reinterpret_cast<uint2 *>(wpool + o);
+            uint2 *dst = reinterpret_cast<uint2 *>(wpool + woff[i]);
             for (uint32_t k = lane; k < 3 * n; k += 32) cp_async8(dst + k, src + k);
         }
         cp_async_wait_all();
