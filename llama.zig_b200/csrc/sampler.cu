@@ -1430,41 +1430,45 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const float w = fminf(z * -0.6931472f, 1e30f);   // -ln P (finite for P = 0)
         return fminf(ex2_approx(fminf(z + tp.K, 40.0f)) * w, 185363.8f);   // 2^17.5
     };
+    // Both roundings are summed: r1 >= r2 element by element (fhi > flo and
+    // y >= 0), and a tile's differences stay far below 2^32, so the two sums
+    // agree exactly when every element's do.
     uint32_t acc = 0u, diff = 0u;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float4 q = quad(j);
-        const float a4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const float y = term_y(__fsub_rn(a4[c], M));
-            const uint32_t r1 = __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
-            const uint32_t r2 = __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
-            diff |= r1 ^ r2;
-            acc += r1;
-        }
-    }
-    acc -= (uint32_t)TILE * 0x4B400000u;   // a tile sums to < 2^22.5
-    // WINDOW tiles: the same for binade lo + 1 (y / 2)
     const uint32_t cls_t = (tp.info >> 2) & 3u;
     const bool win = live && cls_t == CLS_WINDOW;
     uint32_t acch = 0u;
-    if (win) {
-        const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
-#pragma unroll 2
+    {
+        uint32_t acc2 = 0u;
+#pragma unroll
         for (int j = 0; j < 8; j++) {
             const float4 q = quad(j);
             const float a4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float y = term_y(__fsub_rn(a4[c], M));
-                const uint32_t r3 = __float_as_uint(fmaf(y, hh, 12582912.0f));
-                const uint32_t r4 = __float_as_uint(fmaf(y, hl, 12582912.0f));
-                diff |= r3 ^ r4;
-                acch += r3;
+                acc += __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
+                acc2 += __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
             }
         }
-        acch -= (uint32_t)TILE * 0x4B400000u;
+        diff |= acc ^ acc2;
+        acc -= (uint32_t)TILE * 0x4B400000u;   // a tile sums to < 2^22.5
+        if (win) {
+            const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
+            uint32_t acch2 = 0u;
+#pragma unroll 2
+            for (int j = 0; j < 8; j++) {
+                const float4 q = quad(j);
+                const float a4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const float y = term_y(__fsub_rn(a4[c], M));
+                    acch += __float_as_uint(fmaf(y, hh, 12582912.0f));
+                    acch2 += __float_as_uint(fmaf(y, hl, 12582912.0f));
+                }
+            }
+            diff |= acch ^ acch2;
+            acch -= (uint32_t)TILE * 0x4B400000u;
+        }
     }
     uint32_t nanl = 0;
     if (TERM == TERM_P && check_nan && live) {
