@@ -2134,7 +2134,7 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
 }
 
 template <int TERM>
-__global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
+__global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     const uint32_t row = blockIdx.x;
     const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2371,12 +2371,25 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
         for (uint32_t sgi = 0; sgi < nseg; sgi++) {
             const uint32_t nit = s_nit[sgi];
             nitems_all += nit;
-            if (nit <= spec) {
+            // the segment's items from the shared copy, or, when it has more
+            // than that holds, in chunks from global memory (one call site of
+            // slow_item, so that it is inlined and the walk state stays in
+            // registers)
+            const bool held = nit <= spec;
+            for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
+                const Item *src = sall + sgi * spec;
+                uint32_t nc = nit;
+                if (!held) {
+                    nc = min((uint32_t)ITEM_CHUNK, nit - i0);
+                    __syncwarp();
+                    for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ib[sgi * SEG_TILES + i0 + j];
+                    __syncwarp();
+                    src = sitems;
+                }
                 // the common case stays in this loop: the running sum is in
                 // the item's binade and stays there (a SIMPLE stretch, or a
                 // WINDOW stretch that does not cross)
-                const Item *src = sall + sgi * spec;
-                for (uint32_t j = 0; j < nit; j++) {
+                for (uint32_t j = 0; j < nc; j++) {
                     const Item it = src[j];
                     if (st.e == it.lo) {
                         const uint32_t q = (st.m & 1u) ? it.q[1] : it.q[0];
@@ -2385,18 +2398,9 @@ __global__ void __launch_bounds__(KB_THREADS) kernel_b(KBParams P) {
                             continue;
                         }
                     }
-                    slow_item(it, woff[sgi * spec + j]);
+                    slow_item(it, held ? woff[sgi * spec + j] : 0xFFFFFFFFu);
                 }
-            } else {
-                // more items than the shared copy holds: chunks from global memory
-                const Item *ig = ib + sgi * SEG_TILES;
-                for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
-                    const uint32_t nc = min((uint32_t)ITEM_CHUNK, nit - i0);
-                    __syncwarp();
-                    for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ig[i0 + j];
-                    __syncwarp();
-                    for (uint32_t j = 0; j < nc; j++) slow_item(sitems[j], 0xFFFFFFFFu);
-                }
+                if (held) break;
             }
         }
         if (lane == 0) {
