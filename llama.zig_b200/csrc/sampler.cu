@@ -651,16 +651,20 @@ __device__ double block_exscan1_d(double v, double *wtmp, double *total) {
 
 // One warp handles four tiles at a time: lane l holds elements 4(l%8)..+3 of
 // tile l/8 (an 8-lane group per tile, one float4 load per lane).
-__device__ __forceinline__ float4 load_quad(const K12Params &P, const float *x, uint32_t g, uint64_t pol,
-                                            const uint32_t *win, uint32_t nwin) {
+// Logits g .. g+3 from global memory (-inf past the vocabulary) with the
+// repetition penalty applied.  Not inlined: it is the path for rows that
+// cannot be staged in shared memory, and one out-of-line copy keeps the
+// staged loops' instruction footprint small.
+__device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vocab, float rep_penalty, uint64_t pol,
+                                         const uint32_t *win, uint32_t nwin) {
     float4 q;
-    if (g + 4 <= P.vocab && (reinterpret_cast<uintptr_t>(x + g) & 15u) == 0) {
+    if (g + 4 <= vocab && (reinterpret_cast<uintptr_t>(x + g) & 15u) == 0) {
         q = ldg_policy(reinterpret_cast<const float4 *>(x + g), pol);
     } else {
-        q.x = g < P.vocab ? x[g] : NEG_INF;
-        q.y = g + 1 < P.vocab ? x[g + 1] : NEG_INF;
-        q.z = g + 2 < P.vocab ? x[g + 2] : NEG_INF;
-        q.w = g + 3 < P.vocab ? x[g + 3] : NEG_INF;
+        q.x = g < vocab ? x[g] : NEG_INF;
+        q.y = g + 1 < vocab ? x[g + 1] : NEG_INF;
+        q.z = g + 2 < vocab ? x[g + 2] : NEG_INF;
+        q.w = g + 3 < vocab ? x[g + 3] : NEG_INF;
     }
     // repetition penalty (sampler.zig:54-75): each distinct id of the last
     // `window` previous tokens, once
@@ -673,7 +677,7 @@ __device__ __forceinline__ float4 load_quad(const K12Params &P, const float *x, 
             if (first) {
                 float *e = (&q.x) + (id - g);
                 const float a = *e;
-                *e = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
+                *e = a > 0.0f ? __fdiv_rn(a, rep_penalty) : __fmul_rn(a, rep_penalty);
             }
         }
     }
@@ -836,7 +840,7 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
     } else {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float4 q = load_quad(P, x, g0 + tile_elem(tl, j, 0), pol, swin, nwin);
+            const float4 q = load_quad(x, g0 + tile_elem(tl, j, 0), P.vocab, P.rep_penalty, pol, swin, nwin);
             v[4 * j] = q.x;
             v[4 * j + 1] = q.y;
             v[4 * j + 2] = q.z;
@@ -851,7 +855,7 @@ __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, 
                                             const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
                                             uint64_t pol) {
     const uint32_t g = seg * SEG_ELEMS + tl * TILE + tile_elem(tl, j, 0);
-    if (!staged) return load_quad(P, x, g, pol, swin, nwin);
+    if (!staged) return load_quad(x, g, P.vocab, P.rep_penalty, pol, swin, nwin);
     float4 q = sbuf[tl * 8 + ((uint32_t)j ^ (tl & 7u))];
     if (g + 4 > P.vocab) {
         q.x = g < P.vocab ? q.x : NEG_INF;
@@ -868,7 +872,7 @@ __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, 
 // maximum, the sum relative to it, a non-finite flag and, for top-p without a
 // top-k floor, the tail-element histogram.  No cross-CTA step: the row
 // reduction is k1_rows.
-__global__ void __launch_bounds__(K12_THREADS) k1_stats(K12Params P) {
+__global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     grid_dep_launch();
     const uint32_t seg = blockIdx.x, row = blockIdx.y, hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
