@@ -555,11 +555,6 @@ __device__ __forceinline__ bool penalty_active(const K12Params &P) {
     return P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0;
 }
 
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -888,7 +883,9 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     __shared__ float wm[NW];
     __shared__ uint32_t wf[NW];
     __shared__ double wd[NW];
-    const uint64_t pol = l2_policy_evict_last();
+    // the logits stream through L2 once here: marked evict-first, they do not
+    // push out what later kernels reuse (their code, the tile statistics)
+    const uint64_t pol = l2_policy_evict_first();
     const bool pen = penalty_active(P);
     const bool bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen ? 1u : 0u, sbuf, &bar, pol);
     const uint32_t nwin = load_window(P, row, swin);
@@ -1859,28 +1856,42 @@ struct KBParams {
 };
 
 // Exact p of element g (with the repetition penalty), for the recompute path.
-__device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M, const uint32_t *win,
-                            uint32_t nwin) {
-    if (g >= P.vocab) return 0.0f;
-    float v = P.logits[(size_t)row * P.ld + g];
+__device__ __forceinline__ float exact_p_raw(const float *xrow, uint32_t vocab, uint32_t g, float M, float T,
+                                             float pen, const uint32_t *win, uint32_t nwin) {
+    if (g >= vocab) return 0.0f;
+    float v = xrow[g];
     for (uint32_t j = 0; j < nwin; j++) {
         if (win[j] == g) {
-            v = v > 0.0f ? __fdiv_rn(v, P.rep_penalty) : __fmul_rn(v, P.rep_penalty);
+            v = v > 0.0f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
             break;
         }
     }
-    return prob_unnorm(v, M, P.T);
+    return prob_unnorm(v, M, T);
+}
+__device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M, const uint32_t *win,
+                            uint32_t nwin) {
+    return exact_p_raw(P.logits + (size_t)row * P.ld, P.vocab, g, M, P.T, P.rep_penalty, win, nwin);
 }
 
-// The term of element g for the recompute path: p (TERM_P) or the entropy
-// term h (TERM_H, with the normaliser S).
+// The walker's recompute path: the warp adds one tile's terms, p (TERM_P)
+// or the entropy terms h (TERM_H, with the normaliser S), recomputed from
+// the logits, to the running sum s in index order.  Out of line: it is rare,
+// and inlined it would sit in the middle of the walk's hot code.
 template <int TERM>
-__device__ __forceinline__ float exact_term_at(const KBParams &P, uint32_t row, uint32_t g, float M,
-                                               const uint32_t *win, uint32_t nwin, float S) {
-    const float p = exact_p_at(P, row, g, M, win, nwin);
-    if (TERM == TERM_P) return p;
-    const float Pn = __fdiv_rn(p, S);
-    return Pn > 0.0f ? __fmul_rn(Pn, -log_ref(Pn)) : 0.0f;
+__device__ __noinline__ float walk_recompute_tile(float s, const float *xrow, uint32_t vocab, uint32_t tile, float M,
+                                                  float T, float pen, const uint32_t *win, uint32_t nwin, float S,
+                                                  float *tilep) {
+    const uint32_t lane = threadIdx.x & 31u;
+    float t = exact_p_raw(xrow, vocab, tile * TILE + lane, M, T, pen, win, nwin);
+    if (TERM == TERM_H) {
+        const float Pn = __fdiv_rn(t, S);
+        t = Pn > 0.0f ? __fmul_rn(Pn, -log_ref(Pn)) : 0.0f;
+    }
+    tilep[lane] = t;
+    __syncwarp();
+    s = seq_add32_smem(s, tilep);
+    __syncwarp();
+    return s;
 }
 
 // Block-wide bitonic sort (ascending) of npow (a power of two) keys in shared
@@ -1914,9 +1925,9 @@ __device__ __forceinline__ float key_p(unsigned long long k) {
 
 // Stable LSD radix sort (4-bit digits) of n keys by one CTA, global memory.
 // Returns the buffer holding the sorted keys (a or b).
-__device__ unsigned long long *cta_radix_sort(unsigned long long *a, unsigned long long *b, uint32_t n,
-                                              uint32_t *cnt /* smem, 16 * KB_THREADS */,
-                                              unsigned long long *red /* smem, 2 */) {
+__device__ __noinline__ unsigned long long *cta_radix_sort(unsigned long long *a, unsigned long long *b, uint32_t n,
+                                                           uint32_t *cnt /* smem, 16 * KB_THREADS */,
+                                                           unsigned long long *red /* smem, 2 */) {
     const int tid = threadIdx.x;
     // bits that differ between keys
     unsigned long long o = 0, an = ~0ull;
@@ -2286,11 +2297,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         uint32_t wflags = 0, nitems_all = 0, nslow = 0;
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
         // add one tile element by element, p recomputed from the logits
+        const float *xrow = P.logits + (size_t)row * P.ld;
         auto add_tile = [&](uint32_t tile) {
-            tilep[lane] = exact_term_at<TERM>(P, row, tile * TILE + lane, M, swin, nwin, Sx);
-            __syncwarp();
-            st = state_of(seq_add32_smem(float_of(st), tilep));
-            __syncwarp();
+            st = state_of(walk_recompute_tile<TERM>(float_of(st), xrow, P.vocab, tile, M, P.T, P.rep_penalty, swin,
+                                                    nwin, Sx, tilep));
         };
         // everything but the common case: a WINDOW crossing, a stored or
         // recomputed tile, a running sum outside the item's binades
