@@ -1036,6 +1036,18 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     const SegStat *S = P.sstat + (size_t)hrow * MAX_SEG;
     const uint32_t ns = P.nseg;
     for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) kh[b] = 0u;
+    // top-k: every thread requests its first tile maxima now, so that their
+    // loads overlap the row reduction below
+    constexpr int KT = 16;
+    const TileStat *ts = P.tstat + (size_t)hrow * P.ntiles_total;
+    float tmv[KT];
+    if (k_floor) {
+#pragma unroll
+        for (int k = 0; k < KT; k++) {
+            const uint32_t t = (uint32_t)k * K12_THREADS + tid;
+            tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+        }
+    }
     if (warp == 0) {
         float m = NEG_INF;
         uint32_t nf = 0;
@@ -1068,21 +1080,24 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
             if (c < ns) P.sstat[(size_t)hrow * MAX_SEG + c].base = run + incl - sv;
             run += __shfl_sync(0xffffffffu, incl, 31);
         }
-        // entropy estimate: H = ln S - ln2 sum(e x) / S, e = 2^x, x = (v - M) log2e / T
+        // entropy estimate (typical-p alone): H = ln S - ln2 sum(e x) / S,
+        // e = 2^x, x = (v - M) log2e / T
         double e2 = 0.0;
-        for (uint32_t c = lane; c < ns; c += 32) {
-            const SegStat st = S[c];
-            if (st.smax > NEG_INF) {
-                const double o = (double)((st.smax - m) * c2);
-                e2 += (double)ex2_approx((float)o) * (st.ssum2 + o * st.ssum);
+        if (P.tmode == TYP_BAND) {
+            for (uint32_t c = lane; c < ns; c += 32) {
+                const SegStat st = S[c];
+                if (st.smax > NEG_INF) {
+                    const double o = (double)((st.smax - m) * c2);
+                    e2 += (double)ex2_approx((float)o) * (st.ssum2 + o * st.ssum);
+                }
             }
+            e2 = warp_sum_d(e2);
         }
-        e2 = warp_sum_d(e2);
         if (lane == 0) {
             ri.M = m;
             ri.check_nan = nf | ((P.T != P.T) ? 1u : 0u);
             ri.S_raw = run;
-            ri.H_raw = run > 0.0 ? log(run) - 0.6931471805599453 * e2 / run : 0.0;
+            ri.H_raw = (P.tmode == TYP_BAND && run > 0.0) ? log(run) - 0.6931471805599453 * e2 / run : 0.0;
             ri.dband = __int_as_float(0x7f800000);
             ri.tmode = P.tmode;
         }
@@ -1138,15 +1153,15 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     // main pass's per-logit candidate test, which is monotone in the logit)
     uint32_t kcount = 0;   // tiles whose maximum is above the bin edge -(tid+1)/4
     if (k_floor) {
-        const TileStat *ts = P.tstat + (size_t)hrow * P.ntiles_total;
         // all of a thread's tile maxima are requested before the first atomic
-        constexpr int KT = 16;
+        // (the first KT were requested before the row reduction)
         for (uint32_t t0 = 0; t0 < P.ntiles_total; t0 += KT * K12_THREADS) {
-            float tmv[KT];
+            if (t0 > 0) {
 #pragma unroll
-            for (int k = 0; k < KT; k++) {
-                const uint32_t t = t0 + (uint32_t)k * K12_THREADS + tid;
-                tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+                for (int k = 0; k < KT; k++) {
+                    const uint32_t t = t0 + (uint32_t)k * K12_THREADS + tid;
+                    tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+                }
             }
 #pragma unroll
             for (int k = 0; k < KT; k++) {
