@@ -1997,18 +1997,40 @@ __device__ __noinline__ unsigned long long *cta_radix_sort(unsigned long long *a
 // kept mass, draw walk).  The adds stay strictly in list order; only the
 // loads are issued eight ahead, so the loop runs at the add chain's latency
 // instead of a load round trip per element.  `get(i)` returns element i.
+// The terms are >= 0, so the running sum never decreases: the threshold is
+// tested once per eight adds (off the add chain), and only the block that
+// crosses it is searched.  If `cum_out` is given, the running sum after
+// element i is stored there for every element added (the kept mass of any
+// prefix is then read back instead of summed again).
 template <typename Get>
-__device__ __forceinline__ uint32_t seq_first_exceed(Get get, uint32_t n, float thr, float &cum) {
+__device__ __forceinline__ uint32_t seq_first_exceed(Get get, uint32_t n, float thr, float &cum,
+                                                     float *cum_out = nullptr) {
     for (uint32_t i0 = 0; i0 < n; i0 += 8) {
-        float v[8];
+        float v[8], c[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = i0 + k < n ? get(i0 + k) : 0.0f;
+        float t = cum;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            if (i0 + k >= n) return n;
-            cum = __fadd_rn(cum, v[k]);
-            if (cum > thr) return i0 + k;
+            t = __fadd_rn(t, v[k]);   // past n the terms are 0: t is unchanged
+            c[k] = t;
         }
+        if (cum_out) {
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (i0 + k < n) cum_out[i0 + k] = c[k];
+        }
+        if (t > thr) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (c[k] > thr) {
+                    if (i0 + k >= n) break;
+                    cum = c[k];
+                    return i0 + k;
+                }
+            }
+        }
+        cum = t;
     }
     return n;
 }
@@ -2025,18 +2047,23 @@ __device__ __forceinline__ float seq_sum(Get get, uint32_t n) {
     }
     return t;
 }
-// r -= a[i] in order; the first i with r <= 0, or n.
+// r -= a[i] in order; the first i with r <= 0, or n.  The terms are >= 0,
+// so r never increases: tested once per eight subtractions, as above.
 template <typename Get>
 __device__ __forceinline__ uint32_t seq_draw(Get get, uint32_t n, float r) {
     for (uint32_t i0 = 0; i0 < n; i0 += 8) {
-        float v[8];
+        float v[8], c[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = i0 + k < n ? get(i0 + k) : 0.0f;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            if (i0 + k >= n) return n;
             r = __fsub_rn(r, v[k]);
-            if (r <= 0.0f) return i0 + k;
+            c[k] = r;
+        }
+        if (r <= 0.0f) {
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (c[k] <= 0.0f) return i0 + k < n ? i0 + k : n;
         }
     }
     return n;
@@ -2586,10 +2613,14 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         const bool k_act = P.top_k > 0 && P.top_k < P.vocab;
         // top-k (sampler.zig:106-109)
         if (k_act && n_sel > P.top_k) n_sel = P.top_k;
-        // top-p (sampler.zig:111-118): the crossing token is deselected too
+        // top-p (sampler.zig:111-118): the crossing token is deselected too.
+        // Its running sums are kept (in the stored terms' area, free after
+        // the walk): the kept mass below is the same sum over a prefix
+        float *cums = nullptr;
         if (P.top_p > 0.0f && P.top_p < 1.0f) {
             float cum = 0.0f;
-            n_sel = seq_first_exceed([&](uint32_t j) { return probs[j]; }, n_sel, P.top_p, cum);
+            if (n_sel <= (uint32_t)(WC_CAP * TILE)) cums = wcs;
+            n_sel = seq_first_exceed([&](uint32_t j) { return probs[j]; }, n_sel, P.top_p, cum, cums);
         }
         // min-p (sampler.zig:120-126) against probs[indices[0]]
         if (P.min_p > 0.0f && n_pos > 0) {
@@ -2615,8 +2646,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
             hdr->n_sel = P.tmode == TYP_SELECTED ? n_sel : 0u;
             hdr->top_idx = n_pos > 0 ? idxs[0] : 0u;
         } else {
-            // kept mass in sorted order (sampler.zig:156-159)
-            total = seq_sum([&](uint32_t j) { return probs[j]; }, n_sel);
+            // kept mass in sorted order (sampler.zig:156-159): the same adds
+            // from 0 as top-p's running sum, so its value at the last kept
+            // token when that was recorded
+            total = (cums && n_sel > 0) ? cums[n_sel - 1] : seq_sum([&](uint32_t j) { return probs[j]; }, n_sel);
             n_kept = n_sel;
             if (!(total > 0.0f)) {
                 token = n_pos > 0 ? idxs[0] : 0u;  // sampler.zig:160
