@@ -1870,6 +1870,78 @@ struct KBParams {
     uint32_t *out;       // per call row
 };
 
+// The crossing inside a WINDOW stretch of ntl tiles: the first tile c whose
+// prefix count (binade lo, entry parity pi, table wp) brings the running
+// mantissa m to 2^24.  The caller guarantees that the whole stretch does.
+// Called by a full warp: each round samples the window [lo_i, hi_i] at up
+// to 32 evenly spaced tiles (every tile once it is a warp wide) and keeps
+// the part between the last sample below 2^24 and the first at or above it.
+struct Crossing {
+    uint32_t c;        // the crossing tile
+    uint32_t q_prev;   // prefix count through tile c - 1 (0 when c = 0)
+    uint32_t slot;     // tile c's stored exact terms, or >= n_wc
+    Comp suf;          // suffix counts (binade lo + 1) from tile c + 1, if c + 1 < ntl
+};
+__device__ __forceinline__ Crossing find_crossing(const WTile *wp, uint32_t ntl, uint32_t m, uint32_t pi) {
+    const uint32_t lane = threadIdx.x & 31u;
+    // invariant: the crossing lies in [lo_i, hi_i]
+    uint32_t lo_i = 0, hi_i = ntl - 1;
+    while (lo_i < hi_i) {
+        const uint32_t step = (hi_i - lo_i + 32) / 32;
+        const uint32_t kmax = min(31u, (hi_i - lo_i) / step);   // the last sampled lane
+        bool pr = false;
+        if (lane <= kmax) {
+            const Comp c = wp[lo_i + lane * step].pre_lo;
+            pr = m + (pi ? c.q1 : c.q0) >= QLIM;
+        }
+        const uint32_t mask = __ballot_sync(0xffffffffu, pr);
+        if (mask == 0) {
+            lo_i = lo_i + kmax * step + 1;   // past every sampled tile
+        } else {
+            const uint32_t f = __ffs(mask) - 1;
+            hi_i = lo_i + f * step;
+            if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
+        }
+    }
+    Crossing x;
+    x.c = lo_i;
+    x.q_prev = 0u;
+    if (x.c > 0) {
+        const Comp pc = wp[x.c - 1].pre_lo;
+        x.q_prev = pi ? pc.q1 : pc.q0;
+    }
+    x.slot = wp[x.c].slot;
+    x.suf = x.c + 1 < ntl ? wp[x.c + 1].suf_hi : Comp{0u, 0u};
+    return x;
+}
+
+// Check of find_crossing for the test harness: block b (one warp) takes
+// stretches of ntl = b + 1 tiles and every crossing position, with a table
+// that makes the answer known; failures are counted in out[0], cases in out[1].
+__global__ void crossing_check_kernel(WTile *scratch, uint32_t max_ntl, unsigned long long *out) {
+    const uint32_t ntl = blockIdx.x + 1, lane = threadIdx.x;
+    WTile *wp = scratch + (size_t)blockIdx.x * max_ntl;
+    for (uint32_t cs = 0; cs < ntl; cs++) {
+        for (uint32_t pi = 0; pi < 2; pi++) {
+            const uint32_t m = 5u + pi;
+            for (uint32_t k = lane; k < ntl; k += 32) {
+                // prefix counts below the crossing stay under 2^24 - m
+                const uint32_t q = k < cs ? k : QLIM;
+                wp[k] = WTile{Comp{pi ? 7u : q, pi ? q : 7u}, Comp{3 * k, 3 * k + 1}, 1000u + k, 0u};
+            }
+            __syncwarp();
+            const Crossing x = find_crossing(wp, ntl, m, pi);
+            bool ok = x.c == cs && x.slot == 1000u + cs && x.q_prev == (cs > 0 ? cs - 1 : 0u);
+            if (cs + 1 < ntl) ok = ok && x.suf.q0 == 3 * (cs + 1) && x.suf.q1 == 3 * (cs + 1) + 1;
+            if (lane == 0) {
+                atomicAdd(&out[1], 1ull);
+                if (!ok) atomicAdd(&out[0], 1ull);
+            }
+            __syncwarp();
+        }
+    }
+}
+
 // Exact p of element g (with the repetition penalty), for the recompute path.
 __device__ __forceinline__ float exact_p_raw(const float *xrow, uint32_t vocab, uint32_t g, float M, float T,
                                              float pen, const uint32_t *win, uint32_t nwin) {
@@ -2379,30 +2451,9 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
                 // prefix table (shared memory when it was gathered)
                 const WTile *wp = wo != 0xFFFFFFFFu ? wpool + wo : wrow + it.tile;
                 const uint32_t pi = par;
-                uint32_t lo_i = 0, hi_i = ntl - 1;
-                while (lo_i < hi_i) {
-                    const uint32_t step = (hi_i - lo_i + 32) / 32;
-                    const uint32_t pos = lo_i + lane * step;
-                    bool pr = false;
-                    if (pos <= hi_i) {
-                        const Comp c = wp[pos].pre_lo;
-                        pr = st.m + (pi ? c.q1 : c.q0) >= QLIM;
-                    }
-                    const uint32_t mask = __ballot_sync(0xffffffffu, pr);
-                    if (mask == 0) {
-                        lo_i = lo_i + 31 * step + 1;
-                    } else {
-                        const uint32_t f = __ffs(mask) - 1;
-                        hi_i = lo_i + f * step;
-                        if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
-                    }
-                }
-                const uint32_t c = lo_i;
-                if (c > 0) {
-                    const Comp pc = wp[c - 1].pre_lo;
-                    st.m += pi ? pc.q1 : pc.q0;
-                }
-                const uint32_t sl = wp[c].slot;
+                const Crossing x = find_crossing(wp, ntl, st.m, pi);
+                const uint32_t c = x.c, sl = x.slot;
+                st.m += x.q_prev;
                 if (sl < n_wc) {   // stored exact p
                     st = state_of(seq_add32_smem(float_of(st), wcs + sl * TILE));
                 } else {
@@ -2410,8 +2461,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
                 }
                 from = c + 1;
                 if (from < ntl && st.e == it.lo + 1) {
-                    const Comp sh = wp[from].suf_hi;
-                    const uint32_t q = (st.m & 1u) ? sh.q1 : sh.q0;
+                    const uint32_t q = (st.m & 1u) ? x.suf.q1 : x.suf.q0;
                     if (st.m + q < QLIM && q < QSAT) {
                         st.m += q;
                         from = ntl;
@@ -3197,6 +3247,25 @@ extern "C" bs_status bs_debug_cert_check(uint32_t n, uint64_t seed, unsigned lon
     }
     if (e == cudaSuccess) e = cudaMemcpy(h_out, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     cudaFree(d);
+    return cuda_status(e);
+}
+
+// The crossing search on every stretch length 1..max_ntl and crossing
+// position; h_out[0] = failures, h_out[1] = cases.  Synchronous.
+extern "C" bs_status bs_debug_crossing_check(uint32_t max_ntl, unsigned long long *h_out) {
+    if (!h_out || max_ntl == 0 || max_ntl > 4096) return BS_EINVAL;
+    WTile *scratch = nullptr;
+    unsigned long long *d = nullptr;
+    BS_CUDA(cudaMalloc(&scratch, (size_t)max_ntl * max_ntl * sizeof(WTile)));
+    cudaError_t e = cudaMalloc(&d, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(d, 0, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        crossing_check_kernel<<<max_ntl, 32>>>(scratch, max_ntl, d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(h_out, d, 2 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    cudaFree(scratch);
     return cuda_status(e);
 }
 

@@ -222,6 +222,21 @@ def test_certificate_bound_holds(gpu_pkg):
         assert certified > total // 2
 
 
+def test_window_crossing_search_exhaustive(gpu_pkg):
+    # the walker's search for the tile where a WINDOW stretch leaves its
+    # binade (find_crossing in sampler.cu): every stretch length up to 300
+    # tiles, every crossing position, both entry parities
+    import ctypes
+    L = gpu_pkg.lib()
+    L.bs_debug_crossing_check.argtypes = [ctypes.c_uint32, ctypes.c_void_p]
+    L.bs_debug_crossing_check.restype = ctypes.c_int
+    out = np.zeros(2, np.uint64)
+    assert L.bs_debug_crossing_check(300, out.ctypes.data) == 0
+    bad, cases = (int(v) for v in out)
+    assert cases == 2 * sum(range(1, 301))
+    assert bad == 0, f"{bad} of {cases} crossing searches wrong"
+
+
 def test_entropy_certificate_bound_holds(gpu_pkg):
     # the entropy pass's certificate (cert_eps_h): seeds with the top bit set
     # select the entropy-term check
