@@ -116,6 +116,19 @@ def test_odd_vocab_sizes(gpu_pkg, orc, V):
     assert_same(run_gpu(gpu_pkg, c, x, seeds), run_oracle(orc, c, x, seeds), f"V={V}")
 
 
+@pytest.mark.parametrize("scale,min_p", [(0.3, 0.0), (2.5, 0.0), (3.0, 0.0), (3.0, 0.002)])
+def test_top_p_large_kept_sets(gpu_pkg, orc, scale, min_p):
+    # flat rows: top-p keeps thousands of tokens (past the shared-memory
+    # candidate sort and past the stored running sums of the kept mass), and
+    # min-p may cut the top-p prefix further
+    rng = np.random.default_rng(int(scale * 10) + int(min_p * 100))
+    x = (scale * rng.standard_normal((1, 6, 50000))).astype(np.float32)
+    c = dict(temperature=1.0, top_k=0, top_p=0.9, min_p=min_p, typical_p=1.0, seed=5,
+             repetition_window=0, repetition_penalty=1.0)
+    seeds = np.arange(6, dtype=np.uint64) + 5
+    assert_same(run_gpu(gpu_pkg, c, x, seeds), run_oracle(orc, c, x, seeds), f"scale={scale} min_p={min_p}")
+
+
 def _workload(pkg, name, rows, steps=1):
     w = pkg.workloads.WORKLOADS[name]
     x = np.stack([pkg.workloads.make_logits(w, step=s, rows=rows) for s in range(steps)])
