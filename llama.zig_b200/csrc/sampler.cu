@@ -406,14 +406,14 @@ __device__ void block_segscan_comp(Comp *c, const uint32_t *flag, uint32_t n, Se
 // ===========================================================================
 // Decoupled passes.  A row is cut into segments of SEG_TILES tiles; K1 and K2
 // run one CTA per segment with one thread per tile (32 logits in registers).
-//   K1 streams the logits from HBM (L2 evict_last) and writes per-tile
-//      maxima and sums (relative to the tile maximum) plus per-segment
-//      aggregates and histograms; the last CTA of a row to finish reduces them
-//      to the row maximum, the prefix estimate at every segment start and the
-//      candidate floors (no CTA ever waits for another).
-//   K2 runs segments in reverse order, so it re-reads logits K1 left in L2,
-//      classifies tiles, computes the certified grid counts, writes the walk
-//      items and the candidates.
+//   K1 (k1_stats) streams the logits from HBM (L2 evict_first) and writes
+//      per-tile maxima and sums (relative to the tile maximum) plus
+//      per-segment aggregates and histograms; k1_rows, one CTA per row,
+//      reduces them to the row maximum, the prefix estimate at every segment
+//      start and the candidate floors (no CTA ever waits for another).
+//   K2 (k2_main) re-reads each segment in segment-major order (every row's
+//      first segment first), classifies tiles, computes the certified grid
+//      counts, writes the walk items and the candidates.
 // ===========================================================================
 constexpr int SEG_TILES = 256;               // tiles per segment == K1/K2 block size
 constexpr int SEG_ELEMS = SEG_TILES * TILE;  // 8192 logits
