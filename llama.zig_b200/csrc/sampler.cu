@@ -1875,7 +1875,8 @@ struct KBParams {
 // mantissa m to 2^24.  The caller guarantees that the whole stretch does.
 // Called by a full warp: each round samples the window [lo_i, hi_i] at up
 // to 32 evenly spaced tiles (every tile once it is a warp wide) and keeps
-// the part between the last sample below 2^24 and the first at or above it.
+// the part between the last sample below 2^24 and the first at or above it
+// (no division: lanes past the window take part as crossed).
 struct Crossing {
     uint32_t c;        // the crossing tile
     uint32_t q_prev;   // prefix count through tile c - 1 (0 when c = 0)
@@ -1888,18 +1889,20 @@ __device__ __forceinline__ Crossing find_crossing(const WTile *wp, uint32_t ntl,
     uint32_t lo_i = 0, hi_i = ntl - 1;
     while (lo_i < hi_i) {
         const uint32_t step = (hi_i - lo_i + 32) / 32;
-        const uint32_t kmax = min(31u, (hi_i - lo_i) / step);   // the last sampled lane
-        bool pr = false;
-        if (lane <= kmax) {
-            const Comp c = wp[lo_i + lane * step].pre_lo;
+        const uint32_t pos = lo_i + lane * step;
+        // a lane past the window counts as crossed (the crossing is at or
+        // before hi_i), so an empty ballot means every lane's tile is below it
+        bool pr = pos > hi_i;
+        if (!pr) {
+            const Comp c = wp[pos].pre_lo;
             pr = m + (pi ? c.q1 : c.q0) >= QLIM;
         }
         const uint32_t mask = __ballot_sync(0xffffffffu, pr);
         if (mask == 0) {
-            lo_i = lo_i + kmax * step + 1;   // past every sampled tile
+            lo_i = lo_i + 31 * step + 1;
         } else {
             const uint32_t f = __ffs(mask) - 1;
-            hi_i = lo_i + f * step;
+            hi_i = min(hi_i, lo_i + f * step);
             if (f > 0) lo_i = lo_i + (f - 1) * step + 1;
         }
     }
