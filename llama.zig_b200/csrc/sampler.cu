@@ -646,6 +646,16 @@ __device__ double block_exscan1_d(double v, double *wtmp, double *total) {
 
 // One warp handles four tiles at a time: lane l holds elements 4(l%8)..+3 of
 // tile l/8 (an 8-lane group per tile, one float4 load per lane).
+// The repetition penalty on logit a of token g (sampler.zig:54-75): applied
+// once when g is among the window's ids.  Out of line: only rows with a
+// penalty take it.
+__device__ __noinline__ float penalize_once(float a, uint32_t g, const uint32_t *win, uint32_t nwin,
+                                            float rep_penalty) {
+    for (uint32_t j = 0; j < nwin; j++)
+        if (win[j] == g) return a > 0.0f ? __fdiv_rn(a, rep_penalty) : __fmul_rn(a, rep_penalty);
+    return a;
+}
+
 // Logits g .. g+3 from global memory (-inf past the vocabulary) with the
 // repetition penalty applied.  Not inlined: it is the path for rows that
 // cannot be staged in shared memory, and one out-of-line copy keeps the
@@ -1314,6 +1324,11 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     Comp *const carr = reinterpret_cast<Comp *>(uarr2 + SEG_TILES);   // 8-byte aligned: read as uint64_t too
     Comp *const carr2 = carr + SEG_TILES;
     __shared__ uint32_t wlist[SEG_TILES];
+    // uncertified terms of SIMPLE tiles, recounted exactly one per thread:
+    // (tile << 5) | element, and the tiles that still need the warp pass
+    constexpr uint32_t RC_CAP = 512;
+    __shared__ uint16_t rcl[RC_CAP];
+    __shared__ uint32_t nrc, rc_fb[SEG_TILES / 32];
     __shared__ uint32_t nlist, nanflag;
     // the segment's bulk copy overlaps the prologue (and, for the normaliser,
     // the wait for the row reduction: it needs only the logits); it is read
@@ -1341,7 +1356,9 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     if (tid == 0) {
         nlist = 0;
         nanflag = 0;
+        nrc = 0;
     }
+    if ((uint32_t)tid < SEG_TILES / 32) rc_fb[tid] = 0u;
 
     // raw prefix estimate at every tile start of the segment, and from it
     // each tile's candidate binades of the running sum and its main-loop
@@ -1446,10 +1463,13 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const float w = fminf(z * -0.6931472f, 1e30f);   // -ln P (finite for P = 0)
         return fminf(ex2_approx(fminf(z + tp.K, 40.0f)) * w, 185363.8f);   // 2^17.5
     };
-    // Both roundings are summed: r1 >= r2 element by element (fhi > flo and
-    // y >= 0), and a tile's differences stay far below 2^32, so the two sums
-    // agree exactly when every element's do.
-    uint32_t acc = 0u, diff = 0u;
+    // The normaliser pass sums both roundings: r1 >= r2 element by element
+    // (fhi > flo and y >= 0), and a tile's differences stay far below 2^32,
+    // so the two sums agree exactly when every element's do.  The entropy
+    // pass marks the terms whose roundings differ instead (bit 4 j + c of
+    // `bad`): its uncertified terms are recounted one by one below.
+    constexpr bool RC = TERM == TERM_H;
+    uint32_t acc = 0u, diff = 0u, bad = 0u;
     const uint32_t cls_t = (tp.info >> 2) & 3u;
     const bool win = live && cls_t == CLS_WINDOW;
     uint32_t acch = 0u;
@@ -1462,11 +1482,17 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float y = term_y(__fsub_rn(a4[c], M));
-                acc += __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
-                acc2 += __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
+                const uint32_t r1 = __float_as_uint(fmaf(y, tp.fhi, 12582912.0f));
+                const uint32_t r2 = __float_as_uint(fmaf(y, tp.flo, 12582912.0f));
+                acc += r1;
+                if (RC) {
+                    bad |= r1 != r2 ? 1u << (4 * j + c) : 0u;
+                } else {
+                    acc2 += r2;
+                }
             }
         }
-        diff |= acc ^ acc2;
+        diff |= RC ? bad : (acc ^ acc2);
         acc -= (uint32_t)TILE * 0x4B400000u;   // a tile sums to < 2^22.5
         if (win) {
             const float hh = 0.5f * tp.fhi, hl = 0.5f * tp.flo;
@@ -1500,7 +1526,31 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
             }
         }
     }
-    const bool special = live && ((tp.info & TP_SPECIAL) || diff != 0u);
+    // Entropy pass: a SIMPLE tile with a few uncertified terms keeps its
+    // other counts.  The uncertified terms' estimates come off its sum here
+    // and their exact counts (exp, divide and log each) are added below, one
+    // term per thread, instead of a warp pass over the whole tile.  The tile
+    // still goes to the warp pass if a term is a tie (its count would depend
+    // on the parity), leaves the binade, or the list is full.  (For the
+    // normaliser's cheaper terms the warp pass measured faster.)
+    const bool recount = RC && live && !(tp.info & TP_SPECIAL) && cls_t == CLS_SIMPLE && diff != 0u;
+    if (recount) {
+        uint32_t mb = bad;
+        while (mb) {
+            const int b = __ffs(mb) - 1;
+            mb &= mb - 1u;
+            const float4 q = quad(b >> 2);
+            const float a = (b & 3) == 0 ? q.x : ((b & 3) == 1 ? q.y : ((b & 3) == 2 ? q.z : q.w));
+            acc -= __float_as_uint(fmaf(term_y(__fsub_rn(a, M)), tp.fhi, 12582912.0f)) - 0x4B400000u;
+            const uint32_t slot = atomicAdd(&nrc, 1u);
+            if (slot < RC_CAP) {
+                rcl[slot] = (uint16_t)(((uint32_t)tid << 5) | tile_elem(tid, b >> 2, b & 3));
+            } else {
+                atomicOr(&rc_fb[tid >> 5], 1u << (tid & 31));
+            }
+        }
+    }
+    const bool special = live && ((tp.info & TP_SPECIAL) || (diff != 0u && !recount));
     if (live) {
         TileRec rr;
         rr.lo = (int32_t)(tp.info >> 8) - 128;
@@ -1562,6 +1612,35 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     if (__any_sync(0xffffffffu, nanl != 0) && lane == 0) atomicOr(&nanflag, 1u);
     __syncthreads();
     if (nanflag && tid == 0) atomicOr(&hdr->flags, RF_NAN);
+    if (RC && nrc > 0) {   // block-uniform: read after the barrier
+        // the listed terms' exact counts
+        const uint32_t nr = min(nrc, RC_CAP);
+        const float *sb = reinterpret_cast<const float *>(sbuf);
+        for (uint32_t i = tid; i < nr; i += K12_THREADS) {
+            const uint32_t e = rcl[i], lt = e >> 5;
+            const uint32_t g = seg * SEG_ELEMS + lt * TILE + (e & 31u);
+            float a = staged ? sb[lt * TILE + (e & 31u)] : x[g];
+            if (nwin) a = penalize_once(a, g, swin, nwin, P.rep_penalty);
+            const float pt = TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S);
+            const Comp c = elem_comp(pt, rec[lt].lo);
+            if (c.q0 == c.q1 && c.q0 < QLIM) {
+                atomicAdd(&rec[lt].qlo.q0, c.q0);
+                atomicAdd(&rec[lt].qlo.q1, c.q0);
+            } else {
+                atomicOr(&rc_fb[lt >> 5], 1u << (lt & 31));
+            }
+        }
+        __syncthreads();
+        // a recounted tile with a tie, a term out of the binade or a sum of
+        // 2^24 or more joins the exact pass (which composes such tiles)
+        const bool sp = recount && (((rc_fb[tid >> 5] >> (tid & 31)) & 1u) || rec[tid].qlo.q0 >= QLIM);
+        const uint32_t m = __ballot_sync(0xffffffffu, sp);
+        uint32_t base = 0;
+        if (lane == 0 && m) base = atomicAdd(&nlist, (uint32_t)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (sp) wlist[base + __popc(m & ((1u << lane) - 1u))] = tid;
+        __syncthreads();
+    }
     // warp-cooperative exact pass (lane = element, index order) for tiles
     // whose counts need ordered composition (ties), tiny binades or several
     // binades; several-binade tiles also keep their exact p for the walker
