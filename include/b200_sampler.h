@@ -2,8 +2,8 @@
  * b200_sampler.h -- C ABI of the B200 token sampler.
  *
  * A drop-in for the CPU sampler of llama.zig (src/sampler.zig).  The entry
- * points below are what a Zig caller binds with @cImport;
- * they take plain pointers, sizes and a CUDA stream passed as void*.
+ * points below are what a Zig caller binds with @cImport; they take plain
+ * pointers, sizes and a CUDA stream passed as void*.
  *
  * Interfaces replaced (reference file:line):
  *   bs_config            <- SamplerConfig            src/sampler.zig:4-13
@@ -27,6 +27,15 @@
  * handle must be ordered (same stream or externally synchronised), as a Zig
  * Sampler is single-threaded.  Logits are borrowed device pointers; nothing is
  * copied unless the _host variant is used.
+ *
+ * Rows the sampler could not finish: such a row's token comes back as
+ * 0xFFFFFFFF and its RNG state is left as it was (no draw).  With a handle,
+ * bs_last_device_status reports why; the condition is per call, so the next
+ * call starts clean.
+ *
+ * Repetition penalty: the last min(n_prev, repetition_window) previous ids of
+ * each row are penalised once each, for windows of any length (sampler.zig:
+ * 54-75); ids outside the vocabulary match nothing.
  */
 #ifndef B200_SAMPLER_H
 #define B200_SAMPLER_H
@@ -127,7 +136,10 @@ bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uint32_t *n_ca
  * All calls on one device share the scratch: calls that may overlap in time
  * (different streams or host threads) race and must be ordered by the
  * caller.  The first call on each device resolves the scratch address
- * (cudaGetSymbolAddress) and must not be made while a stream is capturing. */
+ * (cudaGetSymbolAddress) and must not be made while a stream is capturing.
+ * There is no handle to ask for a status: a row this call could not finish
+ * comes back as token 0xFFFFFFFF (its RNG state unchanged), and only that
+ * call's rows are affected. */
 #define BS_STATIC_MAX_ROWS 4
 #define BS_STATIC_MAX_VOCAB 131072
 bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, const float *d_logits, size_t ld,

@@ -521,8 +521,8 @@ __host__ __device__ __forceinline__ uint32_t typical_mode(float typical_p, uint3
 struct K12Params {
     const float *logits;
     size_t ld;
-    const uint32_t *prev;
-    uint32_t n_prev;
+    const uint32_t *pen_bm;   // per handle row: ntiles_total words, bit k of word t = token 32 t + k is
+                              // penalised; nullptr when the repetition penalty is off for this call
     uint32_t vocab;
     uint32_t row0;
     uint32_t rows;
@@ -531,7 +531,6 @@ struct K12Params {
     uint32_t top_k;
     float top_p;
     float min_p;
-    uint32_t rep_window;
     float rep_penalty;
     float typical_p;
     uint32_t tmode;           // TYP_*
@@ -539,7 +538,6 @@ struct K12Params {
     uint32_t ntiles_total;
     TileStat *tstat;          // per handle row: ntiles_total
     SegStat *sstat;           // per handle row: MAX_SEG
-    uint32_t *khist;          // per handle row: MAX_SEG x KH_BINS tile counts
     float *mhist;             // per handle row: MAX_SEG x KH_BINS masses
     RowInfo *rinfo;           // per handle row
     RowHdr *hdr;
@@ -548,11 +546,15 @@ struct K12Params {
     float *wcdata;
     Candidate *cand;          // per handle row: cand_stride entries (idx, logit)
     uint32_t cand_stride;
-    uint32_t *kerr;           // per handle: a bounded device wait gave up
+    uint32_t *kerr;           // per handle: the call whose bounded device wait gave up
+    uint32_t seq;             // this call's sequence number (never 0)
 };
 
-__device__ __forceinline__ bool penalty_active(const K12Params &P) {
-    return P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0;
+__device__ __forceinline__ bool penalty_active(const K12Params &P) { return P.pen_bm != nullptr; }
+
+// The repetition penalty of one logit (sampler.zig:62-66).
+__device__ __forceinline__ float penalize(float a, float pen) {
+    return a > 0.0f ? __fdiv_rn(a, pen) : __fmul_rn(a, pen);
 }
 
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
@@ -566,53 +568,6 @@ __device__ __forceinline__ float4 ldg_policy(const float4 *p, uint64_t pol) {
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                  : "l"(p), "l"(pol));
     return v;
-}
-
-// Load tile t of a row (32 logits; -inf beyond the vocabulary) and apply the
-// repetition penalty (sampler.zig:54-75: each distinct id of the last
-// `window` previous tokens, once).
-__device__ __forceinline__ void load_tile(const K12Params &P, const float *x, uint32_t t, uint64_t pol,
-                                          const uint32_t *win, uint32_t nwin, float v[TILE]) {
-    const uint32_t g0 = t * TILE;
-    if (g0 + TILE <= P.vocab && (reinterpret_cast<uintptr_t>(x + g0) & 15u) == 0) {
-        const float4 *x4 = reinterpret_cast<const float4 *>(x + g0);
-#pragma unroll
-        for (int j = 0; j < TILE / 4; j++) {
-            const float4 q = ldg_policy(x4 + j, pol);
-            v[4 * j] = q.x;
-            v[4 * j + 1] = q.y;
-            v[4 * j + 2] = q.z;
-            v[4 * j + 3] = q.w;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < TILE; j++) v[j] = (g0 + j < P.vocab) ? x[g0 + j] : NEG_INF;
-    }
-    for (uint32_t j = 0; j < nwin; j++) {
-        const uint32_t id = win[j];
-        if (id - g0 < (uint32_t)TILE) {
-            bool first = true;
-            for (uint32_t jj = 0; jj < j; jj++)
-                if (win[jj] == id) { first = false; break; }
-            if (first) {
-#pragma unroll
-                for (int k = 0; k < TILE; k++) {
-                    if ((uint32_t)k == id - g0) {
-                        const float a = v[k];
-                        v[k] = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
-                    }
-                }
-            }
-        }
-    }
-}
-
-__device__ uint32_t load_window(const K12Params &P, uint32_t row, uint32_t *swin) {
-    if (!penalty_active(P)) return 0;
-    const uint32_t win = min(min(P.n_prev, P.rep_window), 256u);
-    const uint32_t start = P.n_prev - win;
-    for (uint32_t j = threadIdx.x; j < win; j += blockDim.x) swin[j] = P.prev[(size_t)row * P.n_prev + start + j];
-    return win;
 }
 
 // Block-wide (K12_THREADS) exclusive scan of one double per thread.
@@ -644,24 +599,13 @@ __device__ double block_exscan1_d(double v, double *wtmp, double *total) {
     return ex;
 }
 
-// One warp handles four tiles at a time: lane l holds elements 4(l%8)..+3 of
-// tile l/8 (an 8-lane group per tile, one float4 load per lane).
-// The repetition penalty on logit a of token g (sampler.zig:54-75): applied
-// once when g is among the window's ids.  Out of line: only rows with a
-// penalty take it.
-__device__ __noinline__ float penalize_once(float a, uint32_t g, const uint32_t *win, uint32_t nwin,
-                                            float rep_penalty) {
-    for (uint32_t j = 0; j < nwin; j++)
-        if (win[j] == g) return a > 0.0f ? __fdiv_rn(a, rep_penalty) : __fmul_rn(a, rep_penalty);
-    return a;
-}
-
-// Logits g .. g+3 from global memory (-inf past the vocabulary) with the
-// repetition penalty applied.  Not inlined: it is the path for rows that
-// cannot be staged in shared memory, and one out-of-line copy keeps the
-// staged loops' instruction footprint small.
+// Logits g .. g+3 (g a multiple of 4) from global memory (-inf past the
+// vocabulary) with the repetition penalty applied to the ids marked in the
+// row's bitmap `bm` (nullptr: no penalty).  Not inlined: it is the path for
+// rows that cannot be staged in shared memory, and one out-of-line copy keeps
+// the staged loops' instruction footprint small.
 __device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vocab, float rep_penalty, uint64_t pol,
-                                         const uint32_t *win, uint32_t nwin) {
+                                         const uint32_t *bm) {
     float4 q;
     if (g + 4 <= vocab && (reinterpret_cast<uintptr_t>(x + g) & 15u) == 0) {
         q = ldg_policy(reinterpret_cast<const float4 *>(x + g), pol);
@@ -671,43 +615,27 @@ __device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vo
         q.z = g + 2 < vocab ? x[g + 2] : NEG_INF;
         q.w = g + 3 < vocab ? x[g + 3] : NEG_INF;
     }
-    // repetition penalty (sampler.zig:54-75): each distinct id of the last
-    // `window` previous tokens, once
-    for (uint32_t j = 0; j < nwin; j++) {
-        const uint32_t id = win[j];
-        if (id - g < 4u) {
-            bool first = true;
-            for (uint32_t jj = 0; jj < j; jj++)
-                if (win[jj] == id) { first = false; break; }
-            if (first) {
-                float *e = (&q.x) + (id - g);
-                const float a = *e;
-                *e = a > 0.0f ? __fdiv_rn(a, rep_penalty) : __fmul_rn(a, rep_penalty);
-            }
-        }
+    if (bm) {
+        const uint32_t bits = (bm[g >> 5] >> (g & 31u)) & 0xFu;
+        if (bits & 1u) q.x = penalize(q.x, rep_penalty);
+        if (bits & 2u) q.y = penalize(q.y, rep_penalty);
+        if (bits & 4u) q.z = penalize(q.z, rep_penalty);
+        if (bits & 8u) q.w = penalize(q.w, rep_penalty);
     }
     return q;
 }
 
-__device__ __forceinline__ float group8_max(float v) {
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
-}
-__device__ __forceinline__ float group8_sum(float v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    return v + __shfl_xor_sync(0xffffffffu, v, 4);
-}
-__device__ __forceinline__ uint32_t group8_sum_u(uint32_t v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    return v + __shfl_xor_sync(0xffffffffu, v, 4);
-}
-__device__ __forceinline__ uint32_t group8_or(uint32_t v) {
-    v |= __shfl_xor_sync(0xffffffffu, v, 1);
-    v |= __shfl_xor_sync(0xffffffffu, v, 2);
-    return v | __shfl_xor_sync(0xffffffffu, v, 4);
+// The repetition penalty on the staged copy of tile `tl` (32 logits at
+// sf[32 tl ..]) of segment `seg`: each id marked in the row's bitmap, once.
+// Called by the tile's owner thread right after the copy landed.
+__device__ __forceinline__ void patch_tile_smem(const K12Params &P, uint32_t hrow, uint32_t seg, uint32_t tl,
+                                                float *sf) {
+    uint32_t bits = P.pen_bm[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tl];
+    while (bits) {
+        const int k = __ffs(bits) - 1;
+        bits &= bits - 1u;
+        sf[tl * TILE + k] = penalize(sf[tl * TILE + k], P.rep_penalty);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -778,17 +706,16 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// The segment can be bulk copied: no penalised ids (they are applied while
-// loading), a 16-byte aligned start and a whole number of 16-byte chunks.
-__device__ __forceinline__ bool seg_bulk_ok(const K12Params &P, const float *xs, uint32_t n, uint32_t nwin) {
-    return nwin == 0 && (reinterpret_cast<uintptr_t>(xs) & 15u) == 0 && (n & 3u) == 0;
+// The segment can be bulk copied: a 16-byte aligned start and a whole number
+// of 16-byte chunks.
+__device__ __forceinline__ bool seg_bulk_ok(const float *xs, uint32_t n) {
+    return (reinterpret_cast<uintptr_t>(xs) & 15u) == 0 && (n & 3u) == 0;
 }
 
 // Issues the segment's bulk copy (thread 0) if it is possible; the caller
 // waits with seg_wait.  Returns whether the copy was issued (block-uniform).
-__device__ __forceinline__ bool seg_issue(const K12Params &P, const float *xs, uint32_t n, uint32_t nwin,
-                                          float4 *sbuf, uint64_t *bar, uint64_t pol) {
-    const bool bulk = seg_bulk_ok(P, xs, n, nwin);
+__device__ __forceinline__ bool seg_issue(const float *xs, uint32_t n, float4 *sbuf, uint64_t *bar, uint64_t pol) {
+    const bool bulk = seg_bulk_ok(xs, n);
     if (bulk && threadIdx.x == 0) {
         mbar_init(bar, 1);
         bulk_load(sbuf, xs, n * 4u, bar, pol);
@@ -805,7 +732,7 @@ __device__ __forceinline__ bool seg_wait(const K12Params &P, uint64_t *bar) {
     const bool ok = mbar_wait(bar, 0u, MBAR_WAIT_NS);
     const bool all = __syncthreads_and(ok) != 0;
     if (!all && threadIdx.x == 0) {
-        atomicOr(P.kerr, 1u);
+        atomicExch(P.kerr, P.seq);
         mbar_wait(bar, 0u, MBAR_WAIT_NS);
     }
     return all;
@@ -819,8 +746,8 @@ __device__ __forceinline__ uint32_t tile_elem(uint32_t tl, int j, int c) {
     return 4u * ((uint32_t)j ^ (tl & 7u)) + (uint32_t)c;
 }
 __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, uint32_t seg, uint32_t tl,
-                                            const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
-                                            uint64_t pol, float v[TILE]) {
+                                            const float4 *sbuf, bool staged, const uint32_t *bm, uint64_t pol,
+                                            float v[TILE]) {
     const uint32_t g0 = seg * SEG_ELEMS + tl * TILE;
     if (staged && g0 + TILE <= P.vocab) {   // every tile but the row's last
 #pragma unroll
@@ -845,7 +772,7 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
     } else {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float4 q = load_quad(x, g0 + tile_elem(tl, j, 0), P.vocab, P.rep_penalty, pol, swin, nwin);
+            const float4 q = load_quad(x, g0 + tile_elem(tl, j, 0), P.vocab, P.rep_penalty, pol, bm);
             v[4 * j] = q.x;
             v[4 * j + 1] = q.y;
             v[4 * j + 2] = q.z;
@@ -857,10 +784,9 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
 // Chunk j of tile `tl` (logits 4 (j ^ (tl & 7)) .. +3, -inf past the
 // vocabulary), from the shared copy or from global memory.
 __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, uint32_t seg, uint32_t tl, int j,
-                                            const float4 *sbuf, bool staged, const uint32_t *swin, uint32_t nwin,
-                                            uint64_t pol) {
+                                            const float4 *sbuf, bool staged, const uint32_t *bm, uint64_t pol) {
     const uint32_t g = seg * SEG_ELEMS + tl * TILE + tile_elem(tl, j, 0);
-    if (!staged) return load_quad(x, g, P.vocab, P.rep_penalty, pol, swin, nwin);
+    if (!staged) return load_quad(x, g, P.vocab, P.rep_penalty, pol, bm);
     float4 q = sbuf[tl * 8 + ((uint32_t)j ^ (tl & 7u))];
     if (g + 4 > P.vocab) {
         q.x = g < P.vocab ? q.x : NEG_INF;
@@ -888,7 +814,6 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
     __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ __align__(8) uint64_t bar;
-    __shared__ uint32_t swin[256];
     __shared__ uint32_t mh[KH_BINS];   // tail element counts per bin
     __shared__ float wm[NW];
     __shared__ uint32_t wf[NW];
@@ -896,9 +821,8 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     // the logits stream through L2 once here: marked evict-first, they do not
     // push out what later kernels reuse (their code, the tile statistics)
     const uint64_t pol = l2_policy_evict_first();
-    const bool pen = penalty_active(P);
-    const bool bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen ? 1u : 0u, sbuf, &bar, pol);
-    const uint32_t nwin = load_window(P, row, swin);
+    const bool bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
+    const uint32_t *bm = penalty_active(P) ? P.pen_bm + (size_t)hrow * P.ntiles_total : nullptr;
     const bool k_floor = P.top_k > 0 && P.top_k < P.vocab && P.top_k <= KSEL_MAX;
     const bool p_active = P.top_p > 0.0f && P.top_p < 1.0f;
     const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
@@ -909,12 +833,14 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) mh[b] = 0u;
     if (t_band)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) th[b] = 0.0f;
-    __syncthreads();   // the barrier's initialisation, the window, mh, th
+    __syncthreads();   // the barrier's initialisation, mh, th
     const bool staged = bulk && seg_wait(P, &bar);
 
     const bool live = (uint32_t)tid < ntile;
+    // the penalty on this thread's own staged tile (read back by it alone)
+    if (staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
     float v[TILE];
-    load_tile32(P, x, seg, live ? tid : 0u, sbuf, staged, swin, nwin, pol, v);
+    load_tile32(P, x, seg, live ? tid : 0u, sbuf, staged, bm, pol, v);
     float tm = NEG_INF;
 #pragma unroll
     for (int k = 0; k < TILE; k++) tm = fmaxf(tm, v[k]);
@@ -1309,7 +1235,6 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const float c2 = P.c2, T = P.T;
     RowHdr *hdr = P.hdr + hrow;
 
-    __shared__ uint32_t swin[256];
     __shared__ double wtmp_d[NW + 1];
     __shared__ double hbase;
     __shared__ uint32_t wtmp_u[NW + 1];
@@ -1335,9 +1260,9 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // once more only by the exact pass, so it need not stay in L2
     const uint64_t pol = l2_policy_evict_first();
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
-    const uint32_t pen = penalty_active(P) ? 1u : 0u;
+    const uint32_t *bm = penalty_active(P) ? P.pen_bm + (size_t)hrow * P.ntiles_total : nullptr;
     bool bulk = false;
-    if (TERM == TERM_P) bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen, sbuf, &bar, pol);
+    if (TERM == TERM_P) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
     // the tile statistics come from the statistics pass, complete before this
     // grid could start (the row reduction lets it launch only after its own
     // wait): load them before waiting for the row reduction
@@ -1347,12 +1272,11 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const RowInfo ri = P.rinfo[hrow];
     const float M = ri.M;
     if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
-    if (TERM == TERM_H) bulk = seg_issue(P, x + seg * SEG_ELEMS, nseg_el, pen, sbuf, &bar, pol);
+    if (TERM == TERM_H) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
     // the entropy pass: S exact, log2 S for the terms' exponents
     const float S = TERM == TERM_H ? hdr->S_exact : 1.0f;
     const double lnS = TERM == TERM_H ? log((double)S) : 0.0;
     const float l2S = (float)(lnS * 1.4426950408889634);
-    const uint32_t nwin = load_window(P, row, swin);
     if (tid == 0) {
         nlist = 0;
         nanflag = 0;
@@ -1447,8 +1371,11 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const bool check_nan = ri.check_nan != 0;
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
     const bool staged = bulk && seg_wait(P, &bar);
+    // the penalty on this thread's own staged tile; other threads read it
+    // only after the barriers below
+    if (staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
     const uint32_t tt = live ? (uint32_t)tid : 0u;
-    auto quad = [&](int j) { return tile_quad(P, x, seg, tt, j, sbuf, staged, swin, nwin, pol); };
+    auto quad = [&](int j) { return tile_quad(P, x, seg, tt, j, sbuf, staged, bm, pol); };
     const uint32_t g0 = seg * SEG_ELEMS + (uint32_t)tid * TILE;
     // certified grid counts of binade lo: y = p / u_lo from the fast exp;
     // y (1 - e) and y (1 + e) bracket the exact value, and the count is the
@@ -1620,7 +1547,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
             const uint32_t e = rcl[i], lt = e >> 5;
             const uint32_t g = seg * SEG_ELEMS + lt * TILE + (e & 31u);
             float a = staged ? sb[lt * TILE + (e & 31u)] : x[g];
-            if (nwin) a = penalize_once(a, g, swin, nwin, P.rep_penalty);
+            if (!staged && bm && ((bm[g >> 5] >> (g & 31u)) & 1u)) a = penalize(a, P.rep_penalty);
             const float pt = TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S);
             const Comp c = elem_comp(pt, rec[lt].lo);
             if (c.q0 == c.q1 && c.q0 < QLIM) {
@@ -1653,16 +1580,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         const uint32_t g = tt * TILE + lane;
         float a = NEG_INF;
         if (g < P.vocab) a = staged ? reinterpret_cast<const float *>(sbuf)[lt * TILE + lane] : x[g];
-        // the penalty, as in load_tile
-        for (uint32_t j = 0; j < nwin; j++) {
-            if (swin[j] == g) {
-                bool first = true;
-                for (uint32_t jj = 0; jj < j; jj++)
-                    if (swin[jj] == g) { first = false; break; }
-                if (first) a = a > 0.0f ? __fdiv_rn(a, P.rep_penalty) : __fmul_rn(a, P.rep_penalty);
-                break;
-            }
-        }
+        // the penalty (the staged copy has it already)
+        if (!staged && bm && g < P.vocab && ((bm[g >> 5] >> (g & 31u)) & 1u)) a = penalize(a, P.rep_penalty);
         const float p = g < P.vocab ? (TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S)) : 0.0f;
         r.qlo = warp_tile_comp(elem_comp(p, r.lo));
         if (r.cls == CLS_WINDOW) r.qhi = warp_tile_comp(elem_comp(p, r.lo + 1));
@@ -1922,8 +1841,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
 struct KBParams {
     const float *logits;
     size_t ld;
-    const uint32_t *prev;
-    uint32_t n_prev;
+    const uint32_t *pen_bm;   // as K12Params::pen_bm
     uint32_t vocab;
     uint32_t row0;
     float T;
@@ -1931,7 +1849,6 @@ struct KBParams {
     float top_p;
     float min_p;
     float typical_p;
-    uint32_t rep_window;
     float rep_penalty;
     uint32_t ntiles_total;
     RowHdr *hdr;
@@ -1943,7 +1860,8 @@ struct KBParams {
     uint32_t cand_stride;
     uint64_t *rng;       // per handle row, 4 words
     RowTrace *trace;     // per handle row
-    const uint32_t *kerr;
+    const uint32_t *kerr;   // == seq: a bounded wait of this call gave up
+    uint32_t seq;
     const RowInfo *rinfo;   // per handle row
     uint32_t tmode;      // TYP_*
     uint32_t *out;       // per call row
@@ -2024,22 +1942,20 @@ __global__ void crossing_check_kernel(WTile *scratch, uint32_t max_ntl, unsigned
     }
 }
 
-// Exact p of element g (with the repetition penalty), for the recompute path.
+// Exact p of element g (with the repetition penalty when the row's bitmap
+// `bm` marks it), for the recompute path.
 __device__ __forceinline__ float exact_p_raw(const float *xrow, uint32_t vocab, uint32_t g, float M, float T,
-                                             float pen, const uint32_t *win, uint32_t nwin) {
+                                             float pen, const uint32_t *bm) {
     if (g >= vocab) return 0.0f;
     float v = xrow[g];
-    for (uint32_t j = 0; j < nwin; j++) {
-        if (win[j] == g) {
-            v = v > 0.0f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
-            break;
-        }
-    }
+    if (bm && ((bm[g >> 5] >> (g & 31u)) & 1u)) v = penalize(v, pen);
     return prob_unnorm(v, M, T);
 }
-__device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M, const uint32_t *win,
-                            uint32_t nwin) {
-    return exact_p_raw(P.logits + (size_t)row * P.ld, P.vocab, g, M, P.T, P.rep_penalty, win, nwin);
+__device__ __forceinline__ const uint32_t *row_bitmap(const KBParams &P, uint32_t hrow) {
+    return P.pen_bm ? P.pen_bm + (size_t)hrow * P.ntiles_total : nullptr;
+}
+__device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t hrow, uint32_t g, float M) {
+    return exact_p_raw(P.logits + (size_t)row * P.ld, P.vocab, g, M, P.T, P.rep_penalty, row_bitmap(P, hrow));
 }
 
 // The walker's recompute path: the warp adds one tile's terms, p (TERM_P)
@@ -2048,10 +1964,10 @@ __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t g, float M
 // and inlined it would sit in the middle of the walk's hot code.
 template <int TERM>
 __device__ __noinline__ float walk_recompute_tile(float s, const float *xrow, uint32_t vocab, uint32_t tile, float M,
-                                                  float T, float pen, const uint32_t *win, uint32_t nwin, float S,
+                                                  float T, float pen, const uint32_t *bm, float S,
                                                   float *tilep) {
     const uint32_t lane = threadIdx.x & 31u;
-    float t = exact_p_raw(xrow, vocab, tile * TILE + lane, M, T, pen, win, nwin);
+    float t = exact_p_raw(xrow, vocab, tile * TILE + lane, M, T, pen, bm);
     if (TERM == TERM_H) {
         const float Pn = __fdiv_rn(t, S);
         t = Pn > 0.0f ? __fmul_rn(Pn, -log_ref(Pn)) : 0.0f;
@@ -2231,8 +2147,8 @@ __device__ __forceinline__ uint32_t seq_draw(Get get, uint32_t n, float r) {
 // kept tokens are then taken in probability order (stable) for the mass and
 // the inverse-CDF draw.  In band mode the kept set is trusted only when every
 // token up to the crossing's dev is surely inside the band.
-__device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, float H, const uint32_t *swin,
-                             uint32_t nwin, unsigned long long *skeys, float *sprobs, unsigned long long *red2) {
+__device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, float H, unsigned long long *skeys,
+                             float *sprobs, unsigned long long *red2) {
     const int tid = threadIdx.x;
     RowHdr *hdr = P.hdr + hrow;
     const RowInfo ri = P.rinfo[hrow];
@@ -2270,11 +2186,11 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
     // 2. P in dev order, recomputed from the logits as the normaliser pass did
     float *pd = big ? reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0) : sprobs;
     for (uint32_t i = tid; i < n; i += KB_THREADS)
-        pd[i] = __fdiv_rn(exact_p_at(P, row, (uint32_t)keys[i], M, swin, nwin), S);
+        pd[i] = __fdiv_rn(exact_p_at(P, row, hrow, (uint32_t)keys[i], M), S);
     __syncthreads();
     // 3. cum_typ (sequential f32 in dev order)
     if (tid == 0) {
-        uint32_t nk = n, st = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+        uint32_t nk = n, st = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
         float cum = 0.0f;
         nk = seq_first_exceed([&](uint32_t i) { return pd[i]; }, n, P.typical_p, cum);
         const bool crossed = nk < n;
@@ -2361,7 +2277,6 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     __shared__ __align__(8) WTile wpool[WPOOL];
     __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1], wcnt[KB_THREADS / 32], n_fit;
     __shared__ __align__(16) float tilep[TILE];   // a recomputed tile's p, for the walker
-    __shared__ uint32_t swin[256];
     __shared__ float S_sh;
     __shared__ uint32_t walk_flags, walk_items, walk_slow, n_zero;
     __shared__ unsigned long long red2[2];
@@ -2392,14 +2307,6 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     // the stored exact terms (rows of WC_CAP * TILE floats, 16-byte aligned)
     const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
     for (uint32_t i = tid; i < n_wc * (TILE / 4); i += KB_THREADS) cp_async16(wcs + 4 * i, wcg + 4 * i);
-    // penalty window (for the recompute path)
-    uint32_t nwin = 0;
-    if (P.rep_penalty != 1.0f && P.n_prev > 0 && P.prev != nullptr && P.rep_window > 0) {
-        const uint32_t win = min(min(P.n_prev, P.rep_window), 256u);
-        const uint32_t start = P.n_prev - win;
-        for (uint32_t j = tid; j < win; j += KB_THREADS) cp_async4(swin + j, P.prev + (size_t)row * P.n_prev + start + j);
-        nwin = win;
-    }
     if ((uint32_t)tid < nseg) s_nit[tid] = min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES));
     cp_async_wait_all();
     const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
@@ -2495,8 +2402,8 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         // add one tile element by element, p recomputed from the logits
         const float *xrow = P.logits + (size_t)row * P.ld;
         auto add_tile = [&](uint32_t tile) {
-            st = state_of(walk_recompute_tile<TERM>(float_of(st), xrow, P.vocab, tile, M, P.T, P.rep_penalty, swin,
-                                                    nwin, Sx, tilep));
+            st = state_of(walk_recompute_tile<TERM>(float_of(st), xrow, P.vocab, tile, M, P.T, P.rep_penalty,
+                                                    row_bitmap(P, hrow), Sx, tilep));
         };
         // everything but the common case: a WINDOW crossing, a stored or
         // recomputed tile, a running sum outside the item's binades
@@ -2633,7 +2540,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     }
     __syncthreads();
     if (TERM == TERM_H) {
-        typical_tail(P, row, hrow, S_sh, swin, nwin, skeys, sprobs, red2);
+        typical_tail(P, row, hrow, S_sh, skeys, sprobs, red2);
         return;
     }
 
@@ -2696,7 +2603,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     }
     if (tid != 0) return;
 
-    uint32_t status = *P.kerr ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+    uint32_t status = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
     bool pending = false;
     uint32_t token = 0;
     uint32_t path = 0;
@@ -2827,6 +2734,25 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     P.trace[hrow] = tr;
 }
 
+// Repetition-penalty pre-pass (sampler.zig:54-75), one CTA per row: the
+// row's bitmap of penalised ids, bit k of word t for token 32 t + k.  The
+// reference penalises each token id found among the last `win` previous
+// tokens once, however often it occurs there; ids outside the vocabulary
+// match no logit.
+__global__ void __launch_bounds__(256) k0_penalty(const uint32_t *__restrict__ prev, uint32_t n_prev, uint32_t win,
+                                                  uint32_t vocab, uint32_t row0, uint32_t words,
+                                                  uint32_t *__restrict__ bm) {
+    const uint32_t row = blockIdx.x;
+    uint32_t *b = bm + (size_t)(row0 + row) * words;
+    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) b[i] = 0u;
+    __syncthreads();
+    const uint32_t *p = prev + (size_t)row * n_prev + (n_prev - win);
+    for (uint32_t j = threadIdx.x; j < win; j += blockDim.x) {
+        const uint32_t id = p[j];
+        if (id < vocab) atomicOr(&b[id >> 5], 1u << (id & 31u));
+    }
+}
+
 }  // namespace bs
 
 // ===========================================================================
@@ -2840,12 +2766,12 @@ struct bs_sampler {
     uint32_t vocab;
     int device;
     uint32_t nseg, ntiles_total;
-    size_t smem_a, smem_b;
+    size_t smem_b;
     uint64_t *d_rng;
     RowHdr *d_hdr;
     TileStat *d_tstat;
     SegStat *d_sstat;
-    uint32_t *d_khist;
+    uint32_t *d_penbm;       // repetition-penalty bitmaps, ntiles_total words per row
     float *d_mhist;
     RowInfo *d_rinfo;
     Item *d_items;
@@ -2855,7 +2781,8 @@ struct bs_sampler {
     unsigned long long *d_ctmp;
     uint32_t cand_stride;
     RowTrace *d_trace;
-    uint32_t *d_kerr;        // sticky: a bounded device wait gave up
+    uint32_t *d_kerr;        // sequence number of the last call whose bounded device wait gave up
+    uint32_t seq;            // sequence number of the last call (0 before the first)
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -2911,7 +2838,7 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_hdr);
     cudaFree(s->d_tstat);
     cudaFree(s->d_sstat);
-    cudaFree(s->d_khist);
+    cudaFree(s->d_penbm);
     cudaFree(s->d_mhist);
     cudaFree(s->d_rinfo);
     cudaFree(s->d_items);
@@ -2929,21 +2856,29 @@ static void free_all(bs_sampler *s) {
     delete[] s->prof_ev;
 }
 
-// The dynamic shared-memory limit is a per-function attribute: keep it at the
-// largest size any handle in this process needs.
-static size_t g_smem_a = 0, g_smem_b = 0;
-static cudaError_t raise_smem_limits(size_t a, size_t b) {
-    cudaError_t e = cudaSuccess;
-    if (a > g_smem_a) {
-        e = cudaFuncSetAttribute(k1_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)a);
-        if (e == cudaSuccess) g_smem_a = a;
-    }
-    if (e == cudaSuccess && b > g_smem_b) {
-        e = cudaFuncSetAttribute(kernel_b<TERM_P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel_b<TERM_H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)b);
-        if (e == cudaSuccess) g_smem_b = b;
-    }
+// Dynamic shared memory of the walk kernel (candidate keys, stored terms,
+// probabilities).
+constexpr size_t KB_SMEM = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+
+// Kernel attributes are per device: set them once on each device, with that
+// device current.
+constexpr int MAX_DEVICES = 64;
+static bool g_attrs_set[MAX_DEVICES];
+static std::mutex g_attrs_mu;
+static cudaError_t ensure_kernel_attrs(int dev) {
+    if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_attrs_mu);
+    if (g_attrs_set[dev]) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel_b<TERM_P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KB_SMEM);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel_b<TERM_H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KB_SMEM);
+    if (e == cudaSuccess) g_attrs_set[dev] = true;
     return e;
+}
+
+// The next sequence number of a call (never 0, the value of a clear error word).
+static uint32_t next_seq(uint32_t &seq) {
+    seq = seq + 1u == 0u ? 1u : seq + 1u;
+    return seq;
 }
 
 extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vocab, int device,
@@ -2961,8 +2896,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     s->device = device;
     s->ntiles_total = (vocab + TILE - 1) / TILE;
     s->nseg = (s->ntiles_total + SEG_TILES - 1) / SEG_TILES;
-    s->smem_a = 0;
-    s->smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+    s->smem_b = KB_SMEM;
     s->cand_stride = (vocab + 31u) & ~31u;
 
     cudaError_t e = cudaSuccess;
@@ -2970,7 +2904,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     if (e == cudaSuccess) e = cudaMalloc(&s->d_hdr, (size_t)batch * sizeof(RowHdr));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_tstat, (size_t)batch * s->ntiles_total * sizeof(TileStat));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_sstat, (size_t)batch * MAX_SEG * sizeof(SegStat));
-    if (e == cudaSuccess) e = cudaMalloc(&s->d_khist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_penbm, (size_t)batch * s->ntiles_total * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_mhist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_rinfo, (size_t)batch * sizeof(RowInfo));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_items, (size_t)batch * s->ntiles_total * sizeof(Item));
@@ -3002,7 +2936,7 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     delete[] h;
     if (e == cudaSuccess) e = cudaMemset(s->d_trace, 0, (size_t)batch * sizeof(RowTrace));
     if (e == cudaSuccess) e = cudaMemset(s->d_kerr, 0, sizeof(uint32_t));
-    if (e == cudaSuccess) e = raise_smem_limits(s->smem_a, s->smem_b);
+    if (e == cudaSuccess) e = ensure_kernel_attrs(device);
     if (e != cudaSuccess) {
         fprintf(stderr, "b200_sampler: setup failed: %s\n", cudaGetErrorString(e));
         free_all(s);
@@ -3046,9 +2980,9 @@ static cudaError_t launch_dependent(void (*kern)(Args...), dim3 grid, dim3 block
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, uint32_t row0,
-                               uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out,
-                               void *stream) {
+// One sampling call; `seq` numbers it for the error word (never 0).
+static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
+                             uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, void *stream) {
     if (!s || !d_logits || !d_out || ld < s->vocab) return BS_EINVAL;
     if (row0 > s->batch || rows > s->batch - row0) return BS_EINVAL;
     if (rows == 0) return BS_OK;
@@ -3057,11 +2991,14 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     // sampler.zig:50 -- temperature <= 0: argmax of the raw logits, no draw
     if (c.temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, s->vocab, d_out, stream);
 
+    // sampler.zig:58 -- the penalty applies to the last min(n_prev, window) ids
+    const bool pen = c.repetition_penalty != 1.0f && d_prev != nullptr && n_prev > 0 && c.repetition_window > 0;
+    const uint32_t win = pen ? (n_prev < c.repetition_window ? n_prev : c.repetition_window) : 0u;
+
     K12Params A;
     A.logits = d_logits;
     A.ld = ld;
-    A.prev = d_prev;
-    A.n_prev = d_prev ? n_prev : 0;
+    A.pen_bm = pen ? s->d_penbm : nullptr;
     A.vocab = s->vocab;
     A.row0 = row0;
     A.rows = rows;
@@ -3070,13 +3007,11 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.top_k = c.top_k;
     A.top_p = c.top_p;
     A.min_p = c.min_p;
-    A.rep_window = c.repetition_window;
     A.rep_penalty = c.repetition_penalty;
     A.nseg = s->nseg;
     A.ntiles_total = s->ntiles_total;
     A.tstat = s->d_tstat;
     A.sstat = s->d_sstat;
-    A.khist = s->d_khist;
     A.mhist = s->d_mhist;
     A.rinfo = s->d_rinfo;
     A.hdr = s->d_hdr;
@@ -3086,14 +3021,14 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     A.cand = s->d_cand;
     A.cand_stride = s->cand_stride;
     A.kerr = s->d_kerr;
+    A.seq = seq;
     A.typical_p = c.typical_p;
     A.tmode = typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p);
 
     KBParams B;
     B.logits = d_logits;
     B.ld = ld;
-    B.prev = A.prev;
-    B.n_prev = A.n_prev;
+    B.pen_bm = A.pen_bm;
     B.vocab = s->vocab;
     B.row0 = row0;
     B.T = c.temperature;
@@ -3101,7 +3036,6 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.top_p = c.top_p;
     B.min_p = c.min_p;
     B.typical_p = c.typical_p;
-    B.rep_window = c.repetition_window;
     B.rep_penalty = c.repetition_penalty;
     B.ntiles_total = s->ntiles_total;
     B.hdr = s->d_hdr;
@@ -3114,6 +3048,7 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     B.rng = s->d_rng;
     B.trace = s->d_trace;
     B.kerr = s->d_kerr;
+    B.seq = seq;
     B.rinfo = s->d_rinfo;
     B.tmode = A.tmode;
     B.out = d_out;
@@ -3128,6 +3063,7 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     // statistics pass)
     const dim3 g12(s->nseg, rows), g2(s->nseg * rows);
     if (ev) cudaEventRecord(ev[0], st);
+    if (pen) k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, row0, s->ntiles_total, s->d_penbm);
     k1_stats<<<g12, K12_THREADS, 0, st>>>(A);
     cudaError_t e = launch_dependent(k1_rows, dim3(rows), dim3(K12_THREADS), 0, st, A);
     if (ev) cudaEventRecord(ev[1], st);
@@ -3144,6 +3080,13 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
     return cuda_status(e);
+}
+
+extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, uint32_t row0,
+                               uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out,
+                               void *stream) {
+    if (!s) return BS_EINVAL;
+    return sample_impl(s, next_seq(s->seq), d_logits, ld, row0, rows, d_prev, n_prev, d_out, stream);
 }
 
 extern "C" bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t ld, uint32_t row0,
@@ -3395,14 +3338,14 @@ extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uin
 // from one fixed static device array instead of a handle's allocations.  The
 // caller owns the RNG state (a device buffer of rows x 4 u64).
 constexpr size_t r256(size_t b) { return (b + 255) & ~(size_t)255; }
-constexpr int STATIC_NBUF = 13;
+constexpr int STATIC_NBUF = 13;   // the buffers of a handle, in the order below
 struct StaticSizes {
     size_t b[STATIC_NBUF];
 };
 constexpr StaticSizes static_sizes(uint32_t rows, uint32_t vocab) {
     const size_t nt = (vocab + TILE - 1) / TILE, cs = (vocab + 31u) & ~31u;
     return StaticSizes{{r256(rows * sizeof(RowHdr)), r256(rows * nt * sizeof(TileStat)),
-                        r256(rows * MAX_SEG * sizeof(SegStat)), r256(rows * MAX_SEG * KH_BINS * sizeof(uint32_t)),
+                        r256(rows * MAX_SEG * sizeof(SegStat)), r256(rows * nt * sizeof(uint32_t)),
                         r256(rows * MAX_SEG * KH_BINS * sizeof(float)), r256(rows * sizeof(RowInfo)), r256(rows * nt * sizeof(Item)), r256(rows * nt * sizeof(WTile)),
                         r256(rows * WC_CAP * TILE * sizeof(float)), r256(rows * cs * sizeof(Candidate)),
                         r256(rows * 2 * cs * sizeof(unsigned long long)), r256(rows * sizeof(RowTrace)),
@@ -3419,26 +3362,26 @@ constexpr size_t static_total(uint32_t rows, uint32_t vocab) {
 constexpr size_t STATIC_BYTES = static_total(BS_STATIC_MAX_ROWS, BS_STATIC_MAX_VOCAB);
 static __device__ __align__(256) unsigned char g_static_scratch[STATIC_BYTES];
 
-constexpr int STATIC_MAX_DEVICES = 64;
-static unsigned char *g_static_base[STATIC_MAX_DEVICES];
+static unsigned char *g_static_base[MAX_DEVICES];
+static uint32_t g_static_seq[MAX_DEVICES];   // sequence numbers of the static calls, per device
 static std::mutex g_static_mu;
 
 // Address of this device's copy of the static scratch, resolved once per
-// device (with the kernel's shared-memory attribute raised there).
-static cudaError_t static_scratch_base(int dev, unsigned char **base) {
-    if (dev < 0 || dev >= STATIC_MAX_DEVICES) return cudaErrorInvalidDevice;
+// device (with the kernel attributes set there), and the call's sequence
+// number for the error word in that scratch.
+static cudaError_t static_scratch_base(int dev, unsigned char **base, uint32_t *seq) {
+    if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_static_mu);
     if (!g_static_base[dev]) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess) return e;
-        const size_t smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
-        e = cudaFuncSetAttribute(kernel_b<TERM_P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel_b<TERM_H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b);
+        e = ensure_kernel_attrs(dev);
         if (e != cudaSuccess) return e;
         g_static_base[dev] = static_cast<unsigned char *>(p);
     }
     *base = g_static_base[dev];
+    *seq = next_seq(g_static_seq[dev]);
     return cudaSuccess;
 }
 
@@ -3458,7 +3401,8 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     int dev = 0;
     BS_CUDA(cudaGetDevice(&dev));
     unsigned char *base = nullptr;
-    const cudaError_t e = static_scratch_base(dev, &base);
+    uint32_t seq = 0;
+    const cudaError_t e = static_scratch_base(dev, &base, &seq);
     if (e != cudaSuccess) {
         fprintf(stderr, "b200_sampler: bs_sample_static: static scratch set-up failed: %s\n", cudaGetErrorString(e));
         return BS_ECUDA;
@@ -3472,7 +3416,7 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     s.device = dev;
     s.ntiles_total = (vocab + TILE - 1) / TILE;
     s.nseg = (s.ntiles_total + SEG_TILES - 1) / SEG_TILES;
-    s.smem_b = (size_t)CAND_SMEM * 8 + (size_t)WC_CAP * TILE * 4 + (size_t)CAND_SMEM * 4;
+    s.smem_b = KB_SMEM;
     s.cand_stride = (vocab + 31u) & ~31u;
     s.d_rng = d_rng;
     const StaticSizes sz = static_sizes(rows, vocab);
@@ -3485,7 +3429,7 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     s.d_hdr = static_cast<RowHdr *>(ptr[0]);
     s.d_tstat = static_cast<TileStat *>(ptr[1]);
     s.d_sstat = static_cast<SegStat *>(ptr[2]);
-    s.d_khist = static_cast<uint32_t *>(ptr[3]);
+    s.d_penbm = static_cast<uint32_t *>(ptr[3]);
     s.d_mhist = static_cast<float *>(ptr[4]);
     s.d_rinfo = static_cast<RowInfo *>(ptr[5]);
     s.d_items = static_cast<Item *>(ptr[6]);
@@ -3494,9 +3438,10 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     s.d_cand = static_cast<Candidate *>(ptr[9]);
     s.d_ctmp = static_cast<unsigned long long *>(ptr[10]);
     s.d_trace = static_cast<RowTrace *>(ptr[11]);
-    s.d_kerr = static_cast<uint32_t *>(ptr[12]);   // zero at load; sticky like a handle's
+    s.d_kerr = static_cast<uint32_t *>(ptr[12]);
     // nothing in the scratch has to start at zero: every buffer a call reads
-    // is written earlier in the same call (the error word is zero at load and
-    // only ever set)
-    return bs_sample(&s, d_logits, ld, 0, rows, d_prev, n_prev, d_out, stream);
+    // is written earlier in the same call, and the error word holds the
+    // sequence number of a failed call (zero at load), never this call's
+    // unless this call's own wait gave up
+    return sample_impl(&s, seq, d_logits, ld, 0, rows, d_prev, n_prev, d_out, stream);
 }

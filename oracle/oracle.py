@@ -54,6 +54,8 @@ class OrcTrace(ctypes.Structure):
         ("sum_f64", ctypes.c_double),
         ("cut_topp", ctypes.c_uint32),
         ("_pad", ctypes.c_uint32),
+        ("draw_margin", ctypes.c_double),
+        ("thr_margin", ctypes.c_double),
     ]
 
 
@@ -173,3 +175,36 @@ def sample_batch(cfg: OrcConfig, logits: np.ndarray, seeds=None, states=None, pr
         raise MemoryError("oracle: allocation failed")
     st = np.array([[samplers[r].s[i] for i in range(4)] for r in range(rows)], dtype=np.uint64)
     return out, traces, st
+
+
+def parity_report(got_tokens, ref_tokens, traces, draw_eps: float = 1e-6) -> dict:
+    """Parity counts of one sampled batch against the checker, as the spec asks.
+
+    A row is a draw-boundary case when the reference's uniform draw lies within
+    ``draw_eps`` of a boundary of the kept tokens' CDF (``draw_margin``), and a
+    threshold-boundary case when a filter decision lies closer to its
+    threshold than the reference's own normaliser error (the relative error of
+    its sequential f32 sum against the f64 sum of the same terms).  Mismatches
+    are split by those classes; ``mismatch_other`` must be 0.
+    """
+    got = np.asarray(got_tokens, dtype=np.uint32).ravel()
+    ref = np.asarray(ref_tokens, dtype=np.uint32).ravel()
+    rows = len(ref)
+    draw_b = np.zeros(rows, bool)
+    thr_b = np.zeros(rows, bool)
+    for r in range(rows):
+        t = traces[r]
+        draw_b[r] = t.draw_margin < draw_eps
+        rel = abs(t.sum - t.sum_f64) / t.sum_f64 if t.sum_f64 > 0 else 0.0
+        thr_b[r] = t.thr_margin < rel
+    bad = got != ref
+    return {
+        "rows": int(rows),
+        "exact": int((~bad).sum()),
+        "draw_boundary_rows": int(draw_b.sum()),
+        "threshold_boundary_rows": int(thr_b.sum()),
+        "mismatch_draw_boundary": int((bad & draw_b).sum()),
+        "mismatch_threshold_boundary": int((bad & thr_b & ~draw_b).sum()),
+        "mismatch_other": int((bad & ~draw_b & ~thr_b).sum()),
+        "draw_eps": draw_eps,
+    }

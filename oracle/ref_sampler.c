@@ -256,6 +256,8 @@ uint32_t orc_sample(orc_sampler *sp, const float *logits, size_t n,
     tr->u = NAN;
     tr->r0 = NAN;
     tr->cut_topp = (uint32_t)n;
+    tr->draw_margin = INFINITY;
+    tr->thr_margin = INFINITY;
 
     /* sampler.zig:50 */
     if (cfg->temperature <= 0.0f) {
@@ -334,9 +336,14 @@ uint32_t orc_sample(orc_sampler *sp, const float *logits, size_t n,
         for (size_t j = 0; j < n; j++) {
             const uint32_t idx = indices[j];
             if (!selected[idx]) continue;
+            const float before = cum_p;
             cum_p = cum_p + probs[idx];
             if (cum_p > cfg->top_p) {
-                if (tr->cut_topp == (uint32_t)n) tr->cut_topp = (uint32_t)j;
+                if (tr->cut_topp == (uint32_t)n) {
+                    tr->cut_topp = (uint32_t)j;
+                    const double m = fmin((double)cum_p - cfg->top_p, (double)cfg->top_p - before) / cfg->top_p;
+                    if (m < tr->thr_margin) tr->thr_margin = m;
+                }
                 selected[idx] = 0;
             }
         }
@@ -347,7 +354,12 @@ uint32_t orc_sample(orc_sampler *sp, const float *logits, size_t n,
         const float p_thresh = max_prob * cfg->min_p;
         for (size_t j = 0; j < n; j++) {
             const uint32_t idx = indices[j];
-            if (selected[idx] && probs[idx] < p_thresh) selected[idx] = 0;
+            if (!selected[idx]) continue;
+            if (p_thresh > 0.0f) {
+                const double m = fabs((double)probs[idx] - p_thresh) / p_thresh;
+                if (m < tr->thr_margin) tr->thr_margin = m;
+            }
+            if (probs[idx] < p_thresh) selected[idx] = 0;
         }
     }
     /* :128-154 typical-p: entropy over the full distribution (index order),
@@ -374,11 +386,21 @@ uint32_t orc_sample(orc_sampler *sp, const float *logits, size_t n,
         }
         stable_sort_idx(order, tmp, n, dev, 0);
         float cum_typ = 0.0f;
+        int cut = 0;
         for (size_t j = 0; j < n; j++) {
             const uint32_t idx = order[j];
             if (!selected[idx]) continue;
+            const float before = cum_typ;
             cum_typ = cum_typ + probs[idx];
-            if (cum_typ > cfg->typical_p) selected[idx] = 0;
+            if (cum_typ > cfg->typical_p) {
+                if (!cut) {
+                    cut = 1;
+                    const double m =
+                        fmin((double)cum_typ - cfg->typical_p, (double)cfg->typical_p - before) / cfg->typical_p;
+                    if (m < tr->thr_margin) tr->thr_margin = m;
+                }
+                selected[idx] = 0;
+            }
         }
         free(dev);
         free(order);
@@ -412,10 +434,12 @@ uint32_t orc_sample(orc_sampler *sp, const float *logits, size_t n,
         for (size_t j = 0; j < n; j++) {
             const uint32_t idx = indices[j];
             if (!selected[idx]) continue;
+            const float before = r;
             r = r - probs[idx];
             if (r <= 0.0f) {
                 token = idx;
                 tr->path = ORC_PATH_DRAW;
+                tr->draw_margin = fmin((double)before, -(double)r) / (double)total;
                 break;
             }
         }

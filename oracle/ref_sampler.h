@@ -63,6 +63,16 @@ typedef struct orc_trace {
     double sum_f64;         /* exact-ish f64 sum of the same p_i (diagnostic) */
     uint32_t cut_topp;      /* sorted position of the first token top-p cut (n if none) */
     uint32_t _pad;
+    /* Parity classification (diagnostics, not part of the reference):
+     * draw_margin: distance of the draw u to the nearest boundary of the kept
+     *   tokens' CDF, in units of u (r before and after the winning subtraction,
+     *   divided by the kept mass); +inf without a draw.
+     * thr_margin: the smallest relative distance of a filter decision to its
+     *   threshold (top-p's running sum against top_p at the cut, min-p's
+     *   kept/cut probabilities against p_max * min_p, typical-p's running sum
+     *   against typical_p at its cut); +inf when no such decision was made. */
+    double draw_margin;
+    double thr_margin;
 } orc_trace;
 
 enum {

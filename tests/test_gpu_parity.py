@@ -45,7 +45,8 @@ def run_oracle(orc, c, logits_steps, seeds, prev_steps=None):
     toks, sts, trs = [], [], []
     for i in range(logits_steps.shape[0]):
         out, tr, states = orc.sample_batch(oc, logits_steps[i], seeds=seeds if states is None else None,
-                                           states=states, prev=None if prev_steps is None else prev_steps[i])
+                                           states=states, prev=None if prev_steps is None else prev_steps[i],
+                                           nthreads=os.cpu_count() or 1)
         toks.append(out)
         sts.append(states)
         trs.append([(t.sum, t.total, t.u, t.path) for t in tr])
@@ -83,6 +84,23 @@ def test_reference_tests_through_c_abi(gpu_pkg):
     c.update(top_k=1, seed=1)
     x = np.tile(np.array([2.0, 1.9, 1.8], np.float32), (16, 1, 1))
     assert run_gpu(gpu_pkg, c, x, seeds=[1])[0].ravel().tolist() == [0] * 16
+
+
+def test_xoshiro256pp_known_answer_on_gpu(gpu_pkg):
+    # the published xoshiro256++ vector from the state {1, 2, 3, 4}: one draw
+    # consumes the first output, 41943041, whose Random.float(f32) value is
+    # 2^-39 (1 + 2^-23); the state then is {7, 0, 262146, 6 * 2^45}
+    c = gpu_pkg.SamplerConfig(temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, typical_p=1.0, seed=1,
+                              repetition_window=0, repetition_penalty=1.0)
+    s = gpu_pkg.Sampler(c, batch=1, vocab=4)
+    s.rng_state = np.array([[1, 2, 3, 4]], np.uint64)
+    tok = s.sample(torch.zeros((1, 4), dtype=torch.float32, device="cuda"))
+    torch.cuda.synchronize()
+    assert int(tok.cpu()[0]) == 0          # r = u * 1 <= 0.25: the first token
+    tr = s.traces()[0]
+    assert np.float32(tr.u) == np.float32(2.0 ** -39 * (1 + 2.0 ** -23))
+    assert s.rng_state.tolist() == [[7, 0, 262146, 6 << 45]]
+    s.close()
 
 
 GOLDEN = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
@@ -135,11 +153,14 @@ def _workload(pkg, name, rows, steps=1):
     return w, x
 
 
+# every configuration at its full batch (c4's 512 rows on one GPU here; its
+# vocabulary-sharded form is tested in test_gpu_vocab_shard.py)
 @pytest.mark.parametrize("name,rows,steps", [
     ("c1", 64, 2),
     ("headline", 256, 1),
-    ("headline_topp", 128, 1),
-    ("c4", 64, 1),
+    ("headline_topp", 256, 1),
+    ("c2", 256, 1),
+    ("c4", 512, 1),
     ("c0", 1, 40),
 ])
 def test_benchmark_configs_match_checker(gpu_pkg, orc, name, rows, steps):
@@ -150,9 +171,10 @@ def test_benchmark_configs_match_checker(gpu_pkg, orc, name, rows, steps):
 
 
 def test_topk1_large_vocab(gpu_pkg, orc):
-    w, x = _workload(gpu_pkg, "c3_topk1", 32)
+    # config 3's top_k = 1 run at its full size, 1024 rows x 256000
+    w, x = _workload(gpu_pkg, "c3_topk1", 1024)
     c = w.config()
-    seeds = w.seeds(32)
+    seeds = w.seeds(1024)
     assert_same(run_gpu(gpu_pkg, c, x, seeds), run_oracle(orc, c, x, seeds), "c3_topk1")
 
 
@@ -217,6 +239,27 @@ def test_repetition_penalty(gpu_pkg, orc):
     c = w.config(repetition_window=16, repetition_penalty=1.5)
     seeds = w.seeds(8)
     assert_same(run_gpu(gpu_pkg, c, x, seeds, prev), run_oracle(orc, c, x, seeds, prev), "penalty")
+
+
+@pytest.mark.parametrize("window,n_prev", [(300, 400), (1000, 400), (5000, 6000)])
+def test_repetition_penalty_long_window(gpu_pkg, orc, window, n_prev):
+    # windows of any length (sampler.zig:58: the last min(n_prev, window) ids):
+    # the likely tokens sit inside the window, decoys just before it must stay
+    # unpenalised, ids past the vocabulary match nothing
+    w, x = _workload(gpu_pkg, "c1", 6, steps=1)
+    rng = np.random.default_rng(window)
+    prev = rng.integers(0, w.vocab, size=(1, 6, n_prev)).astype(np.uint32)
+    order = np.argsort(-x, axis=2)
+    win = min(window, n_prev)
+    prev[:, :, n_prev - win:n_prev - win + 4] = order[:, :, :4]      # oldest ids inside the window
+    prev[:, :, n_prev - 3] = order[:, :, 0]                          # repeated: penalised once
+    prev[:, :, n_prev - 2] = w.vocab + 7                             # outside the vocabulary
+    if n_prev > win:
+        prev[:, :, n_prev - win - 1] = order[:, :, 4]                # just outside the window
+    c = w.config(repetition_window=window, repetition_penalty=1.3)
+    seeds = w.seeds(6)
+    assert_same(run_gpu(gpu_pkg, c, x, seeds, prev), run_oracle(orc, c, x, seeds, prev),
+                f"penalty window={window} n_prev={n_prev}")
 
 
 def test_certificate_bound_holds(gpu_pkg):

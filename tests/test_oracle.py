@@ -43,6 +43,60 @@ def test_splitmix64_known_outputs(orc):
                                     0x06C45D188009454F, 0xF88BB8A8724C81EC]
 
 
+def test_xoshiro256pp_published_vector(orc):
+    # xoshiro256++ (Blackman & Vigna) from the state {1, 2, 3, 4}: the
+    # published reference outputs.  The first two follow by hand from the
+    # algorithm: out = rotl(s0 + s3, 23) + s0 = rotl(5, 23) + 1 = 41943041;
+    # the step gives s = {7, 0, 262146, rotl(6, 45) = 6 * 2^45}, so the second
+    # is rotl(7 + 6 * 2^45, 23) + 7 = 7 * 2^23 + 96 + 7 = 58720359.
+    L = orc.lib()
+    import ctypes
+    st = (ctypes.c_uint64 * 4)(1, 2, 3, 4)
+    outs = [int(L.orc_rng_next(st)) for _ in range(10)]
+    assert outs == [41943041, 58720359, 3588806011781223, 3591011842654386,
+                    9228616714210784205, 9973669472204895162, 14011001112246962877,
+                    12406186145184390807, 15849039046786891736, 10450023813501588000]
+    st = (ctypes.c_uint64 * 4)(1, 2, 3, 4)
+    L.orc_rng_next(st)
+    assert list(st) == [7, 0, 262146, 6 << 45]
+
+
+def test_random_float_known_answers(orc):
+    # Zig's Random.float(f32) (sampler.zig:162): mantissa = the low 23 bits of
+    # one u64 word, exponent = 126 - (leading zeros of the word); a word with
+    # 41 or more leading zeros draws a second word.  From {1, 2, 3, 4} the
+    # first word is 41943041 = 0x2800001: 38 leading zeros, mantissa 1, so
+    # u = 2^(88 - 127) * (1 + 2^-23).
+    L = orc.lib()
+    import ctypes
+    st = (ctypes.c_uint64 * 4)(1, 2, 3, 4)
+    words = ctypes.c_uint32(0)
+    u = L.orc_rng_float(st, ctypes.byref(words))
+    assert np.float32(u) == np.float32(2.0 ** -39 * (1 + 2.0 ** -23))
+    assert words.value == 1
+    # the second word, 58720359 = 0x3800067: 38 leading zeros, mantissa 0x67
+    u = L.orc_rng_float(st, ctypes.byref(words))
+    assert np.float32(u) == np.float32(2.0 ** -39 * (1 + 0x67 / 2.0 ** 23))
+
+
+def test_parity_report_classes(orc):
+    # the report's classes on the checker itself: a batch compared with itself
+    # is all exact; a planted mismatch lands in a class
+    rng = np.random.default_rng(11)
+    x = (3 * rng.standard_normal((8, 2000))).astype(np.float32)
+    c = orc.make_config(temperature=0.8, top_k=0, top_p=0.9, min_p=0.0, typical_p=1.0, seed=3,
+                        repetition_window=0, repetition_penalty=1.0)
+    ref, tr, _ = orc.sample_batch(c, x, seeds=np.arange(8, dtype=np.uint64) + 3)
+    rep = orc.parity_report(ref, ref, tr)
+    assert rep["rows"] == 8 and rep["exact"] == 8
+    assert rep["mismatch_other"] + rep["mismatch_draw_boundary"] + rep["mismatch_threshold_boundary"] == 0
+    bad = ref.copy()
+    bad[0] ^= 1
+    rep = orc.parity_report(bad, ref, tr)
+    assert rep["exact"] == 7
+    assert rep["mismatch_other"] + rep["mismatch_draw_boundary"] + rep["mismatch_threshold_boundary"] == 1
+
+
 def test_random_float_mapping(orc):
     L = orc.lib()
     import ctypes
