@@ -105,22 +105,41 @@ def workload_desc(w):
             f"min_p={w.min_p} typical_p={w.typical_p}")
 
 
-def cpu_baseline(pkg, w, budget_s: float, nthreads: int):
-    """The checker (C restatement of sampler.zig) on the host cores, bounded sample."""
+def cpu_baseline(pkg, w, budget_s: float, nthreads: int, x=None):
+    """The checker (C restatement of sampler.zig, single-threaded per row like
+    the reference) on the host cores: rows spread over all `nthreads` threads,
+    and one core alone, each on a bounded sample of the workload's rows."""
     orc = graft.load_oracle()
-    n = max(nthreads, min(w.rows * 2, int(budget_s / 0.025)))
-    x = pkg.workloads.make_logits(w, rows=min(n, w.rows))
-    reps = (n + x.shape[0] - 1) // x.shape[0]
     cfg = orc.make_config(**w.config())
-    t0 = time.perf_counter()
-    done = 0
-    for r in range(reps):
-        m = min(x.shape[0], n - done)
-        orc.sample_batch(cfg, x[:m], seeds=w.seeds(m), nthreads=nthreads)
-        done += m
-    dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": "rows/s", "cores": nthreads, "kind": "port",
-            "sample": f"{done} rows of {w.name} (V={w.vocab}) on {nthreads} threads, {dt:.1f} s"}
+    if x is None:
+        x = pkg.workloads.make_logits(w, rows=min(w.rows, max(nthreads, 16)))
+
+    def timed(threads, rows_min, budget):
+        done, t0 = 0, time.perf_counter()
+        while done < rows_min or time.perf_counter() - t0 < budget:
+            m = min(x.shape[0], max(threads, 1))
+            orc.sample_batch(cfg, x[:m], seeds=w.seeds(m), nthreads=threads)
+            done += m
+        return done, time.perf_counter() - t0
+
+    n_all, t_all = timed(nthreads, 2 * nthreads, budget_s)
+    n_one, t_one = timed(1, 2, budget_s / 2)
+    return {"value": n_all / t_all, "unit": "rows/s", "cores": nthreads, "kind": "port",
+            "sample": f"{n_all} rows of {w.name} (V={w.vocab}) on {nthreads} threads, {t_all:.1f} s",
+            "value_1core": n_one / t_one,
+            "sample_1core": f"{n_one} rows on 1 thread, {t_one:.1f} s"}
+
+
+def parity_check(pkg, w, smp, dev_x, host_x, states):
+    """One step of the benched batch against the checker: exact token matches
+    and the draw-/threshold-boundary classes (the sampler is meant to match
+    everywhere; boundary cases are only counted)."""
+    orc = graft.load_oracle()
+    smp.rng_state = states
+    got = smp.sample(dev_x).cpu().numpy().astype(np.uint32)
+    ref, traces, _ = orc.sample_batch(orc.make_config(**w.config()), host_x, states=states,
+                                      nthreads=os.cpu_count() or 1)
+    return orc.parity_report(got, ref, traces)
 
 
 def run_reference(args, pkg, w):
@@ -130,7 +149,12 @@ def run_reference(args, pkg, w):
     nthreads = os.cpu_count() or 1
     orc = graft.load_oracle()
     cfg = orc.make_config(**w.config())
-    x = pkg.workloads.make_logits(w, rows=min(w.rows, nthreads))
+    # the benched batch itself, unless the run's --steps/--warmup would then
+    # take longer than a few minutes (about 25 ms per row on one core)
+    per_row_s = 0.025 * max(1.0, w.vocab / 128256) / nthreads
+    fit = int(args.ref_budget / max(1, args.steps + args.warmup) / per_row_s)
+    rows = max(min(w.rows, nthreads), min(w.rows, fit))
+    x = pkg.workloads.make_logits(w, rows=rows)
     seeds = w.seeds(x.shape[0])
     for _ in range(args.warmup):
         orc.sample_batch(cfg, x, seeds=seeds, nthreads=nthreads)
@@ -145,9 +169,11 @@ def run_reference(args, pkg, w):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_desc(w), "rows_per_step": x.shape[0]},
+        "config": {"workload": workload_desc(w), "rows_per_step": x.shape[0],
+                   "same_batch": x.shape[0] == w.rows},
         "cpu_baseline": {"value": v, "unit": "rows/s", "cores": nthreads, "kind": "port",
-                         "sample": f"{x.shape[0]} rows per step (one per host thread), {args.steps} steps"},
+                         "sample": f"{x.shape[0]} of the {w.rows} rows per step on {nthreads} threads "
+                                   f"(one sampler per row), {args.steps} steps"},
         "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -232,7 +258,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--ref-budget", type=float, default=150.0,
+                    help="seconds the reference arm may take in all (sizes its rows per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -264,6 +293,7 @@ def main():
     dev = [torch.from_numpy(h).cuda() for h in host]
     cfg = pkg.SamplerConfig(**w.config())
     smp = pkg.Sampler(cfg, batch=B, vocab=V, device=local, seeds=shard.seeds(w.seed))
+    states0 = smp.rng_state
     out = torch.empty(B, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
 
@@ -289,6 +319,17 @@ def main():
     ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
     if smp.last_status() != 0:
         raise RuntimeError(f"sampler status {smp.last_status()}")
+    # per-step device times (events around every step) for the median and p95
+    nper = min(args.steps, 200)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nper)]
+    for i in range(nper):
+        evs[i][0].record(stream)
+        smp.sample(dev[i % ROTATE], out=out)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    per_us = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
+    step_us = {"median": per_us[len(per_us) // 2], "p95": per_us[min(len(per_us) - 1, int(0.95 * len(per_us)))],
+               "steps": nper}
     launches_per_step = 1 if greedy else (6 if w.typical_p < 1.0 else 4)
     kernel_ms = None
     if not greedy:
@@ -313,6 +354,16 @@ def main():
         smp.sample(pin_np[i % 2])
     e2e_s = pkg.sharding.max_over_ranks(time.perf_counter() - t0, dist, device="cuda")
     e2e_rows = pkg.sharding.aggregate_rows_per_s(shard, args.e2e_steps, e2e_s)
+
+    # parity of one benched step against the checker, summed over the ranks
+    parity = None
+    if not args.no_parity and not greedy:
+        parity = parity_check(pkg, w, smp, dev[0], host[0], states0)
+        if dist:
+            keys = [k for k, v in parity.items() if isinstance(v, int)]
+            t = torch.tensor([parity[k] for k in keys], dtype=torch.int64, device="cuda")
+            dist.all_reduce(t)
+            parity.update({k: int(v) for k, v in zip(keys, t.tolist())})
 
     if rank == 0:
         rows_per_s = pkg.sharding.aggregate_rows_per_s(shard, args.steps, ms / 1e3)
@@ -344,7 +395,10 @@ def main():
             "e2e": {"value": e2e_rows, "unit": "rows/s", "h2d_bytes_per_step": int(alg_bytes),
                     "d2h_bytes_per_step": 4 * B, "api": "bs_sample_host (pinned host logits)"},
             "gpu_launches": launches_per_step * args.steps,
+            "step_us": step_us,
         }
+        if parity is not None:
+            line["parity"] = parity
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(pkg, w, args.cpu_budget, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)

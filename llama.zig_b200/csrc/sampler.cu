@@ -548,6 +548,10 @@ struct K12Params {
     uint32_t cand_stride;
     uint32_t *kerr;           // per handle: the call whose bounded device wait gave up
     uint32_t seq;             // this call's sequence number (never 0)
+    // persistent kernel (k_fused): task scheduler state of this call
+    uint32_t *ctl;            // [0] next statistics task, [1] next main task, [2] ready rows;
+                              // then per call row: statistics tasks done; all zeroed before the call
+    unsigned long long *ready;   // per slot: (seq << 32) | row once the slot publishes that row's main tasks
 };
 
 __device__ __forceinline__ bool penalty_active(const K12Params &P) { return P.pen_bm != nullptr; }
@@ -803,21 +807,33 @@ __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, 
 // maximum, the sum relative to it, a non-finite flag and, for top-p without a
 // top-k floor, the tail-element histogram.  No cross-CTA step: the row
 // reduction is k1_rows.
-__global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
-    grid_dep_launch();
-    const uint32_t seg = blockIdx.x, row = blockIdx.y, hrow = P.row0 + row;
+// Shared memory of one statistics task (segment `seg` of row `row`).
+struct __align__(128) StatsSmem {
+    float4 sbuf[SEG_ELEMS / 4];          // the segment's logits
+    uint32_t mh[KH_BINS];                // tail element counts per bin
+    float th[KH_BINS];                   // typical band: mass per bin
+    float wm[K12_THREADS / 32];
+    uint32_t wf[K12_THREADS / 32];
+    double wd[K12_THREADS / 32], wd2[K12_THREADS / 32];
+};
+
+__device__ __forceinline__ void stats_task(const K12Params &P, uint32_t seg, uint32_t row, StatsSmem &ss_,
+                                           uint64_t *barp) {
+    const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
     const float *x = P.logits + (size_t)row * P.ld;
     const float c2 = P.c2;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
-    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ uint32_t mh[KH_BINS];   // tail element counts per bin
-    __shared__ float wm[NW];
-    __shared__ uint32_t wf[NW];
-    __shared__ double wd[NW];
+    float4 *const sbuf = ss_.sbuf;
+    uint64_t &bar = *barp;
+    uint32_t *const mh = ss_.mh;
+    float *const th = ss_.th;
+    float *const wm = ss_.wm;
+    uint32_t *const wf = ss_.wf;
+    double *const wd = ss_.wd;
+    double *const wd2 = ss_.wd2;
     // the logits stream through L2 once here: marked evict-first, they do not
     // push out what later kernels reuse (their code, the tile statistics)
     const uint64_t pol = l2_policy_evict_first();
@@ -828,7 +844,6 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
     const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
     const bool t_band = P.tmode == TYP_BAND;
-    __shared__ float th[KH_BINS];      // typical band: mass per bin
     if (p_floor)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) mh[b] = 0u;
     if (t_band)
@@ -918,7 +933,6 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
     }
     ss = warp_sum_d(ss);
     ss2 = warp_sum_d(ss2);
-    __shared__ double wd2[NW];
     if (lane == 0) {
         wd[warp] = ss;
         wd2[warp] = ss2;
@@ -945,6 +959,13 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = th[b];
 }
 
+__global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
+    __shared__ StatsSmem sm;
+    __shared__ __align__(8) uint64_t bar;
+    grid_dep_launch();
+    stats_task(P, blockIdx.x, blockIdx.y, sm, &bar);
+}
+
 // Row reduction, one CTA per row: the row maximum M, the raw prefix estimate
 // at every segment start, and the candidate floor (log2 p relative to M):
 //   top-k: from the tile maxima, binned by quarter octaves below M: the
@@ -952,10 +973,36 @@ __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
 //   top-p without top-k: from the segments' tail-element histograms (a
 //     bound on the mass below each grid point);
 //   min-p: ln(min_p) in log2 units, minus a margin.
-__global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
-    grid_dep_wait();     // the statistics pass's results
-    grid_dep_launch();   // after the wait: the main pass may read the statistics before its own wait
-    const uint32_t row = blockIdx.x, hrow = P.row0 + row;
+// Shared memory of one row reduction.
+struct __align__(16) RowsSmem {
+    float off[MAX_SEG];   // (segment max - M) log2e / T
+    float ssc[MAX_SEG];   // segment tail mass scale 2^off
+    RowInfo ri;
+    uint32_t kh[KH_BINS];
+    int kj_w[K12_THREADS / 32], pj_w[K12_THREADS / 32];
+    float dh[TB_CELLS];
+    float cumm[RED_CHUNK * KH_BINS];
+    float mtot[RED_CHUNK];
+};
+
+// Loads of data another CTA of the same grid wrote (the persistent kernel's
+// tasks): through L2, never from a possibly stale L1 line.
+__device__ __forceinline__ SegStat ld_segstat(const SegStat *p) {
+    SegStat st;
+    st.smax = __ldcg(&p->smax);
+    st.nonfin = __ldcg(&p->nonfin);
+    st.ssum = __ldcg(&p->ssum);
+    st.base = __ldcg(&p->base);
+    st.ssum2 = __ldcg(&p->ssum2);
+    return st;
+}
+__device__ __forceinline__ TileStat ld_tilestat(const TileStat *p) {
+    const float4 v = __ldcg(reinterpret_cast<const float4 *>(p));
+    return TileStat{v.x, v.y, v.z, v.w};
+}
+
+__device__ __forceinline__ void rows_task(const K12Params &P, uint32_t row, RowsSmem &rs_) {
+    const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
     const float c2 = P.c2;
@@ -964,11 +1011,12 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     const double p_margin = fmax(2e-3, 0.05 * (1.0 - (double)P.top_p));
     const bool p_floor = p_active && (1.0 - (double)P.top_p) > 2.0 * p_margin && !k_floor;
 
-    __shared__ float off[MAX_SEG];   // (segment max - M) log2e / T
-    __shared__ float ssc[MAX_SEG];   // segment tail mass scale 2^off
-    __shared__ RowInfo ri;
-    __shared__ uint32_t kh[KH_BINS];
-    __shared__ int kj_w[NW], pj_w[NW];
+    float *const off = rs_.off;
+    float *const ssc = rs_.ssc;
+    RowInfo &ri = rs_.ri;
+    uint32_t *const kh = rs_.kh;
+    int *const kj_w = rs_.kj_w;
+    int *const pj_w = rs_.pj_w;
     const SegStat *S = P.sstat + (size_t)hrow * MAX_SEG;
     const uint32_t ns = P.nseg;
     for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) kh[b] = 0u;
@@ -981,14 +1029,14 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
 #pragma unroll
         for (int k = 0; k < KT; k++) {
             const uint32_t t = (uint32_t)k * K12_THREADS + tid;
-            tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+            tmv[k] = t < P.ntiles_total ? __ldcg(&ts[t].tmax) : NEG_INF;
         }
     }
     if (warp == 0) {
         float m = NEG_INF;
         uint32_t nf = 0;
         for (uint32_t c = lane; c < ns; c += 32) {
-            const SegStat st = S[c];
+            const SegStat st = ld_segstat(S + c);
             m = fmaxf(m, st.smax);
             nf |= st.nonfin;
         }
@@ -1001,7 +1049,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
             double sv = 0.0;
             float o = NEG_INF;
             if (c < ns) {
-                const SegStat st = S[c];
+                const SegStat st = ld_segstat(S + c);
                 o = (st.smax > NEG_INF) ? (st.smax - m) * c2 : NEG_INF;
                 sv = st.smax > NEG_INF ? st.ssum * (double)ex2_approx(o) : 0.0;
                 off[c] = o;
@@ -1021,7 +1069,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
         double e2 = 0.0;
         if (P.tmode == TYP_BAND) {
             for (uint32_t c = lane; c < ns; c += 32) {
-                const SegStat st = S[c];
+                const SegStat st = ld_segstat(S + c);
                 if (st.smax > NEG_INF) {
                     const double o = (double)((st.smax - m) * c2);
                     e2 += (double)ex2_approx((float)o) * (st.ssum2 + o * st.ssum);
@@ -1045,7 +1093,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     // (segment c, quarter-octave b) lies wholly inside the band once
     // d >= max(H_hi - s_lo, s_hi - H_lo); those d are histogrammed by mass.
     if (P.tmode == TYP_BAND && ri.S_raw > 0.0) {
-        __shared__ float dh[TB_CELLS];
+        float *const dh = rs_.dh;
         for (uint32_t j = tid; j < TB_CELLS; j += K12_THREADS) dh[j] = 0.0f;
         __syncthreads();
         const double lnS = log(ri.S_raw), H = ri.H_raw;
@@ -1054,7 +1102,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
         for (uint32_t i = tid; i < ns * KH_BINS; i += K12_THREADS) {
             const uint32_t c = i / KH_BINS, b = i - c * KH_BINS;
             const float o = off[c];
-            const float mass = TH[i];
+            const float mass = __ldcg(TH + i);
             if (!(o > NEG_INF) || !(mass > 0.0f)) continue;
             const double xs_hi = (double)o - 0.25 * (double)b, xs_lo = (double)o - 0.25 * (double)(b + 1);
             const double s_lo = lnS - xs_hi * 0.6931471805599453, s_hi = lnS - xs_lo * 0.6931471805599453;
@@ -1096,7 +1144,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
 #pragma unroll
                 for (int k = 0; k < KT; k++) {
                     const uint32_t t = t0 + (uint32_t)k * K12_THREADS + tid;
-                    tmv[k] = t < P.ntiles_total ? ts[t].tmax : NEG_INF;
+                    tmv[k] = t < P.ntiles_total ? __ldcg(&ts[t].tmax) : NEG_INF;
                 }
             }
 #pragma unroll
@@ -1122,8 +1170,8 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     // processed in chunks of RED_CHUNK: one warp per segment turns its
     // histogram into a cumulative one in shared memory, then thread j
     // accumulates grid point j.
-    __shared__ float cumm[RED_CHUNK * KH_BINS];
-    __shared__ float mtot[RED_CHUNK];
+    float *const cumm = rs_.cumm;
+    float *const mtot = rs_.mtot;
     const float *MH = P.mhist + (size_t)hrow * MAX_SEG * KH_BINS;
     float mbelow = 0.0f;   // mass possibly below f_j (over-count), units of p(M)
     if (p_floor) {
@@ -1136,7 +1184,7 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
                 float ms = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    ms += MH[(size_t)c * KH_BINS + lane * 8 + j];
+                    ms += __ldcg(MH + (size_t)c * KH_BINS + lane * 8 + j);
                     mc[j] = ms;
                 }
                 float mi = ms;
@@ -1213,6 +1261,13 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
     }
 }
 
+__global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
+    __shared__ RowsSmem rs;
+    grid_dep_wait();     // the statistics pass's results
+    grid_dep_launch();   // after the wait: the main pass may read the statistics before its own wait
+    rows_task(P, blockIdx.x, rs);
+}
+
 // ---------------------------------------------------------------------------
 // K2: classification, certified grid counts, candidates, walk items.
 // TERM_P: the terms p_i of the normaliser S (sampler.zig:83-88).
@@ -1220,12 +1275,42 @@ __global__ void __launch_bounds__(K12_THREADS) k1_rows(K12Params P) {
 // known; only for typical-p rows whose token is not yet final.
 enum : int { TERM_P = 0, TERM_H = 1 };
 
+// Shared memory of one main-pass task (segment `seg` of row `row`).
+constexpr uint32_t RC_CAP = 512;   // uncertified terms recounted one per thread (entropy pass)
+struct __align__(128) MainSmem {
+    float4 sbuf[SEG_ELEMS / 4];         // the segment's logits; later the item phase's arrays
+    TileRec rec[SEG_TILES];
+    double wtmp_d[K12_THREADS / 32 + 1];
+    double hbase;
+    SegComp wtmp_s[2 * (K12_THREADS / 32) + 2];
+    uint32_t wtmp_u[K12_THREADS / 32 + 1];
+    uint32_t wlist[SEG_TILES];
+    uint16_t rcl[RC_CAP];               // (tile << 5) | element
+    uint32_t nrc, rc_fb[SEG_TILES / 32];
+    uint32_t nlist, nanflag;
+    int32_t lo0;
+    uint32_t wsum_u[K12_THREADS / 32];
+    uint64_t ch_a[K12_THREADS / 32], ch_b[K12_THREADS / 32];
+    uint32_t ch_heads[K12_THREADS / 32], ch_start[K12_THREADS / 32];
+};
+
+__device__ __forceinline__ RowInfo ld_rowinfo(const RowInfo *p) {
+    RowInfo r;
+    r.M = __ldcg(&p->M);
+    r.xf2 = __ldcg(&p->xf2);
+    r.binding = __ldcg(&p->binding);
+    r.check_nan = __ldcg(&p->check_nan);
+    r.S_raw = __ldcg(&p->S_raw);
+    r.H_raw = __ldcg(&p->H_raw);
+    r.dband = __ldcg(&p->dband);
+    r.tmode = __ldcg(&p->tmode);
+    return r;
+}
+
 template <int TERM>
-__global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
-    // segment-major order over a 1-D grid: every row's segment 0 first (the
-    // row start holds most exact-pass tiles, so those CTAs live several times
-    // longer), the last segments last, so the kernel's tail is short CTAs
-    const uint32_t seg = blockIdx.x / P.rows, row = blockIdx.x - seg * P.rows, hrow = P.row0 + row;
+__device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint32_t row, MainSmem &ms_,
+                                          uint64_t *barp) {
+    const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
@@ -1235,26 +1320,26 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     const float c2 = P.c2, T = P.T;
     RowHdr *hdr = P.hdr + hrow;
 
-    __shared__ double wtmp_d[NW + 1];
-    __shared__ double hbase;
-    __shared__ uint32_t wtmp_u[NW + 1];
-    __shared__ SegComp wtmp_s[2 * NW + 2];
-    __shared__ TileRec rec[SEG_TILES];
-    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
-    __shared__ __align__(8) uint64_t bar;
+    double *const wtmp_d = ms_.wtmp_d;
+    double &hbase = ms_.hbase;
+    uint32_t *const wtmp_u = ms_.wtmp_u;
+    SegComp *const wtmp_s = ms_.wtmp_s;
+    TileRec *const rec = ms_.rec;
+    float4 *const sbuf = ms_.sbuf;
+    uint64_t &bar = *barp;
     // the item phase's arrays reuse the segment copy, which is dead by then
     // (6 KB less shared memory per CTA: five CTAs fit an SM instead of four)
     uint32_t *const uarr = reinterpret_cast<uint32_t *>(sbuf);
     uint32_t *const uarr2 = uarr + SEG_TILES;
     Comp *const carr = reinterpret_cast<Comp *>(uarr2 + SEG_TILES);   // 8-byte aligned: read as uint64_t too
     Comp *const carr2 = carr + SEG_TILES;
-    __shared__ uint32_t wlist[SEG_TILES];
+    uint32_t *const wlist = ms_.wlist;
     // uncertified terms of SIMPLE tiles, recounted exactly one per thread:
     // (tile << 5) | element, and the tiles that still need the warp pass
-    constexpr uint32_t RC_CAP = 512;
-    __shared__ uint16_t rcl[RC_CAP];
-    __shared__ uint32_t nrc, rc_fb[SEG_TILES / 32];
-    __shared__ uint32_t nlist, nanflag;
+    uint16_t *const rcl = ms_.rcl;
+    uint32_t &nrc = ms_.nrc;
+    uint32_t *const rc_fb = ms_.rc_fb;
+    uint32_t &nlist = ms_.nlist, &nanflag = ms_.nanflag;
     // the segment's bulk copy overlaps the prologue (and, for the normaliser,
     // the wait for the row reduction: it needs only the logits); it is read
     // once more only by the exact pass, so it need not stay in L2
@@ -1267,14 +1352,14 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // grid could start (the row reduction lets it launch only after its own
     // wait): load them before waiting for the row reduction
     TileStat ts_pre = TileStat{NEG_INF, 0.0f, 0.0f, 0.0f};
-    if (live) ts_pre = P.tstat[(size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid];
+    if (live) ts_pre = ld_tilestat(P.tstat + (size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid);
     grid_dep_wait();   // the row reduction (and, for the entropy, the normaliser's walk)
-    const RowInfo ri = P.rinfo[hrow];
+    const RowInfo ri = ld_rowinfo(P.rinfo + hrow);
     const float M = ri.M;
-    if (TERM == TERM_H && hdr->tdone) return;   // the row's token is already final
+    if (TERM == TERM_H && __ldcg(&hdr->tdone)) return;   // the row's token is already final
     if (TERM == TERM_H) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
     // the entropy pass: S exact, log2 S for the terms' exponents
-    const float S = TERM == TERM_H ? hdr->S_exact : 1.0f;
+    const float S = TERM == TERM_H ? __ldcg(&hdr->S_exact) : 1.0f;
     const double lnS = TERM == TERM_H ? log((double)S) : 0.0;
     const float l2S = (float)(lnS * 1.4426950408889634);
     if (tid == 0) {
@@ -1310,13 +1395,13 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
         }
         double base;
         if (TERM == TERM_P) {
-            base = P.sstat[(size_t)hrow * MAX_SEG + seg].base;
+            base = __ldcg(&P.sstat[(size_t)hrow * MAX_SEG + seg].base);
         } else {
             // entropy mass of the earlier segments, from their statistics
             if (warp == 0) {
                 double hb = 0.0;
                 for (uint32_t c = lane; c < seg; c += 32) {
-                    const SegStat st = P.sstat[(size_t)hrow * MAX_SEG + c];
+                    const SegStat st = ld_segstat(P.sstat + (size_t)hrow * MAX_SEG + c);
                     if (st.smax > NEG_INF) {
                         const double o = (double)((st.smax - M) * c2);
                         hb += fmax(0.0, (double)ex2_approx((float)o) *
@@ -1607,8 +1692,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     // the common segment (past the row start): every tile SIMPLE in one
     // binade with parity-free counts -- a single item, from a block sum
     {
-        __shared__ int32_t lo0;
-        __shared__ uint32_t wsum_u[NW];
+        int32_t &lo0 = ms_.lo0;
+        uint32_t *const wsum_u = ms_.wsum_u;
         if (tid == 0) lo0 = rec[0].lo;
         __syncthreads();
         const TileRec rt = live ? rec[tid] : rec[0];
@@ -1647,8 +1732,8 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     if (!ties) {
         // each warp builds the items of its chunk of 32 tiles; a stretch that
         // runs into a chunk from before is carried from the chunk summaries
-        __shared__ uint64_t ch_a[NW], ch_b[NW];   // counts from the chunk's last head (or start) to its end
-        __shared__ uint32_t ch_heads[NW], ch_start[NW];
+        uint64_t *const ch_a = ms_.ch_a, *const ch_b = ms_.ch_b;   // counts from the chunk's last head (or start) to its end
+        uint32_t *const ch_heads = ms_.ch_heads, *const ch_start = ms_.ch_start;
         uint32_t *sid = uarr;                                   // item of each WINDOW tile
         uint64_t *sb = reinterpret_cast<uint64_t *>(carr);      // hi prefix of each WINDOW tile
         uint64_t *itb = reinterpret_cast<uint64_t *>(carr2);    // hi total of each item
@@ -1834,6 +1919,139 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
     if (tid == 0) {
         hdr->seg_items[seg] = nitems;
         hdr->seg_tile0[seg] = tile0;
+    }
+}
+
+template <int TERM>
+__global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
+    __shared__ MainSmem ms;
+    __shared__ __align__(8) uint64_t bar;
+    // segment-major order over a 1-D grid: every row's segment 0 first (the
+    // row start holds most exact-pass tiles, so those CTAs live several times
+    // longer), the last segments last, so the kernel's tail is short CTAs
+    const uint32_t seg = blockIdx.x / P.rows, row = blockIdx.x - seg * P.rows;
+    main_task<TERM>(P, seg, row, ms, &bar);
+}
+
+// ---------------------------------------------------------------------------
+// Persistent form of the statistics pass, the row reduction and the
+// normaliser's main pass: one launch whose resident CTAs take tasks from
+// counters in device memory.
+//   statistics task (row, segment), in row-major order;
+//   the CTA that finishes a row's last statistics task runs the row
+//     reduction and then publishes the row's main tasks (a slot of the ready
+//     list, released after everything the tasks read);
+//   main task (slot, segment): taken first whenever one is published, so a
+//     row's logits are read again soon after the statistics streamed them
+//     (from L2), and the HBM-bound statistics of later rows overlap the
+//     issue-bound main tasks of earlier ones.
+// A CTA waits only for tasks that running CTAs hold, never for one that no
+// CTA has taken; every wait is bounded (a timeout marks the call failed).
+// Loads of data another task wrote go through L2 (__ldcg): L1 is not
+// coherent across SMs.
+enum : uint32_t { TK_STATS = 0, TK_MAIN = 1, TK_EXIT = 2 };
+constexpr uint64_t FUSED_WAIT_NS = 1000000000ull;   // one second without a task
+
+union __align__(128) FusedSmem {
+    StatsSmem s;
+    RowsSmem r;
+    MainSmem m;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+constexpr int FUSED_CTAS_PER_SM = 4;
+__global__ void __launch_bounds__(K12_THREADS, FUSED_CTAS_PER_SM) k_fused(K12Params P) {
+    __shared__ FusedSmem u;
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t t_kind, t_row, t_seg, t_last;
+    const uint32_t nseg = P.nseg, total = P.rows * P.nseg;
+    uint32_t *const s_next = P.ctl, *const m_next = P.ctl + 1, *const n_ready = P.ctl + 2;
+    uint32_t *const row_done = P.ctl + 4;
+    // thread 0's scheduling state: the statistics tasks are all taken; the
+    // main-task ticket it holds (a fetch-add on the main counter, taken only
+    // when a reduced row is likely waiting, so claims never contend; a ticket
+    // whose row is not published yet is kept while the CTA takes statistics
+    // tasks)
+    constexpr uint32_t NONE = 0xFFFFFFFFu;
+    bool s_done = false;
+    uint32_t ticket = NONE;
+    for (;;) {
+        if (threadIdx.x == 0) {
+            uint32_t kind = TK_EXIT, row = 0, seg = 0;
+            const uint64_t t0 = global_ns();
+            for (uint32_t it = 0;; it++) {
+                if (ticket == NONE && __ldcg(m_next) < min(__ldcg(n_ready) * nseg, total)) {
+                    const uint32_t t = atomicAdd(m_next, 1u);
+                    if (t < total) ticket = t;
+                }
+                if (ticket != NONE) {
+                    const uint32_t slot = ticket / nseg;
+                    const unsigned long long rv = ld_acquire_u64(P.ready + slot);
+                    if ((uint32_t)(rv >> 32) == P.seq) {
+                        kind = TK_MAIN;
+                        row = (uint32_t)rv;
+                        seg = ticket - slot * nseg;
+                        ticket = NONE;
+                        break;
+                    }
+                }
+                if (!s_done) {
+                    const uint32_t t = atomicAdd(s_next, 1u);
+                    if (t < total) {
+                        kind = TK_STATS;
+                        row = t / nseg;
+                        seg = t - row * nseg;
+                        break;
+                    }
+                    s_done = true;
+                }
+                if (ticket == NONE && __ldcg(m_next) >= total) break;   // every task is taken
+                // a main task remains whose row is not published yet: the
+                // statistics it needs are in running CTAs' hands
+                if (global_ns() - t0 > FUSED_WAIT_NS || it > (1u << 24)) {
+                    atomicExch(P.kerr, P.seq);
+                    break;
+                }
+                __nanosleep(128);
+            }
+            t_kind = kind;
+            t_row = row;
+            t_seg = seg;
+        }
+        __syncthreads();
+        const uint32_t kind = t_kind, row = t_row, seg = t_seg;
+        if (kind == TK_EXIT) break;
+        if (kind == TK_STATS) {
+            stats_task(P, seg, row, u.s, &bar);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();   // the task's statistics before its count
+                t_last = atomicAdd(row_done + row, 1u) + 1u == nseg ? 1u : 0u;
+            }
+            __syncthreads();
+            if (t_last) {
+                __threadfence();   // every statistics task of the row before its reduction
+                rows_task(P, row, u.r);
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    __threadfence();
+                    const uint32_t slot = atomicAdd(n_ready, 1u);
+                    st_release_u64(P.ready + slot, ((unsigned long long)P.seq << 32) | row);
+                }
+            }
+        } else {
+            __threadfence();   // after thread 0's acquire of the slot: the row's reduction
+            main_task<TERM_P>(P, seg, row, u.m, &bar);
+        }
+        __syncthreads();   // the task's shared memory is free again
     }
 }
 
@@ -2772,6 +2990,8 @@ struct bs_sampler {
     TileStat *d_tstat;
     SegStat *d_sstat;
     uint32_t *d_penbm;       // repetition-penalty bitmaps, ntiles_total words per row
+    uint32_t *d_fctl;        // persistent kernel: 4 control words + batch row counters (zeroed per call)
+    unsigned long long *d_ready;   // persistent kernel: ready list, batch slots
     float *d_mhist;
     RowInfo *d_rinfo;
     Item *d_items;
@@ -2783,6 +3003,7 @@ struct bs_sampler {
     RowTrace *d_trace;
     uint32_t *d_kerr;        // sequence number of the last call whose bounded device wait gave up
     uint32_t seq;            // sequence number of the last call (0 before the first)
+    uint32_t fused;          // 1: the persistent kernel instead of separate statistics / row / main kernels
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -2839,6 +3060,8 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_tstat);
     cudaFree(s->d_sstat);
     cudaFree(s->d_penbm);
+    cudaFree(s->d_fctl);
+    cudaFree(s->d_ready);
     cudaFree(s->d_mhist);
     cudaFree(s->d_rinfo);
     cudaFree(s->d_items);
@@ -2875,6 +3098,23 @@ static cudaError_t ensure_kernel_attrs(int dev) {
     return e;
 }
 
+// Resident CTAs of the persistent kernel on a device (all of them run at once).
+static int g_fused_ctas[MAX_DEVICES];
+static cudaError_t fused_grid(int dev, int *ctas) {
+    if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_attrs_mu);
+    if (g_fused_ctas[dev] == 0) {
+        int per_sm = 0, sms = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused, K12_THREADS, 0);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        if (per_sm <= 0 || sms <= 0) return cudaErrorInvalidConfiguration;
+        g_fused_ctas[dev] = per_sm * sms;
+    }
+    *ctas = g_fused_ctas[dev];
+    return cudaSuccess;
+}
+
 // The next sequence number of a call (never 0, the value of a clear error word).
 static uint32_t next_seq(uint32_t &seq) {
     seq = seq + 1u == 0u ? 1u : seq + 1u;
@@ -2905,6 +3145,9 @@ extern "C" bs_status bs_create(const bs_config *cfg, uint32_t batch, uint32_t vo
     if (e == cudaSuccess) e = cudaMalloc(&s->d_tstat, (size_t)batch * s->ntiles_total * sizeof(TileStat));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_sstat, (size_t)batch * MAX_SEG * sizeof(SegStat));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_penbm, (size_t)batch * s->ntiles_total * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_fctl, (4 + (size_t)batch) * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->d_ready, (size_t)batch * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(s->d_ready, 0, (size_t)batch * sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_mhist, (size_t)batch * MAX_SEG * KH_BINS * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_rinfo, (size_t)batch * sizeof(RowInfo));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_items, (size_t)batch * s->ntiles_total * sizeof(Item));
@@ -3022,6 +3265,8 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     A.cand_stride = s->cand_stride;
     A.kerr = s->d_kerr;
     A.seq = seq;
+    A.ctl = s->d_fctl;
+    A.ready = s->d_ready;
     A.typical_p = c.typical_p;
     A.tmode = typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p);
 
@@ -3058,6 +3303,32 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     // the entropy terms (profiled with the main pass | the final walk).
     cudaEvent_t *ev = nullptr;
     if (s->prof_ev && s->prof_n < s->prof_cap) ev = s->prof_ev + 4 * s->prof_n++;
+    // the persistent kernel for the statistics, row reduction and main pass
+    // (one launch; the walk follows as an ordinary launch).  Profiling runs
+    // the separate kernels, whose groups the events can split
+    if (!ev && s->fused && s->d_fctl) {
+        int ctas = 0;
+        cudaError_t e = fused_grid(s->device, &ctas);
+        const uint32_t tasks = rows * s->nseg;
+        if (e == cudaSuccess) e = cudaMemsetAsync(s->d_fctl, 0, (4 + (size_t)rows) * sizeof(uint32_t), st);
+        if (e == cudaSuccess && pen)
+            k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, row0, s->ntiles_total, s->d_penbm);
+        if (e == cudaSuccess) k_fused<<<(uint32_t)ctas < tasks ? (uint32_t)ctas : tasks, K12_THREADS, 0, st>>>(A);
+        const dim3 g2(s->nseg * rows);
+        if (A.tmode != TYP_OFF) {
+            if (e == cudaSuccess) {
+                kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
+                e = launch_dependent(k2_main<TERM_H>, g2, dim3(K12_THREADS), 0, st, A);
+            }
+            if (e == cudaSuccess)
+                e = launch_dependent(kernel_b<TERM_H>, dim3(rows), dim3(KB_THREADS), s->smem_b, st, B);
+        } else if (e == cudaSuccess) {
+            kernel_b<TERM_P><<<rows, KB_THREADS, s->smem_b, st>>>(B);
+        }
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
+        return cuda_status(e);
+    }
     // (with profiling on, the event records between the groups keep them
     // from overlapping; the unprofiled step overlaps every boundary after the
     // statistics pass)
@@ -3126,6 +3397,18 @@ extern "C" bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t
     for (uint32_t i = 0; i < rows; i++)
         if (h_out[i] == 0xFFFFFFFFu) return bs_last_device_status(s);
     return BS_OK;
+}
+
+// Test and tuning hooks: 1 selects the persistent kernel instead of the
+// separate kernels (same results); the persistent kernel's grid on a device.
+extern "C" bs_status bs_debug_set_fused(bs_sampler *s, uint32_t fused) {
+    if (!s) return BS_EINVAL;
+    s->fused = fused;
+    return BS_OK;
+}
+extern "C" int bs_debug_fused_ctas(int device) {
+    int ctas = 0;
+    return fused_grid(device, &ctas) == cudaSuccess ? ctas : -1;
 }
 
 extern "C" bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state) {
@@ -3338,7 +3621,7 @@ extern "C" bs_status bs_profile_read(bs_sampler *s, float *ms, uint32_t cap, uin
 // from one fixed static device array instead of a handle's allocations.  The
 // caller owns the RNG state (a device buffer of rows x 4 u64).
 constexpr size_t r256(size_t b) { return (b + 255) & ~(size_t)255; }
-constexpr int STATIC_NBUF = 13;   // the buffers of a handle, in the order below
+constexpr int STATIC_NBUF = 15;   // the buffers of a handle, in the order below
 struct StaticSizes {
     size_t b[STATIC_NBUF];
 };
@@ -3349,7 +3632,8 @@ constexpr StaticSizes static_sizes(uint32_t rows, uint32_t vocab) {
                         r256(rows * MAX_SEG * KH_BINS * sizeof(float)), r256(rows * sizeof(RowInfo)), r256(rows * nt * sizeof(Item)), r256(rows * nt * sizeof(WTile)),
                         r256(rows * WC_CAP * TILE * sizeof(float)), r256(rows * cs * sizeof(Candidate)),
                         r256(rows * 2 * cs * sizeof(unsigned long long)), r256(rows * sizeof(RowTrace)),
-                        r256(sizeof(uint32_t))}};
+                        r256(sizeof(uint32_t)), r256((4 + rows) * sizeof(uint32_t)),
+                        r256(rows * sizeof(unsigned long long))}};
 }
 constexpr size_t static_total(uint32_t rows, uint32_t vocab) {
     const StaticSizes s = static_sizes(rows, vocab);
@@ -3439,6 +3723,8 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
     s.d_ctmp = static_cast<unsigned long long *>(ptr[10]);
     s.d_trace = static_cast<RowTrace *>(ptr[11]);
     s.d_kerr = static_cast<uint32_t *>(ptr[12]);
+    s.d_fctl = static_cast<uint32_t *>(ptr[13]);        // zeroed by each call before use
+    s.d_ready = static_cast<unsigned long long *>(ptr[14]);   // earlier calls' sequence numbers only
     // nothing in the scratch has to start at zero: every buffer a call reads
     // is written earlier in the same call, and the error word holds the
     // sequence number of a failed call (zero at load), never this call's

@@ -364,3 +364,26 @@ def test_config0_thousand_sequential_steps(gpu_pkg, orc):
         assert got == int(exp[0]), f"step {step}: gpu {got} ref {int(exp[0])}"
     assert np.array_equal(s.rng_state, states)
     s.close()
+
+
+@pytest.mark.parametrize("name,rows", [("c1", 64), ("headline_topp", 256), ("c2", 64), ("c3_topk1", 64)])
+def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows):
+    # the persistent-kernel form of the statistics, row reduction and main
+    # pass (one launch, tasks claimed from device counters) against the checker
+    import ctypes
+    L = gpu_pkg.sampler.lib()
+    L.bs_debug_set_fused.argtypes = [ctypes.c_void_p, ctypes.c_uint32]
+    w, x = _workload(gpu_pkg, name, rows, steps=2)
+    c = w.config()
+    seeds = w.seeds(rows)
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=rows, vocab=w.vocab, seeds=seeds)
+    assert L.bs_debug_set_fused(s._h, 1) == 0
+    toks, states = [], []
+    for i in range(2):
+        toks.append(s.sample(torch.from_numpy(x[i]).cuda()).cpu().numpy().astype(np.uint32))
+        states.append(s.rng_state)
+        assert s.last_status() == 0
+    s.close()
+    ref = run_oracle(orc, c, x, seeds)
+    assert np.array_equal(np.array(toks), ref[0]), name
+    assert np.array_equal(np.array(states), ref[1]), name
