@@ -14,6 +14,11 @@
  *                           and main.zig:667 call it today
  *   bs_argmax            <- sampleArgmax             src/sampler.zig:31-41
  *                           and Dispatcher.executeTopK src/compute_graph.zig:948-985
+ *   bs_argmax_ex         <- executeTopK's logit_scale_bits (src/shaders/topk_bda.glsl:38-40)
+ *                           and the host soft-cap before sampleArgmax (src/engine.zig:341-354)
+ *   bs_set_logit_prologue <- the engine's logit prologue before Sampler.sample
+ *                           (src/engine.zig:341-354, src/main.zig:653-666), from
+ *                           ModelConfig.final_logit_softcapping / logit_scale (src/model.zig:34-35)
  *   bs_get/set_rng_state <- the DefaultPrng field    src/sampler.zig:17
  *   bs_destroy           <- (Zig: the Sampler goes out of scope)
  *   bs_status            <- error.OutOfMemory        src/sampler.zig:26 (!TokenID)
@@ -103,6 +108,22 @@ bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t ld, uint32
  * lowest index on ties, a NaN never wins unless it is element 0). */
 bs_status bs_argmax(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
                     uint32_t *d_out, void *stream);
+
+/* sampleArgmax after the engine's logit prologue: with a soft-cap s > 0 each
+ * logit is taken as tanh(v / s) * s (Zig's f32 std.math.tanh), then, unless
+ * logit_scale is 1 or 0, multiplied by the f32 reciprocal of logit_scale.
+ * softcap <= 0 and logit_scale 1 give bs_argmax.  The logits are not changed
+ * in memory. */
+bs_status bs_argmax_ex(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
+                       float final_logit_softcapping, float logit_scale, uint32_t *d_out, void *stream);
+
+/* The engine's logit prologue, fused into every later bs_sample on this
+ * handle (the engine.zig loop applies it to the host logits before
+ * Sampler.sample): soft-cap tanh(v / s) * s when final_logit_softcapping > 0,
+ * then v * (1 / logit_scale) unless logit_scale is 1 or 0.  It comes before
+ * the repetition penalty, and the T <= 0 argmax sees it too.  The logits are
+ * read, not rewritten.  (0, 1) turns it off. */
+bs_status bs_set_logit_prologue(bs_sampler *s, float final_logit_softcapping, float logit_scale);
 
 /* Per-row xoshiro256++ state, batch x 4 u64 (host memory).  Synchronous. */
 bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state);

@@ -180,6 +180,110 @@ __device__ __forceinline__ float log_ref(float x) {
     return __fadd_rn(r, __fmul_rn(dk, LN2HI));
 }
 
+// exp(x) - 1 in f32 as Zig's std.math.expm1 computes it (a port of the
+// musl / FreeBSD msun expm1f): x = k ln2 + r with ln2 in two parts, the
+// scheme's published two-coefficient correction (Q1, Q2) and its case split on
+// k for the reconstruction.  Every operation is one IEEE f32 operation.
+__device__ __forceinline__ float expm1_ref(float x) {
+    const float o_threshold = 8.8721679688e+01f;   // 0x42b17180
+    const float ln2_hi = 6.9313812256e-01f;        // 0x3f317180
+    const float ln2_lo = 9.0580006145e-06f;        // 0x3717f7d1
+    const float invln2 = 1.4426950216e+00f;        // 0x3fb8aa3b
+    const float Q1 = -3.3333212137e-2f;            // -0x888868.0p-28
+    const float Q2 = 1.5807170421e-3f;             // 0xcf3010.0p-33
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t hx = ux & 0x7fffffffu;
+    const bool sign = (ux >> 31) != 0;
+    float hi, lo, c = 0.0f, t;
+    int k;
+    if (hx >= 0x4195b844u) {                       // |x| >= 27 ln2
+        if (hx > 0x7f800000u) return x;            // NaN
+        if (sign) return -1.0f;
+        if (x > o_threshold) return __fmul_rn(x, 0x1p127f);
+    }
+    if (hx > 0x3eb17218u) {                        // |x| > ln2/2
+        if (hx < 0x3f851592u) {                    // and |x| < 3ln2/2
+            if (!sign) {
+                hi = __fsub_rn(x, ln2_hi);
+                lo = ln2_lo;
+                k = 1;
+            } else {
+                hi = __fadd_rn(x, ln2_hi);
+                lo = -ln2_lo;
+                k = -1;
+            }
+        } else {
+            k = __float2int_rz(__fadd_rn(__fmul_rn(invln2, x), sign ? -0.5f : 0.5f));
+            t = __int2float_rn(k);
+            hi = __fsub_rn(x, __fmul_rn(t, ln2_hi));
+            lo = __fmul_rn(t, ln2_lo);
+        }
+        x = __fsub_rn(hi, lo);
+        c = __fsub_rn(__fsub_rn(hi, x), lo);
+    } else if (hx < 0x33000000u) {                 // |x| < 2^-25
+        return x;
+    } else {
+        k = 0;
+    }
+    const float hfx = __fmul_rn(0.5f, x);
+    const float hxs = __fmul_rn(x, hfx);
+    const float r1 = __fadd_rn(1.0f, __fmul_rn(hxs, __fadd_rn(Q1, __fmul_rn(hxs, Q2))));
+    t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+    float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(x, t))));
+    if (k == 0) return __fsub_rn(x, __fsub_rn(__fmul_rn(x, e), hxs));
+    e = __fsub_rn(__fmul_rn(x, __fsub_rn(e, c)), c);
+    e = __fsub_rn(e, hxs);
+    if (k == -1) return __fsub_rn(__fmul_rn(0.5f, __fsub_rn(x, e)), 0.5f);
+    if (k == 1) {
+        if (x < -0.25f) return __fmul_rn(-2.0f, __fsub_rn(e, __fadd_rn(x, 0.5f)));
+        return __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(x, e)));
+    }
+    const float twopk = __uint_as_float((uint32_t)(0x7f + k) << 23);
+    if (k < 0 || k > 56) {
+        float y = __fadd_rn(__fsub_rn(x, e), 1.0f);
+        y = (k == 128) ? __fmul_rn(__fmul_rn(y, 2.0f), 0x1p127f) : __fmul_rn(y, twopk);
+        return __fsub_rn(y, 1.0f);
+    }
+    const float uf = __uint_as_float((uint32_t)(0x7f - k) << 23);
+    if (k < 23) return __fmul_rn(__fadd_rn(__fsub_rn(x, e), __fsub_rn(1.0f, uf)), twopk);
+    return __fmul_rn(__fadd_rn(__fsub_rn(x, __fadd_rn(e, uf)), 1.0f), twopk);
+}
+
+// tanh in f32 as Zig's std.math.tanh computes it (a port of musl tanhf):
+// three ranges of |x| through expm1, |x| > 10 saturating to 1.
+__device__ __forceinline__ float tanh_ref(float x) {
+    const uint32_t u = __float_as_uint(x);
+    const uint32_t ux = u & 0x7fffffffu;
+    const float ax = __uint_as_float(ux);
+    float t;
+    if (ux > 0x3f0c9f54u) {                        // |x| > log(3)/2, or NaN
+        if (ux > 0x41200000u) {                    // |x| > 10
+            t = __fadd_rn(1.0f, __fdiv_rn(0.0f, x));
+        } else {
+            t = expm1_ref(__fmul_rn(2.0f, ax));
+            t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(t, 2.0f)));
+        }
+    } else if (ux > 0x3e82c578u) {                 // |x| > log(5/3)/2
+        t = expm1_ref(__fmul_rn(2.0f, ax));
+        t = __fdiv_rn(t, __fadd_rn(t, 2.0f));
+    } else if (ux >= 0x00800000u) {                // |x| >= 2^-126
+        t = expm1_ref(__fmul_rn(-2.0f, ax));
+        t = __fdiv_rn(-t, __fadd_rn(t, 2.0f));
+    } else {                                       // subnormal
+        t = ax;
+    }
+    return (u >> 31) ? -t : t;
+}
+
+// The engine's logit prologue before sampling (engine.zig:341-354): with a
+// soft-cap s > 0, tanh(v / s) * s; then, when `scale_on`, v * inv (inv the
+// f32 reciprocal of logit_scale).
+__device__ __forceinline__ float prologue_ref(float v, float softcap, bool cap_on, float inv, bool scale_on) {
+    if (cap_on) v = __fmul_rn(tanh_ref(__fdiv_rn(v, softcap)), softcap);
+    if (scale_on) v = __fmul_rn(v, inv);
+    return v;
+}
+
 // p_i = exp((v - max) / T) exactly as sampler.zig:85 evaluates it.
 __device__ __forceinline__ float prob_unnorm(float v, float m, float t) {
     return exp_ref(__fdiv_rn(__fsub_rn(v, m), t));

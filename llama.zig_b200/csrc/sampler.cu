@@ -241,10 +241,23 @@ __device__ __forceinline__ float4 ldg_stream(const float4 *p) {
     return v;
 }
 
+// The engine's logit prologue (engine.zig:341-354) as applied here: PRO_CAP
+// the soft-cap tanh(v / softcap) * softcap, then PRO_SCALE v * pinv (pinv the
+// f32 reciprocal of logit_scale).  pro == 0: the logits as given.
+enum : uint32_t { PRO_CAP = 1u, PRO_SCALE = 2u };
+struct Prologue {
+    uint32_t pro;
+    float softcap, pinv;
+    __device__ __forceinline__ float operator()(float v) const {
+        return prologue_ref(v, softcap, (pro & PRO_CAP) != 0u, pinv, (pro & PRO_SCALE) != 0u);
+    }
+};
+
 // ---------------------------------------------------------------------------
-// sampleArgmax (sampler.zig:31-41): one CTA per row.
+// sampleArgmax (sampler.zig:31-41): one CTA per row, of the logits after the
+// prologue (the engine applies it before sampling).
 __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ logits, size_t ld,
-                                                     uint32_t vocab, uint32_t *__restrict__ out) {
+                                                     uint32_t vocab, uint32_t *__restrict__ out, Prologue pr) {
     const uint32_t row = blockIdx.x;
     const float *x = logits + (size_t)row * ld;
     ArgBest best{NEG_INF, 0xFFFFFFFFu};
@@ -255,7 +268,11 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
         const float4 *x4 = reinterpret_cast<const float4 *>(x);
         for (uint32_t i = threadIdx.x; i < n4; i += blockDim.x) {
             const float4 v = ldg_stream(x4 + i);
-            const float a[4] = {v.x, v.y, v.z, v.w};
+            float a[4] = {v.x, v.y, v.z, v.w};
+            if (pr.pro) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) a[k] = pr(a[k]);
+            }
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const float f = a[k] != a[k] ? NEG_INF : a[k];
@@ -265,7 +282,7 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
         done = n4 * 4;
     }
     for (uint32_t i = done + threadIdx.x; i < vocab; i += blockDim.x) {
-        const float f = x[i];
+        const float f = pr.pro ? pr(x[i]) : x[i];
         best = arg_better(best, ArgBest{f != f ? NEG_INF : f, i});
     }
     best = warp_arg(best);
@@ -275,7 +292,7 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ l
     if (threadIdx.x == 0) {
         ArgBest b = wb[0];
         for (int w = 1; w < (int)(blockDim.x >> 5); w++) b = arg_better(b, wb[w]);
-        const float x0 = x[0];
+        const float x0 = pr.pro ? pr(x[0]) : x[0];
         uint32_t r = b.i;
         if (x0 != x0 || b.i == 0xFFFFFFFFu) r = 0;  // leading NaN wins; all -inf -> 0
         out[row] = r;
@@ -548,6 +565,10 @@ struct K12Params {
     uint32_t cand_stride;
     uint32_t *kerr;           // per handle: the call whose bounded device wait gave up
     uint32_t seq;             // this call's sequence number (never 0)
+    // logit prologue (engine.zig:341-354): PRO_CAP soft-cap tanh(v / softcap) * softcap,
+    // then PRO_SCALE v * pinv
+    uint32_t pro;
+    float softcap, pinv;
     // persistent kernel (k_fused): task scheduler state of this call
     uint32_t *ctl;            // [0] next statistics task, [1] next main task, [2] ready rows;
                               // then per call row: statistics tasks done; all zeroed before the call
@@ -555,6 +576,8 @@ struct K12Params {
 };
 
 __device__ __forceinline__ bool penalty_active(const K12Params &P) { return P.pen_bm != nullptr; }
+
+__device__ __forceinline__ Prologue prologue_of(const K12Params &P) { return Prologue{P.pro, P.softcap, P.pinv}; }
 
 // The repetition penalty of one logit (sampler.zig:62-66).
 __device__ __forceinline__ float penalize(float a, float pen) {
@@ -609,7 +632,7 @@ __device__ double block_exscan1_d(double v, double *wtmp, double *total) {
 // rows that cannot be staged in shared memory, and one out-of-line copy keeps
 // the staged loops' instruction footprint small.
 __device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vocab, float rep_penalty, uint64_t pol,
-                                         const uint32_t *bm) {
+                                         const uint32_t *bm, Prologue pr) {
     float4 q;
     if (g + 4 <= vocab && (reinterpret_cast<uintptr_t>(x + g) & 15u) == 0) {
         q = ldg_policy(reinterpret_cast<const float4 *>(x + g), pol);
@@ -619,6 +642,12 @@ __device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vo
         q.z = g + 2 < vocab ? x[g + 2] : NEG_INF;
         q.w = g + 3 < vocab ? x[g + 3] : NEG_INF;
     }
+    if (pr.pro) {   // the logit prologue comes before the penalty (the engine applies it first)
+        q.x = pr(q.x);
+        q.y = pr(q.y);
+        q.z = pr(q.z);
+        q.w = pr(q.w);
+    }
     if (bm) {
         const uint32_t bits = (bm[g >> 5] >> (g & 31u)) & 0xFu;
         if (bits & 1u) q.x = penalize(q.x, rep_penalty);
@@ -627,6 +656,14 @@ __device__ __noinline__ float4 load_quad(const float *x, uint32_t g, uint32_t vo
         if (bits & 8u) q.w = penalize(q.w, rep_penalty);
     }
     return q;
+}
+
+// The logit prologue on the staged copy of tile `tl` (32 logits at
+// sf[32 tl ..]), by the tile's owner thread, before the penalty.
+__device__ __forceinline__ void prologue_tile_smem(const K12Params &P, uint32_t tl, float *sf) {
+    const Prologue pr = prologue_of(P);
+#pragma unroll 4
+    for (int k = 0; k < TILE; k++) sf[tl * TILE + k] = pr(sf[tl * TILE + k]);
 }
 
 // The repetition penalty on the staged copy of tile `tl` (32 logits at
@@ -776,7 +813,7 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
     } else {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float4 q = load_quad(x, g0 + tile_elem(tl, j, 0), P.vocab, P.rep_penalty, pol, bm);
+            const float4 q = load_quad(x, g0 + tile_elem(tl, j, 0), P.vocab, P.rep_penalty, pol, bm, prologue_of(P));
             v[4 * j] = q.x;
             v[4 * j + 1] = q.y;
             v[4 * j + 2] = q.z;
@@ -790,7 +827,7 @@ __device__ __forceinline__ void load_tile32(const K12Params &P, const float *x, 
 __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, uint32_t seg, uint32_t tl, int j,
                                             const float4 *sbuf, bool staged, const uint32_t *bm, uint64_t pol) {
     const uint32_t g = seg * SEG_ELEMS + tl * TILE + tile_elem(tl, j, 0);
-    if (!staged) return load_quad(x, g, P.vocab, P.rep_penalty, pol, bm);
+    if (!staged) return load_quad(x, g, P.vocab, P.rep_penalty, pol, bm, prologue_of(P));
     float4 q = sbuf[tl * 8 + ((uint32_t)j ^ (tl & 7u))];
     if (g + 4 > P.vocab) {
         q.x = g < P.vocab ? q.x : NEG_INF;
@@ -852,7 +889,9 @@ __device__ __forceinline__ void stats_task(const K12Params &P, uint32_t seg, uin
     const bool staged = bulk && seg_wait(P, &bar);
 
     const bool live = (uint32_t)tid < ntile;
-    // the penalty on this thread's own staged tile (read back by it alone)
+    // the prologue and the penalty on this thread's own staged tile (read
+    // back by it alone)
+    if (staged && P.pro && live) prologue_tile_smem(P, tid, reinterpret_cast<float *>(sbuf));
     if (staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
     float v[TILE];
     load_tile32(P, x, seg, live ? tid : 0u, sbuf, staged, bm, pol, v);
@@ -1456,8 +1495,9 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     const bool check_nan = ri.check_nan != 0;
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
     const bool staged = bulk && seg_wait(P, &bar);
-    // the penalty on this thread's own staged tile; other threads read it
-    // only after the barriers below
+    // the prologue and the penalty on this thread's own staged tile; other
+    // threads read it only after the barriers below
+    if (staged && P.pro && live) prologue_tile_smem(P, tid, reinterpret_cast<float *>(sbuf));
     if (staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
     const uint32_t tt = live ? (uint32_t)tid : 0u;
     auto quad = [&](int j) { return tile_quad(P, x, seg, tt, j, sbuf, staged, bm, pol); };
@@ -1632,6 +1672,7 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
             const uint32_t e = rcl[i], lt = e >> 5;
             const uint32_t g = seg * SEG_ELEMS + lt * TILE + (e & 31u);
             float a = staged ? sb[lt * TILE + (e & 31u)] : x[g];
+            if (!staged) a = prologue_of(P)(a);
             if (!staged && bm && ((bm[g >> 5] >> (g & 31u)) & 1u)) a = penalize(a, P.rep_penalty);
             const float pt = TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S);
             const Comp c = elem_comp(pt, rec[lt].lo);
@@ -1665,7 +1706,8 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
         const uint32_t g = tt * TILE + lane;
         float a = NEG_INF;
         if (g < P.vocab) a = staged ? reinterpret_cast<const float *>(sbuf)[lt * TILE + lane] : x[g];
-        // the penalty (the staged copy has it already)
+        // the prologue and the penalty (the staged copy has them already)
+        if (!staged && g < P.vocab) a = prologue_of(P)(a);
         if (!staged && bm && g < P.vocab && ((bm[g >> 5] >> (g & 31u)) & 1u)) a = penalize(a, P.rep_penalty);
         const float p = g < P.vocab ? (TERM == TERM_P ? prob_unnorm(a, M, T) : entropy_term(a, M, T, S)) : 0.0f;
         r.qlo = warp_tile_comp(elem_comp(p, r.lo));
@@ -2080,6 +2122,8 @@ struct KBParams {
     RowTrace *trace;     // per handle row
     const uint32_t *kerr;   // == seq: a bounded wait of this call gave up
     uint32_t seq;
+    uint32_t pro;           // as K12Params
+    float softcap, pinv;
     const RowInfo *rinfo;   // per handle row
     uint32_t tmode;      // TYP_*
     uint32_t *out;       // per call row
@@ -2160,20 +2204,23 @@ __global__ void crossing_check_kernel(WTile *scratch, uint32_t max_ntl, unsigned
     }
 }
 
-// Exact p of element g (with the repetition penalty when the row's bitmap
-// `bm` marks it), for the recompute path.
+// Exact p of element g (the logit prologue, then the repetition penalty when
+// the row's bitmap `bm` marks it), for the recompute path.
 __device__ __forceinline__ float exact_p_raw(const float *xrow, uint32_t vocab, uint32_t g, float M, float T,
-                                             float pen, const uint32_t *bm) {
+                                             float pen, const uint32_t *bm, Prologue pr) {
     if (g >= vocab) return 0.0f;
     float v = xrow[g];
+    if (pr.pro) v = pr(v);
     if (bm && ((bm[g >> 5] >> (g & 31u)) & 1u)) v = penalize(v, pen);
     return prob_unnorm(v, M, T);
 }
+__device__ __forceinline__ Prologue prologue_of(const KBParams &P) { return Prologue{P.pro, P.softcap, P.pinv}; }
 __device__ __forceinline__ const uint32_t *row_bitmap(const KBParams &P, uint32_t hrow) {
     return P.pen_bm ? P.pen_bm + (size_t)hrow * P.ntiles_total : nullptr;
 }
 __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t hrow, uint32_t g, float M) {
-    return exact_p_raw(P.logits + (size_t)row * P.ld, P.vocab, g, M, P.T, P.rep_penalty, row_bitmap(P, hrow));
+    return exact_p_raw(P.logits + (size_t)row * P.ld, P.vocab, g, M, P.T, P.rep_penalty, row_bitmap(P, hrow),
+                       prologue_of(P));
 }
 
 // The walker's recompute path: the warp adds one tile's terms, p (TERM_P)
@@ -2182,10 +2229,10 @@ __device__ float exact_p_at(const KBParams &P, uint32_t row, uint32_t hrow, uint
 // and inlined it would sit in the middle of the walk's hot code.
 template <int TERM>
 __device__ __noinline__ float walk_recompute_tile(float s, const float *xrow, uint32_t vocab, uint32_t tile, float M,
-                                                  float T, float pen, const uint32_t *bm, float S,
+                                                  float T, float pen, const uint32_t *bm, Prologue pr, float S,
                                                   float *tilep) {
     const uint32_t lane = threadIdx.x & 31u;
-    float t = exact_p_raw(xrow, vocab, tile * TILE + lane, M, T, pen, bm);
+    float t = exact_p_raw(xrow, vocab, tile * TILE + lane, M, T, pen, bm, pr);
     if (TERM == TERM_H) {
         const float Pn = __fdiv_rn(t, S);
         t = Pn > 0.0f ? __fmul_rn(Pn, -log_ref(Pn)) : 0.0f;
@@ -2621,7 +2668,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         const float *xrow = P.logits + (size_t)row * P.ld;
         auto add_tile = [&](uint32_t tile) {
             st = state_of(walk_recompute_tile<TERM>(float_of(st), xrow, P.vocab, tile, M, P.T, P.rep_penalty,
-                                                    row_bitmap(P, hrow), Sx, tilep));
+                                                    row_bitmap(P, hrow), prologue_of(P), Sx, tilep));
         };
         // everything but the common case: a WINDOW crossing, a stored or
         // recomputed tile, a running sum outside the item's binades
@@ -2791,9 +2838,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         // sum <= 0 (sampler.zig:89): sampleArgmax of the raw logits.  Not
         // reachable with a finite maximum (its own term is exp(0) = 1).
         const float *x = P.logits + (size_t)row * P.ld;
+        const Prologue pr = prologue_of(P);   // the logits the engine passed: with the prologue, unpenalised
         ArgBest b{NEG_INF, 0xFFFFFFFFu};
         for (uint32_t i = tid; i < P.vocab; i += KB_THREADS) {
-            const float f = x[i];
+            const float f = pr.pro ? pr(x[i]) : x[i];
             b = arg_better(b, ArgBest{f != f ? NEG_INF : f, i});
         }
         b = warp_arg(b);
@@ -2802,7 +2850,8 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         if (tid == 0) {
             ArgBest bb = rbest[0];
             for (int w = 1; w < KB_THREADS / 32; w++) bb = arg_better(bb, rbest[w]);
-            rawarg_sh = (x[0] != x[0] || bb.i == 0xFFFFFFFFu) ? 0u : bb.i;
+            const float x0 = pr.pro ? pr(x[0]) : x[0];
+            rawarg_sh = (x0 != x0 || bb.i == 0xFFFFFFFFu) ? 0u : bb.i;
         }
         __syncthreads();
     }
@@ -3004,6 +3053,7 @@ struct bs_sampler {
     uint32_t *d_kerr;        // sequence number of the last call whose bounded device wait gave up
     uint32_t seq;            // sequence number of the last call (0 before the first)
     uint32_t fused;          // 1: the persistent kernel instead of separate statistics / row / main kernels
+    Prologue pro;            // the logit prologue set by bs_set_logit_prologue (pro.pro == 0: none)
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -3197,12 +3247,44 @@ extern "C" void bs_destroy(bs_sampler *s) {
     delete s;
 }
 
-extern "C" bs_status bs_argmax(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
+// The prologue for a model's final_logit_softcapping and logit_scale, as the
+// engine decides it (engine.zig:341,351): the soft-cap when it is > 0, the
+// scale unless it is 1 or 0; the reciprocal is one f32 division, as
+// `1.0 / cfg.logit_scale` in the engine.
+static Prologue make_prologue(float softcap, float logit_scale) {
+    Prologue p{0u, softcap, 1.0f};
+    if (softcap > 0.0f) p.pro |= PRO_CAP;
+    if (logit_scale != 1.0f && logit_scale != 0.0f) {
+        p.pro |= PRO_SCALE;
+        volatile float one = 1.0f;   // one IEEE f32 division at run time
+        p.pinv = one / logit_scale;
+    }
+    return p;
+}
+
+static bs_status argmax_launch(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab, Prologue pr,
                                uint32_t *d_out, void *stream) {
     if (!d_logits || !d_out || vocab == 0 || ld < vocab) return BS_EINVAL;
     if (rows == 0) return BS_OK;
-    argmax_kernel<<<rows, 512, 0, (cudaStream_t)stream>>>(d_logits, ld, vocab, d_out);
+    argmax_kernel<<<rows, 512, 0, (cudaStream_t)stream>>>(d_logits, ld, vocab, d_out, pr);
     return cuda_status(cudaGetLastError());
+}
+
+extern "C" bs_status bs_argmax(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
+                               uint32_t *d_out, void *stream) {
+    return argmax_launch(d_logits, ld, rows, vocab, Prologue{0u, 0.0f, 1.0f}, d_out, stream);
+}
+
+extern "C" bs_status bs_argmax_ex(const float *d_logits, size_t ld, uint32_t rows, uint32_t vocab,
+                                  float final_logit_softcapping, float logit_scale, uint32_t *d_out, void *stream) {
+    return argmax_launch(d_logits, ld, rows, vocab, make_prologue(final_logit_softcapping, logit_scale), d_out,
+                         stream);
+}
+
+extern "C" bs_status bs_set_logit_prologue(bs_sampler *s, float final_logit_softcapping, float logit_scale) {
+    if (!s) return BS_EINVAL;
+    s->pro = make_prologue(final_logit_softcapping, logit_scale);
+    return BS_OK;
 }
 
 // A launch that may overlap the previous kernel of the stream (the kernel
@@ -3231,8 +3313,9 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     if (rows == 0) return BS_OK;
     cudaStream_t st = (cudaStream_t)stream;
     const bs_config &c = s->cfg;
-    // sampler.zig:50 -- temperature <= 0: argmax of the raw logits, no draw
-    if (c.temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, s->vocab, d_out, stream);
+    // sampler.zig:50 -- temperature <= 0: argmax of the logits (after the
+    // engine's prologue), no penalty, no draw
+    if (c.temperature <= 0.0f) return argmax_launch(d_logits, ld, rows, s->vocab, s->pro, d_out, stream);
 
     // sampler.zig:58 -- the penalty applies to the last min(n_prev, window) ids
     const bool pen = c.repetition_penalty != 1.0f && d_prev != nullptr && n_prev > 0 && c.repetition_window > 0;
@@ -3265,6 +3348,9 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     A.cand_stride = s->cand_stride;
     A.kerr = s->d_kerr;
     A.seq = seq;
+    A.pro = s->pro.pro;
+    A.softcap = s->pro.softcap;
+    A.pinv = s->pro.pinv;
     A.ctl = s->d_fctl;
     A.ready = s->d_ready;
     A.typical_p = c.typical_p;
@@ -3294,6 +3380,9 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     B.trace = s->d_trace;
     B.kerr = s->d_kerr;
     B.seq = seq;
+    B.pro = s->pro.pro;
+    B.softcap = s->pro.softcap;
+    B.pinv = s->pro.pinv;
     B.rinfo = s->d_rinfo;
     B.tmode = A.tmode;
     B.out = d_out;
@@ -3681,7 +3770,7 @@ extern "C" bs_status bs_sample_static(const bs_config *cfg, uint64_t *d_rng, con
         return BS_EINVAL;
     }
     if (rows == 0) return BS_OK;
-    if (cfg->temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, vocab, d_out, stream);
+    if (cfg->temperature <= 0.0f) return bs_argmax(d_logits, ld, rows, vocab, d_out, stream);   // no prologue here
     int dev = 0;
     BS_CUDA(cudaGetDevice(&dev));
     unsigned char *base = nullptr;

@@ -33,7 +33,8 @@ BS_OK, BS_EINVAL, BS_ENOMEM, BS_ECUDA, BS_ENCCL, BS_ETIMEOUT, BS_ENOTSUP, BS_EIN
 EXPORTS = [
     "bs_config_default", "bs_create", "bs_sample", "bs_sample_host", "bs_argmax",
     "bs_get_rng_state", "bs_set_rng_state", "bs_last_device_status", "bs_destroy",
-    "bs_status_string", "bs_profile_enable", "bs_profile_read",
+    "bs_status_string", "bs_profile_enable", "bs_profile_read", "bs_argmax_ex", "bs_set_logit_prologue",
+    "bs_sample_static",
 ]
 
 
@@ -116,6 +117,8 @@ def lib() -> ctypes.CDLL:
         L.bs_sample.argtypes = [vp, vp, ctypes.c_size_t, u32, u32, vp, u32, vp, vp]
         L.bs_sample_host.argtypes = [vp, vp, ctypes.c_size_t, u32, u32, vp, u32, vp]
         L.bs_argmax.argtypes = [vp, ctypes.c_size_t, u32, u32, vp, vp]
+        L.bs_argmax_ex.argtypes = [vp, ctypes.c_size_t, u32, u32, ctypes.c_float, ctypes.c_float, vp, vp]
+        L.bs_set_logit_prologue.argtypes = [vp, ctypes.c_float, ctypes.c_float]
         L.bs_get_rng_state.argtypes = [vp, u64p]
         L.bs_set_rng_state.argtypes = [vp, u64p]
         L.bs_last_device_status.argtypes = [vp]
@@ -126,7 +129,8 @@ def lib() -> ctypes.CDLL:
         L.bs_debug_row_traces.argtypes = [vp, vp, ctypes.c_size_t]
         L.bs_profile_enable.argtypes = [vp, u32]
         L.bs_profile_read.argtypes = [vp, vp, u32, ctypes.POINTER(u32)]
-        for name in ("bs_create", "bs_sample", "bs_sample_host", "bs_argmax", "bs_get_rng_state",
+        for name in ("bs_create", "bs_sample", "bs_sample_host", "bs_argmax", "bs_argmax_ex",
+                     "bs_set_logit_prologue", "bs_get_rng_state",
                      "bs_set_rng_state", "bs_last_device_status", "bs_debug_row_traces",
                      "bs_profile_enable", "bs_profile_read"):
             getattr(L, name).restype = ctypes.c_int
@@ -252,6 +256,12 @@ class Sampler:
         _check(lib().bs_set_rng_state(self._h, a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))),
                "bs_set_rng_state")
 
+    def set_logit_prologue(self, final_logit_softcapping: float = 0.0, logit_scale: float = 1.0) -> None:
+        """The engine's logit prologue (engine.zig:341-354) for every later
+        sample(): soft-cap tanh(v / s) * s when s > 0, then v * (1 / logit_scale)
+        unless it is 1 or 0; the model's ModelConfig fields (model.zig:34-35)."""
+        _check(lib().bs_set_logit_prologue(self._h, final_logit_softcapping, logit_scale), "bs_set_logit_prologue")
+
     def last_status(self) -> int:
         return lib().bs_last_device_status(self._h)
 
@@ -275,14 +285,15 @@ class Sampler:
         return tr
 
 
-def sample_argmax(logits, out=None, stream=None):
-    """sampleArgmax (sampler.zig:31-41) on each row of a CUDA float32 tensor."""
+def sample_argmax(logits, out=None, stream=None, final_logit_softcapping: float = 0.0, logit_scale: float = 1.0):
+    """sampleArgmax (sampler.zig:31-41) on each row of a CUDA float32 tensor,
+    after the engine's logit prologue when a soft-cap or scale is given."""
     import torch
     x = logits if logits.dim() == 2 else logits.unsqueeze(0)
     if x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1:
         raise ValueError("logits must be a CUDA float32 tensor with unit column stride")
     if out is None:
         out = torch.empty(x.shape[0], dtype=torch.int32, device=x.device)
-    _check(lib().bs_argmax(x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], out.data_ptr(),
-                           _stream_ptr(stream)), "bs_argmax")
+    _check(lib().bs_argmax_ex(x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], final_logit_softcapping,
+                              logit_scale, out.data_ptr(), _stream_ptr(stream)), "bs_argmax_ex")
     return out

@@ -84,6 +84,12 @@ def lib() -> ctypes.CDLL:
         L.orc_expf.restype = ctypes.c_float
         L.orc_logf.argtypes = [ctypes.c_float]
         L.orc_logf.restype = ctypes.c_float
+        L.orc_expm1f.argtypes = [ctypes.c_float]
+        L.orc_expm1f.restype = ctypes.c_float
+        L.orc_tanhf.argtypes = [ctypes.c_float]
+        L.orc_tanhf.restype = ctypes.c_float
+        L.orc_prologue.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float, ctypes.c_float]
+        L.orc_prologue.restype = None
         L.orc_sampler_init.argtypes = [ctypes.POINTER(OrcSampler), ctypes.POINTER(OrcConfig)]
         L.orc_argmax.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.orc_argmax.restype = ctypes.c_uint32
@@ -130,6 +136,14 @@ class Sampler:
                                None if p is None else p.ctypes.data, 0 if p is None else p.size,
                                ctypes.byref(tr))
         return (tok, tr) if trace else tok
+
+
+def prologue(logits: np.ndarray, softcap: float, logit_scale: float) -> np.ndarray:
+    """The engine's logit prologue (engine.zig:341-354) on a copy: soft-cap
+    tanh(v / s) * s when s > 0, then v *= 1 / logit_scale unless it is 1 or 0."""
+    x = np.array(logits, dtype=np.float32, copy=True, order="C")
+    lib().orc_prologue(x.ctypes.data, x.size, softcap, logit_scale)
+    return x
 
 
 def argmax(logits: np.ndarray) -> int:

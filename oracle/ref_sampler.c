@@ -152,6 +152,109 @@ static const float LOG_LG2 = 0xccce13.0p-25f;     /* 0.40000972152 */
 static const float LOG_LG3 = 0x91e9ee.0p-25f;     /* 0.28498786688 */
 static const float LOG_LG4 = 0xf89e26.0p-26f;     /* 0.24279078841 */
 
+/* exp(x) - 1 in f32 as Zig's std.math.expm1 computes it (a port of the
+ * musl / FreeBSD msun expm1f): reduction x = k ln2 + r with ln2 split in two,
+ * the scheme's published two-coefficient rational correction (Q1, Q2), and
+ * the scheme's case split on k for the reconstruction. */
+float orc_expm1f(float x) {
+    const float o_threshold = 8.8721679688e+01f;   /* 0x42b17180 */
+    const float ln2_hi = 6.9313812256e-01f;        /* 0x3f317180 */
+    const float ln2_lo = 9.0580006145e-06f;        /* 0x3717f7d1 */
+    const float invln2 = 1.4426950216e+00f;        /* 0x3fb8aa3b */
+    const float Q1 = -3.3333212137e-2f;            /* -0x888868.0p-28 */
+    const float Q2 = 1.5807170421e-3f;             /* 0xcf3010.0p-33 */
+    float y, hi, lo, c = 0.0f, t, e, hxs, hfx, r1, twopk;
+    const uint32_t ux = f2u(x);
+    const uint32_t hx = ux & 0x7fffffffu;
+    const int sign = (int)(ux >> 31);
+    int k;
+    if (hx >= 0x4195b844u) {                       /* |x| >= 27 ln2 */
+        if (hx > 0x7f800000u) return x;            /* NaN */
+        if (sign) return -1.0f;
+        if (x > o_threshold) return x * 0x1p127f;  /* overflow */
+    }
+    if (hx > 0x3eb17218u) {                        /* |x| > ln2/2 */
+        if (hx < 0x3f851592u) {                    /* and |x| < 3ln2/2 */
+            if (!sign) { hi = x - ln2_hi; lo = ln2_lo; k = 1; }
+            else       { hi = x + ln2_hi; lo = -ln2_lo; k = -1; }
+        } else {
+            k = (int)(invln2 * x + (sign ? -0.5f : 0.5f));
+            t = (float)k;
+            hi = x - t * ln2_hi;
+            lo = t * ln2_lo;
+        }
+        x = hi - lo;
+        c = (hi - x) - lo;
+    } else if (hx < 0x33000000u) {                 /* |x| < 2^-25 */
+        return x;
+    } else {
+        k = 0;
+    }
+    hfx = 0.5f * x;
+    hxs = x * hfx;
+    r1 = 1.0f + hxs * (Q1 + hxs * Q2);
+    t = 3.0f - r1 * hfx;
+    e = hxs * ((r1 - t) / (6.0f - x * t));
+    if (k == 0) return x - (x * e - hxs);
+    e = x * (e - c) - c;
+    e -= hxs;
+    if (k == -1) return 0.5f * (x - e) - 0.5f;
+    if (k == 1) {
+        if (x < -0.25f) return -2.0f * (e - (x + 0.5f));
+        return 1.0f + 2.0f * (x - e);
+    }
+    twopk = u2f((uint32_t)(0x7f + k) << 23);
+    if (k < 0 || k > 56) {
+        y = x - e + 1.0f;
+        if (k == 128) y = y * 2.0f * 0x1p127f;
+        else y = y * twopk;
+        return y - 1.0f;
+    }
+    const float uf = u2f((uint32_t)(0x7f - k) << 23);
+    if (k < 23) return (x - e + (1.0f - uf)) * twopk;
+    return (x - (e + uf) + 1.0f) * twopk;
+}
+
+/* tanh in f32 as Zig's std.math.tanh computes it (a port of musl tanhf):
+ * three ranges of |x| through expm1, |x| > 10 saturating to 1. */
+float orc_tanhf(float x) {
+    const uint32_t u = f2u(x);
+    const uint32_t ux = u & 0x7fffffffu;
+    const float ax = u2f(ux);
+    const int sign = (int)(u >> 31);
+    float t;
+    if (ux > 0x3f0c9f54u) {                        /* |x| > log(3)/2, or NaN */
+        if (ux > 0x41200000u) {                    /* |x| > 10 */
+            t = 1.0f + 0.0f / x;
+        } else {
+            t = orc_expm1f(2.0f * ax);
+            t = 1.0f - 2.0f / (t + 2.0f);
+        }
+    } else if (ux > 0x3e82c578u) {                 /* |x| > log(5/3)/2 */
+        t = orc_expm1f(2.0f * ax);
+        t = t / (t + 2.0f);
+    } else if (ux >= 0x00800000u) {                /* |x| >= 2^-126 */
+        t = orc_expm1f(-2.0f * ax);
+        t = -t / (t + 2.0f);
+    } else {                                       /* subnormal */
+        t = ax;
+    }
+    return sign ? -t : t;
+}
+
+/* The engine's logit prologue before sampling (engine.zig:341-354,
+ * main.zig:653-666): with a soft-cap s > 0 every logit becomes
+ * tanh(v / s) * s; then, unless logit_scale is 1 or 0, v *= 1 / logit_scale
+ * (the reciprocal rounded once, as f32). */
+void orc_prologue(float *logits, size_t n, float softcap, float logit_scale) {
+    if (softcap > 0.0f)
+        for (size_t i = 0; i < n; i++) logits[i] = orc_tanhf(logits[i] / softcap) * softcap;
+    if (logit_scale != 1.0f && logit_scale != 0.0f) {
+        const float inv = 1.0f / logit_scale;
+        for (size_t i = 0; i < n; i++) logits[i] *= inv;
+    }
+}
+
 float orc_logf(float x) {
     uint32_t ix = f2u(x);
     int k = 0;

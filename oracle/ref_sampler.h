@@ -89,6 +89,10 @@ uint64_t orc_rng_next(uint64_t s[4]);              /* Xoshiro256.next */
 float orc_rng_float(uint64_t s[4], uint32_t *words);/* Random.float(f32) */
 float orc_expf(float x);                           /* compiler_rt expf */
 float orc_logf(float x);                           /* compiler_rt logf */
+float orc_expm1f(float x);                         /* std.math.expm1 (f32) */
+float orc_tanhf(float x);                          /* std.math.tanh (f32) */
+/* The engine's logit prologue (engine.zig:341-354): soft-cap, then 1/scale. */
+void orc_prologue(float *logits, size_t n, float softcap, float logit_scale);
 
 /* --- sampler.zig ---------------------------------------------------------- */
 void orc_sampler_init(orc_sampler *sp, const orc_config *cfg);

@@ -387,3 +387,53 @@ def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows):
     ref = run_oracle(orc, c, x, seeds)
     assert np.array_equal(np.array(toks), ref[0]), name
     assert np.array_equal(np.array(states), ref[1]), name
+
+
+@pytest.mark.parametrize("softcap,scale,fused", [(30.0, 1.0, 0), (0.0, 8.0, 0), (30.0, 0.5, 0), (30.0, 8.0, 1)])
+def test_logit_prologue_matches_checker(gpu_pkg, orc, softcap, scale, fused):
+    # the engine's prologue (engine.zig:341-354: soft-cap, then 1 / logit_scale)
+    # fused into the sampler, with a repetition penalty on top; the checker
+    # samples the logits the engine would hand it
+    import ctypes
+    w, x = _workload(gpu_pkg, "c1", 16, steps=2)
+    rng = np.random.default_rng(5)
+    prev = rng.integers(0, w.vocab, size=(2, 16, 24)).astype(np.uint32)
+    prev[:, :, -3:] = np.argsort(-x, axis=2)[:, :, :3]
+    c = w.config(repetition_window=16, repetition_penalty=1.3)
+    seeds = w.seeds(16)
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=16, vocab=w.vocab, seeds=seeds)
+    s.set_logit_prologue(softcap, scale)
+    L = gpu_pkg.sampler.lib()
+    L.bs_debug_set_fused.argtypes = [ctypes.c_void_p, ctypes.c_uint32]
+    L.bs_debug_set_fused(s._h, fused)
+    toks, states = [], []
+    for i in range(2):
+        pv = torch.from_numpy(prev[i].astype(np.int32)).cuda()
+        toks.append(s.sample(torch.from_numpy(x[i]).cuda(), pv).cpu().numpy().astype(np.uint32))
+        states.append(s.rng_state)
+        assert s.last_status() == 0
+    s.close()
+    xp = np.stack([orc.prologue(x[i], softcap, scale) for i in range(2)])
+    ref = run_oracle(orc, c, xp, seeds, prev)
+    assert np.array_equal(np.array(toks), ref[0])
+    assert np.array_equal(np.array(states), ref[1])
+
+
+@pytest.mark.parametrize("softcap,scale", [(30.0, 1.0), (0.0, 8.0), (5.0, 0.25)])
+def test_argmax_after_prologue(gpu_pkg, orc, softcap, scale):
+    # T <= 0 (sampler.zig:50) on the engine's logits: the soft-cap saturates
+    # large logits to equal values, so the first of them wins
+    w = gpu_pkg.workloads.WORKLOADS["c3_greedy"]
+    x = gpu_pkg.workloads.make_logits(w, rows=64, vocab=20000)
+    x[:, 7] = 500.0
+    x[:, 3000] = 400.0              # both saturate under a small soft-cap
+    got = gpu_pkg.sample_argmax(torch.from_numpy(x).cuda(), final_logit_softcapping=softcap,
+                                logit_scale=scale).cpu().numpy()
+    ref = np.array([orc.argmax(orc.prologue(x[r], softcap, scale)) for r in range(64)])
+    assert np.array_equal(got, ref)
+    c = dict(temperature=0.0, top_k=0, top_p=1.0, min_p=0.0, typical_p=1.0, seed=1,
+             repetition_window=0, repetition_penalty=1.0)
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=64, vocab=20000)
+    s.set_logit_prologue(softcap, scale)
+    assert np.array_equal(s.sample(torch.from_numpy(x).cuda()).cpu().numpy(), ref)
+    s.close()

@@ -218,3 +218,30 @@ def test_golden_fixture_reproduces(orc, path):
                                           states=states, prev=prev)
         assert np.array_equal(out, f["tokens"][s])
         assert np.array_equal(states, f["states"][s])
+
+
+def test_expm1_tanh_within_one_ulp(orc):
+    # the restated std.math.expm1 / std.math.tanh (musl scheme) against f64
+    L = orc.lib()
+    rng = np.random.default_rng(17)
+    xs = np.concatenate([rng.uniform(-20, 20, 20000), rng.uniform(-0.6, 0.6, 10000),
+                         rng.uniform(-1e-6, 1e-6, 2000), [0.0, -0.0, 10.0, 10.5, -30.0, 88.0]]).astype(np.float32)
+    # (musl's tanhf is within 2 ulp: its -t/(t+2) form rounds twice)
+    for f, ref_f, bound in ((L.orc_expm1f, np.expm1, 1), (L.orc_tanhf, np.tanh, 2)):
+        got = np.array([f(float(x)) for x in xs], np.float32)
+        ref = ref_f(xs.astype(np.float64)).astype(np.float32)
+        ulps = np.abs(got.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+        assert ulps.max() <= bound, (f, xs[np.argmax(ulps)])
+    assert L.orc_tanhf(float("inf")) == 1.0 and L.orc_tanhf(float("-inf")) == -1.0
+    assert np.isnan(L.orc_tanhf(float("nan")))
+
+
+def test_prologue_order(orc):
+    # soft-cap first, then the reciprocal of logit_scale (engine.zig:341-354)
+    x = np.array([-40.0, -3.0, 0.0, 2.5, 31.0], np.float32)
+    y = orc.prologue(x, 30.0, 4.0)
+    s, inv = np.float32(30.0), np.float32(1.0) / np.float32(4.0)
+    exp = np.array([np.float32(orc.lib().orc_tanhf(float(np.float32(v) / s))) * s for v in x], np.float32) * inv
+    assert np.array_equal(y, exp.astype(np.float32))
+    assert np.array_equal(orc.prologue(x, 0.0, 1.0), x)        # both off
+    assert np.array_equal(orc.prologue(x, 0.0, 0.0), x)        # scale 0 counts as off
