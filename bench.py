@@ -182,8 +182,11 @@ def run_reference(args, pkg, w):
 
 def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
     """Config 4: all B rows, vocab split over the ranks (a tensor-parallel LM
-    head).  One step = the all-to-all transpose, sampling this rank's B/G rows
-    and the all-gather of the B token ids (replicated on every rank)."""
+    head).  One step = the exact partial merge: statistics of this rank's
+    shard, one all-gather of per-row partials, the main pass, the chain of
+    walks over the shards in rank order, the broadcast of the normaliser, one
+    all-gather of the candidates and the draw (every rank returns the same B
+    token ids)."""
     B, V = w.rows, w.vocab
     cfg = pkg.SamplerConfig(**w.config())
     vs = pkg.sharding.VocabShardedSampler(cfg, B, V, dist if world > 1 else None, device=local)
@@ -205,8 +208,8 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
         end.record(stream)
         torch.cuda.synchronize()
     ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
-    if vs.local.last_status() != 0:
-        raise RuntimeError(f"sampler status {vs.local.last_status()}")
+    if vs.last_status() != 0:
+        raise RuntimeError(f"sampler status {vs.last_status()}")
     # end to end: pinned host shard -> device, sample, B token ids -> host
     pinned = [torch.from_numpy(h).pin_memory() for h in host[:2]]
     d_in = torch.empty_like(dev[0])
@@ -229,8 +232,9 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": workload_desc(w), "rows": B, "vocab": V,
-                       "parallelism": f"vocab-sharded x{world}: all-to-all transpose, B/G rows per rank, "
-                                      "all-gather of the token ids",
+                       "parallelism": (f"vocab-sharded x{world}: exact partial merge (all-gather of per-row "
+                                       "partials, chain of shard walks, all-gather of candidates)"
+                                       if vs.exact else f"vocab-sharded x{world}: all-to-all transpose"),
                        "l2": f"{ROTATE} rotating shard batches ({ROTATE * per_gpu_bytes / 1e6:.0f} MB per GPU)"},
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "traffic": None, "peak_kind": peak_kind,
@@ -239,7 +243,7 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
             "e2e": {"value": B * args.e2e_steps / e2e_s, "unit": "rows/s",
                     "h2d_bytes_per_step": int(per_gpu_bytes), "d2h_bytes_per_step": 4 * B,
                     "api": "VocabShardedSampler.sample (pinned host shard)"},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": (8 if vs.exact else 4) * args.steps,
         }
         print(json.dumps(line), flush=True)
     vs.close()

@@ -125,6 +125,38 @@ bs_status bs_argmax_ex(const float *d_logits, size_t ld, uint32_t rows, uint32_t
  * read, not rewritten.  (0, 1) turns it off. */
 bs_status bs_set_logit_prologue(bs_sampler *s, float final_logit_softcapping, float logit_scale);
 
+/* Vocabulary sharding for a tensor-parallel LM head:
+ * rank g of `world` holds columns [col0, col0 + vocab) of every row, the
+ * handle created with the shard width as its vocab and the same seeds on
+ * every rank.  Replaces the reference's LM head -> host logits -> sample
+ * sequence (src/compute_graph.zig:505-528, src/engine.zig:339-355) when the
+ * head is split over GPUs.  Exact: the tokens and RNG states equal a single
+ * Sampler's over the whole row.  One call is five steps on every rank, with
+ * the caller's collectives between them (stream-ordered, device buffers):
+ *   1 bs_vshard_stats   -> d_part (rows entries); all-gather -> [world][rows]
+ *   2 bs_vshard_main(parts, world, rank)
+ *   3 bs_vshard_walk(entry, exit): entry = NULL on rank 0, else the exit sums
+ *     received from rank - 1; send exit to rank + 1; the last rank's exit is
+ *     the row normaliser S: broadcast it from rank world - 1
+ *   4 bs_vshard_export -> d_cand (rows x BS_VSHARD_CAND_CAP), d_count (rows);
+ *     all-gather both -> [world][rows][..], [world][rows]
+ *   5 bs_vshard_draw(cand_all, count_all, world, S) -> d_out (rows tokens,
+ *     the same on every rank)
+ * Needs temperature > 0, 0 < top_k <= 256 and typical-p off (BS_ENOTSUP
+ * otherwise); a shard with more than BS_VSHARD_CAND_CAP candidates in a row
+ * fails that row (token 0xFFFFFFFF). */
+typedef struct bs_vshard_part { float max_logit; uint32_t nonfinite; double sum; } bs_vshard_part;
+typedef struct bs_vshard_cand { uint32_t id; float logit; } bs_vshard_cand;
+#define BS_VSHARD_CAND_CAP 512
+bs_status bs_vshard_stats(bs_sampler *s, const float *d_shard, size_t ld, uint32_t col0, uint32_t rows,
+                          const uint32_t *d_prev, uint32_t n_prev, bs_vshard_part *d_part, void *stream);
+bs_status bs_vshard_main(bs_sampler *s, const bs_vshard_part *d_parts, uint32_t world, uint32_t rank,
+                         void *stream);
+bs_status bs_vshard_walk(bs_sampler *s, const float *d_entry, float *d_exit, void *stream);
+bs_status bs_vshard_export(bs_sampler *s, uint32_t col0, bs_vshard_cand *d_cand, uint32_t *d_count, void *stream);
+bs_status bs_vshard_draw(bs_sampler *s, const bs_vshard_cand *d_cand_all, const uint32_t *d_count_all,
+                         uint32_t world, const float *d_S, uint32_t *d_out, void *stream);
+
 /* Per-row xoshiro256++ state, batch x 4 u64 (host memory).  Synchronous. */
 bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state);
 bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state);

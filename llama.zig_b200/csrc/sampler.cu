@@ -515,6 +515,14 @@ struct SegStat {
     double ssum2;      // sum of 2^x x
 };
 
+// Vocabulary sharding: one shard's partial of a row (its maximum, its sum of
+// 2^x relative to that maximum, a non-finite flag); 16 bytes.
+struct VsPart {
+    float m;
+    uint32_t nonfin;
+    double S;
+};
+
 struct RowInfo {   // written by the row reduction, read by the main and walk passes
     float M;
     float xf2;         // candidate floor, log2 p units
@@ -569,6 +577,10 @@ struct K12Params {
     // then PRO_SCALE v * pinv
     uint32_t pro;
     float softcap, pinv;
+    // vocabulary sharding: the gathered partials of every shard ([world][rows]),
+    // or nullptr; this shard's rank
+    const VsPart *vs_parts;
+    uint32_t vs_world, vs_rank;
     // persistent kernel (k_fused): task scheduler state of this call
     uint32_t *ctl;            // [0] next statistics task, [1] next main task, [2] ready rows;
                               // then per call row: statistics tasks done; all zeroed before the call
@@ -1082,7 +1094,29 @@ __device__ __forceinline__ void rows_task(const K12Params &P, uint32_t row, Rows
         m = warp_max(m);
         nf = __any_sync(0xffffffffu, nf != 0) ? 1u : 0u;
         // raw prefix at each segment start, in units of p(M) = 1
-        double run = 0.0;
+        double run = 0.0, vs_after = 0.0;
+        if (P.vs_parts) {
+            // a vocabulary shard: the row maximum over all shards, and the
+            // estimate of the lower-index shards' mass at this shard's start
+            float gm = NEG_INF;
+            uint32_t gnf = 0;
+            for (uint32_t h = lane; h < P.vs_world; h += 32) {
+                const VsPart q = P.vs_parts[(size_t)h * P.rows + row];
+                gm = fmaxf(gm, q.m);
+                gnf |= q.nonfin;
+            }
+            m = warp_max(gm);
+            nf = __any_sync(0xffffffffu, gnf != 0) ? 1u : 0u;
+            double before = 0.0, after = 0.0;
+            for (uint32_t h = lane; h < P.vs_world; h += 32) {
+                const VsPart q = P.vs_parts[(size_t)h * P.rows + row];
+                const double v = q.m > NEG_INF ? q.S * (double)ex2_approx((q.m - m) * c2) : 0.0;
+                if (h < P.vs_rank) before += v;
+                if (h > P.vs_rank) after += v;
+            }
+            run = warp_sum_d(before);
+            vs_after = warp_sum_d(after);
+        }
         for (uint32_t c0 = 0; c0 < ns; c0 += 32) {
             const uint32_t c = c0 + lane;
             double sv = 0.0;
@@ -1119,7 +1153,7 @@ __device__ __forceinline__ void rows_task(const K12Params &P, uint32_t row, Rows
         if (lane == 0) {
             ri.M = m;
             ri.check_nan = nf | ((P.T != P.T) ? 1u : 0u);
-            ri.S_raw = run;
+            ri.S_raw = run + vs_after;
             ri.H_raw = (P.tmode == TYP_BAND && run > 0.0) ? log(run) - 0.6931471805599453 * e2 / run : 0.0;
             ri.dband = __int_as_float(0x7f800000);
             ri.tmode = P.tmode;
@@ -2098,6 +2132,9 @@ __global__ void __launch_bounds__(K12_THREADS, FUSED_CTAS_PER_SM) k_fused(K12Par
 }
 
 // ---------------------------------------------------------------------------
+enum : uint32_t { VS_OFF = 0, VS_WALK = 1, VS_DRAW = 2 };
+constexpr uint32_t VS_CAND_CAP = 512;   // candidates a shard exports per row (BS_VSHARD_CAND_CAP)
+
 struct KBParams {
     const float *logits;
     size_t ld;
@@ -2124,6 +2161,14 @@ struct KBParams {
     uint32_t seq;
     uint32_t pro;           // as K12Params
     float softcap, pinv;
+    // vocabulary sharding: VS_WALK walks this shard's items from the running
+    // sum vs_entry[row] (nullptr: the empty sum) and writes the sum after them
+    // to vs_exit[row]; VS_DRAW takes the row's normaliser from vs_S[row] and
+    // draws from the merged candidates of every shard
+    uint32_t vs_mode;
+    const float *vs_entry;
+    float *vs_exit;
+    const float *vs_S;
     const RowInfo *rinfo;   // per handle row
     uint32_t tmode;      // TYP_*
     uint32_t *out;       // per call row
@@ -2656,12 +2701,16 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     }
     __syncthreads();
 
-    if (warp == 0) {
+    if (warp == 0 && P.vs_mode == VS_DRAW) {
+        // the normaliser of every shard's terms, from the chain of walks
+        if (lane == 0) S_sh = P.vs_S[row];
+    } else if (warp == 0) {
         // ---- the exact walk of the sequential f32 sum (skipped for a NaN
         // row, whose sum is NaN whatever the order; warp 0 must still stay
         // out of the sort's named barrier below) ----
-        if (!(flags0 & RF_NAN)) {
-        SumState st{-126, 0u};
+        const float entry = P.vs_entry ? P.vs_entry[row] : 0.0f;
+        if (!(flags0 & RF_NAN) && entry == entry) {
+        SumState st = state_of(entry);   // the empty sum: binade -126, count 0
         uint32_t wflags = 0, nitems_all = 0, nslow = 0;
         const WTile *wrow = P.wpre + (size_t)hrow * P.ntiles_total;
         // add one tile element by element, p recomputed from the logits
@@ -2770,7 +2819,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
             walk_slow = nslow;
         }
         }
-    } else if (TERM == TERM_P && !big) {
+    } else if (TERM == TERM_P && !big && P.vs_mode != VS_WALK) {
         // ---- candidate keys (exact p), then the sort in shared memory,
         // ascending key, while warp 0 walks ----
         const int t2 = tid - 32, nthr = KB_THREADS - 32;
@@ -2804,6 +2853,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         asm volatile("bar.sync 1, %0;" ::"r"(nthr));
     }
     __syncthreads();
+    if (P.vs_mode == VS_WALK) {   // this shard's part of the chain ends here
+        if (tid == 0) P.vs_exit[row] = S_sh;
+        return;
+    }
     if (TERM == TERM_H) {
         typical_tail(P, row, hrow, S_sh, skeys, sprobs, red2);
         return;
@@ -2831,10 +2884,11 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
 
     const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
     const float S = S_sh;
-    const bool nan_row = (flags0 & RF_NAN) != 0;
+    // a NaN anywhere in the row makes the sum NaN (for shards: the chain's S)
+    const bool nan_row = P.vs_mode == VS_DRAW ? (S != S) : (flags0 & RF_NAN) != 0;
     __shared__ uint32_t rawarg_sh;
     __shared__ ArgBest rbest[KB_THREADS / 32];
-    if (!nan_row && !(S > 0.0f)) {
+    if (!nan_row && !(S > 0.0f) && P.vs_mode != VS_DRAW) {
         // sum <= 0 (sampler.zig:89): sampleArgmax of the raw logits.  Not
         // reachable with a finite maximum (its own term is exp(0) = 1).
         const float *x = P.logits + (size_t)row * P.ld;
@@ -2894,6 +2948,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     } else if (!(S > 0.0f)) {
         token = rawarg_sh;   // sampler.zig:89
         path = 1;
+        if (P.vs_mode == VS_DRAW) status = ROW_EINTERNAL;   // the raw logits are spread over the shards
     } else {
         // idxs[2*i] aliases the low word of keys[i]
         uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);
@@ -2935,8 +2990,9 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
             while (j < n_sel && !(probs[j] < thr)) j++;
             n_sel = j;
         }
-        const bool cover_ok = binding == 0 || binding == 1 || binding == 3 || binding == 4 || n_sel < n_pos ||
-                              (k_act && P.top_k <= n_pos);
+        const bool cover_ok = (binding == 0 || binding == 1 || binding == 3 || binding == 4 || n_sel < n_pos ||
+                               (k_act && P.top_k <= n_pos)) &&
+                              !(flags0 & RF_CAND_SHORT);   // (a shard's candidates overflowed)
         if (status != ROW_OK) {
             // a bounded device wait gave up: nothing of this call is trusted
         } else if (!cover_ok) {
@@ -3001,13 +3057,76 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     P.trace[hrow] = tr;
 }
 
+// Vocabulary sharding: each row's partial over this shard, from the
+// statistics pass's segment aggregates (one warp per row).
+__global__ void k_vs_partials(const SegStat *__restrict__ sstat, uint32_t nseg, uint32_t rows, float c2,
+                              VsPart *__restrict__ out) {
+    const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31u;
+    if (row >= rows) return;
+    const SegStat *S = sstat + (size_t)row * MAX_SEG;
+    float m = NEG_INF;
+    uint32_t nf = 0;
+    for (uint32_t c = lane; c < nseg; c += 32) {
+        m = fmaxf(m, S[c].smax);
+        nf |= S[c].nonfin;
+    }
+    m = warp_max(m);
+    nf = __any_sync(0xffffffffu, nf != 0) ? 1u : 0u;
+    double sum = 0.0;
+    for (uint32_t c = lane; c < nseg; c += 32)
+        if (S[c].smax > NEG_INF) sum += S[c].ssum * (double)ex2_approx((S[c].smax - m) * c2);
+    sum = warp_sum_d(sum);
+    if (lane == 0) out[row] = VsPart{m, nf, sum};
+}
+
+// This shard's candidates with global token ids (col0 added), at most
+// VS_CAND_CAP per row; count[row] = VS_CAND_CAP + 1 marks an overflow.
+__global__ void k_vs_export(const RowHdr *__restrict__ hdr, const Candidate *__restrict__ cand, uint32_t cand_stride,
+                            uint32_t col0, Candidate *__restrict__ out, uint32_t *__restrict__ count) {
+    const uint32_t row = blockIdx.x;
+    const uint32_t n = hdr[row].n_cand;
+    const uint32_t m = n < VS_CAND_CAP ? n : VS_CAND_CAP;
+    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+        const Candidate c = cand[(size_t)row * cand_stride + i];
+        out[(size_t)row * VS_CAND_CAP + i] = Candidate{c.idx + col0, c.v};
+    }
+    if (threadIdx.x == 0) count[row] = n <= VS_CAND_CAP ? n : VS_CAND_CAP + 1;
+}
+
+// The candidates of every shard ([world][rows][VS_CAND_CAP]) as this
+// handle's candidate list of each row (a shard that overflowed flags the row).
+__global__ void k_vs_merge(const Candidate *__restrict__ all, const uint32_t *__restrict__ counts, uint32_t world,
+                           uint32_t rows, RowHdr *__restrict__ hdr, Candidate *__restrict__ cand, uint32_t cand_stride) {
+    const uint32_t row = blockIdx.x;
+    __shared__ uint32_t base[65];
+    if (threadIdx.x == 0) {
+        uint32_t b = 0, over = 0;
+        for (uint32_t h = 0; h < world; h++) {
+            const uint32_t c = counts[(size_t)h * rows + row];
+            base[h] = b;
+            over |= c > VS_CAND_CAP ? 1u : 0u;
+            b += c > VS_CAND_CAP ? VS_CAND_CAP : c;
+        }
+        base[world] = b;
+        hdr[row].n_cand = b < cand_stride ? b : cand_stride;
+        if (over) atomicOr(&hdr[row].flags, RF_CAND_SHORT);   // the row cannot be drawn exactly
+    }
+    __syncthreads();
+    for (uint32_t h = 0; h < world; h++) {
+        const uint32_t n = base[h + 1] - base[h];
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+            if (base[h] + i < cand_stride)
+                cand[(size_t)row * cand_stride + base[h] + i] = all[((size_t)h * rows + row) * VS_CAND_CAP + i];
+    }
+}
+
 // Repetition-penalty pre-pass (sampler.zig:54-75), one CTA per row: the
 // row's bitmap of penalised ids, bit k of word t for token 32 t + k.  The
 // reference penalises each token id found among the last `win` previous
 // tokens once, however often it occurs there; ids outside the vocabulary
 // match no logit.
 __global__ void __launch_bounds__(256) k0_penalty(const uint32_t *__restrict__ prev, uint32_t n_prev, uint32_t win,
-                                                  uint32_t vocab, uint32_t row0, uint32_t words,
+                                                  uint32_t vocab, uint32_t col0, uint32_t row0, uint32_t words,
                                                   uint32_t *__restrict__ bm) {
     const uint32_t row = blockIdx.x;
     uint32_t *b = bm + (size_t)(row0 + row) * words;
@@ -3015,7 +3134,7 @@ __global__ void __launch_bounds__(256) k0_penalty(const uint32_t *__restrict__ p
     __syncthreads();
     const uint32_t *p = prev + (size_t)row * n_prev + (n_prev - win);
     for (uint32_t j = threadIdx.x; j < win; j += blockDim.x) {
-        const uint32_t id = p[j];
+        const uint32_t id = p[j] - col0;   // this (shard's) slice of the vocabulary
         if (id < vocab) atomicOr(&b[id >> 5], 1u << (id & 31u));
     }
 }
@@ -3054,6 +3173,11 @@ struct bs_sampler {
     uint32_t seq;            // sequence number of the last call (0 before the first)
     uint32_t fused;          // 1: the persistent kernel instead of separate statistics / row / main kernels
     Prologue pro;            // the logit prologue set by bs_set_logit_prologue (pro.pro == 0: none)
+    // the vocabulary-shard call in progress (bs_vshard_stats sets it up)
+    K12Params vs_A;
+    KBParams vs_B;
+    uint32_t vs_rows;
+    bool vs_ready;
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -3305,23 +3429,16 @@ static cudaError_t launch_dependent(void (*kern)(Args...), dim3 grid, dim3 block
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// One sampling call; `seq` numbers it for the error word (never 0).
-static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
-                             uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, void *stream) {
-    if (!s || !d_logits || !d_out || ld < s->vocab) return BS_EINVAL;
-    if (row0 > s->batch || rows > s->batch - row0) return BS_EINVAL;
-    if (rows == 0) return BS_OK;
-    cudaStream_t st = (cudaStream_t)stream;
+// The kernels' parameters of one call (rows [row0, row0 + rows) of the
+// handle, logits row i at d_logits + i ld).
+static void make_params(const bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
+                        uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, K12Params &A,
+                        KBParams &B, bool &pen, uint32_t &win) {
     const bs_config &c = s->cfg;
-    // sampler.zig:50 -- temperature <= 0: argmax of the logits (after the
-    // engine's prologue), no penalty, no draw
-    if (c.temperature <= 0.0f) return argmax_launch(d_logits, ld, rows, s->vocab, s->pro, d_out, stream);
-
     // sampler.zig:58 -- the penalty applies to the last min(n_prev, window) ids
-    const bool pen = c.repetition_penalty != 1.0f && d_prev != nullptr && n_prev > 0 && c.repetition_window > 0;
-    const uint32_t win = pen ? (n_prev < c.repetition_window ? n_prev : c.repetition_window) : 0u;
+    pen = c.repetition_penalty != 1.0f && d_prev != nullptr && n_prev > 0 && c.repetition_window > 0;
+    win = pen ? (n_prev < c.repetition_window ? n_prev : c.repetition_window) : 0u;
 
-    K12Params A;
     A.logits = d_logits;
     A.ld = ld;
     A.pen_bm = pen ? s->d_penbm : nullptr;
@@ -3353,10 +3470,12 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     A.pinv = s->pro.pinv;
     A.ctl = s->d_fctl;
     A.ready = s->d_ready;
+    A.vs_parts = nullptr;
+    A.vs_world = 1;
+    A.vs_rank = 0;
     A.typical_p = c.typical_p;
     A.tmode = typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p);
 
-    KBParams B;
     B.logits = d_logits;
     B.ld = ld;
     B.pen_bm = A.pen_bm;
@@ -3386,6 +3505,30 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     B.rinfo = s->d_rinfo;
     B.tmode = A.tmode;
     B.out = d_out;
+    B.vs_mode = VS_OFF;
+    B.vs_entry = nullptr;
+    B.vs_exit = nullptr;
+    B.vs_S = nullptr;
+
+}
+
+// One sampling call; `seq` numbers it for the error word (never 0).
+static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
+                             uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, void *stream) {
+    if (!s || !d_logits || !d_out || ld < s->vocab) return BS_EINVAL;
+    if (row0 > s->batch || rows > s->batch - row0) return BS_EINVAL;
+    if (rows == 0) return BS_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bs_config &c = s->cfg;
+    // sampler.zig:50 -- temperature <= 0: argmax of the logits (after the
+    // engine's prologue), no penalty, no draw
+    if (c.temperature <= 0.0f) return argmax_launch(d_logits, ld, rows, s->vocab, s->pro, d_out, stream);
+
+    K12Params A;
+    KBParams B;
+    bool pen = false;
+    uint32_t win = 0;
+    make_params(s, seq, d_logits, ld, row0, rows, d_prev, n_prev, d_out, A, B, pen, win);
 
     // statistics, row reduction | main pass | walk and draw.  With typical-p
     // the normaliser's walk hands over to a second main pass and walk over
@@ -3401,7 +3544,7 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
         const uint32_t tasks = rows * s->nseg;
         if (e == cudaSuccess) e = cudaMemsetAsync(s->d_fctl, 0, (4 + (size_t)rows) * sizeof(uint32_t), st);
         if (e == cudaSuccess && pen)
-            k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, row0, s->ntiles_total, s->d_penbm);
+            k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, 0u, row0, s->ntiles_total, s->d_penbm);
         if (e == cudaSuccess) k_fused<<<(uint32_t)ctas < tasks ? (uint32_t)ctas : tasks, K12_THREADS, 0, st>>>(A);
         const dim3 g2(s->nseg * rows);
         if (A.tmode != TYP_OFF) {
@@ -3423,7 +3566,7 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     // statistics pass)
     const dim3 g12(s->nseg, rows), g2(s->nseg * rows);
     if (ev) cudaEventRecord(ev[0], st);
-    if (pen) k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, row0, s->ntiles_total, s->d_penbm);
+    if (pen) k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, 0u, row0, s->ntiles_total, s->d_penbm);
     k1_stats<<<g12, K12_THREADS, 0, st>>>(A);
     cudaError_t e = launch_dependent(k1_rows, dim3(rows), dim3(K12_THREADS), 0, st, A);
     if (ev) cudaEventRecord(ev[1], st);
@@ -3447,6 +3590,99 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
                                void *stream) {
     if (!s) return BS_EINVAL;
     return sample_impl(s, next_seq(s->seq), d_logits, ld, row0, rows, d_prev, n_prev, d_out, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary sharding, exact (a tensor-parallel LM head: rank g holds
+// columns [col0, col0 + vocab) of all rows; the handle's vocab is the shard
+// width).  The reference's normaliser is one sequential f32 sum over the
+// whole row in index order; it is reproduced as a chain over the shards in
+// rank order.  Per call, on every rank, with the collectives between the
+// steps done by the caller (NCCL):
+//   bs_vshard_stats   the statistics pass on the shard; per-row partials
+//   (all-gather of the partials, [world][rows])
+//   bs_vshard_main    row reduction against the global maximum and the lower
+//                     shards' mass estimate; the main pass (items, candidates)
+//   bs_vshard_walk    the walk of this shard's items from the running sum the
+//                     previous rank ended with (rank 0: the empty sum)
+//   (rank g receives rank g-1's exit sums and sends its own on; the last
+//    rank's exit is the normaliser S, broadcast to all ranks)
+//   bs_vshard_export  this shard's candidates with global ids
+//   (all-gather of the candidates)
+//   bs_vshard_draw    filters and the draw on the merged candidates, with the
+//                     row's RNG state (the same on every rank)
+// Exact only with a top-k bound: every kept token is among its shard's local
+// top-k, which each shard's candidates contain.
+static bool vs_supported(const bs_sampler *s) {
+    const bs_config &c = s->cfg;
+    return c.temperature > 0.0f && c.top_k > 0 && c.top_k <= (uint32_t)KSEL_MAX &&
+           typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p) == TYP_OFF;
+}
+
+extern "C" bs_status bs_vshard_stats(bs_sampler *s, const float *d_shard, size_t ld, uint32_t col0, uint32_t rows,
+                                     const uint32_t *d_prev, uint32_t n_prev, bs_vshard_part *d_part, void *stream) {
+    if (!s || !d_shard || !d_part || ld < s->vocab || rows == 0 || rows > s->batch) return BS_EINVAL;
+    if (!vs_supported(s)) return BS_ENOTSUP;
+    cudaStream_t st = (cudaStream_t)stream;
+    bool pen = false;
+    uint32_t win = 0;
+    make_params(s, next_seq(s->seq), d_shard, ld, 0, rows, d_prev, n_prev, nullptr, s->vs_A, s->vs_B, pen, win);
+    s->vs_rows = rows;
+    s->vs_ready = true;
+    if (pen)
+        k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, col0, 0u, s->ntiles_total, s->d_penbm);
+    k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(s->vs_A);
+    k_vs_partials<<<(rows + 7) / 8, 256, 0, st>>>(s->d_sstat, s->nseg, rows, s->vs_A.c2,
+                                                   reinterpret_cast<VsPart *>(d_part));
+    return cuda_status(cudaGetLastError());
+}
+
+extern "C" bs_status bs_vshard_main(bs_sampler *s, const bs_vshard_part *d_parts, uint32_t world, uint32_t rank,
+                                    void *stream) {
+    if (!s || !d_parts || world == 0 || world > 64 || rank >= world) return BS_EINVAL;
+    if (!s->vs_ready) return BS_EINVAL;
+    cudaStream_t st = (cudaStream_t)stream;
+    K12Params A = s->vs_A;
+    A.vs_parts = reinterpret_cast<const VsPart *>(d_parts);
+    A.vs_world = world;
+    A.vs_rank = rank;
+    k1_rows<<<s->vs_rows, K12_THREADS, 0, st>>>(A);
+    cudaError_t e = launch_dependent(k2_main<TERM_P>, dim3(s->nseg * s->vs_rows), dim3(K12_THREADS), 0, st, A);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return cuda_status(e);
+}
+
+extern "C" bs_status bs_vshard_walk(bs_sampler *s, const float *d_entry, float *d_exit, void *stream) {
+    if (!s || !d_exit || !s->vs_ready) return BS_EINVAL;
+    KBParams B = s->vs_B;
+    B.vs_mode = VS_WALK;
+    B.vs_entry = d_entry;
+    B.vs_exit = d_exit;
+    kernel_b<TERM_P><<<s->vs_rows, KB_THREADS, s->smem_b, (cudaStream_t)stream>>>(B);
+    return cuda_status(cudaGetLastError());
+}
+
+extern "C" bs_status bs_vshard_export(bs_sampler *s, uint32_t col0, bs_vshard_cand *d_cand, uint32_t *d_count,
+                                      void *stream) {
+    if (!s || !d_cand || !d_count || !s->vs_ready) return BS_EINVAL;
+    k_vs_export<<<s->vs_rows, 256, 0, (cudaStream_t)stream>>>(s->d_hdr, s->d_cand, s->cand_stride, col0,
+                                                               reinterpret_cast<Candidate *>(d_cand), d_count);
+    return cuda_status(cudaGetLastError());
+}
+
+extern "C" bs_status bs_vshard_draw(bs_sampler *s, const bs_vshard_cand *d_cand_all, const uint32_t *d_count_all,
+                                    uint32_t world, const float *d_S, uint32_t *d_out, void *stream) {
+    if (!s || !d_cand_all || !d_count_all || !d_S || !d_out || world == 0 || world > 64 || !s->vs_ready)
+        return BS_EINVAL;
+    cudaStream_t st = (cudaStream_t)stream;
+    k_vs_merge<<<s->vs_rows, 256, 0, st>>>(reinterpret_cast<const Candidate *>(d_cand_all), d_count_all, world,
+                                          s->vs_rows, s->d_hdr, s->d_cand, s->cand_stride);
+    KBParams B = s->vs_B;
+    B.vs_mode = VS_DRAW;
+    B.vs_S = d_S;
+    B.out = d_out;
+    kernel_b<TERM_P><<<s->vs_rows, KB_THREADS, s->smem_b, st>>>(B);
+    return cuda_status(cudaGetLastError());
 }
 
 extern "C" bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t ld, uint32_t row0,

@@ -119,6 +119,13 @@ def lib() -> ctypes.CDLL:
         L.bs_argmax.argtypes = [vp, ctypes.c_size_t, u32, u32, vp, vp]
         L.bs_argmax_ex.argtypes = [vp, ctypes.c_size_t, u32, u32, ctypes.c_float, ctypes.c_float, vp, vp]
         L.bs_set_logit_prologue.argtypes = [vp, ctypes.c_float, ctypes.c_float]
+        L.bs_vshard_stats.argtypes = [vp, vp, ctypes.c_size_t, u32, u32, vp, u32, vp, vp]
+        L.bs_vshard_main.argtypes = [vp, vp, u32, u32, vp]
+        L.bs_vshard_walk.argtypes = [vp, vp, vp, vp]
+        L.bs_vshard_export.argtypes = [vp, u32, vp, vp, vp]
+        L.bs_vshard_draw.argtypes = [vp, vp, vp, u32, vp, vp, vp]
+        for name in ("bs_vshard_stats", "bs_vshard_main", "bs_vshard_walk", "bs_vshard_export", "bs_vshard_draw"):
+            getattr(L, name).restype = ctypes.c_int
         L.bs_get_rng_state.argtypes = [vp, u64p]
         L.bs_set_rng_state.argtypes = [vp, u64p]
         L.bs_last_device_status.argtypes = [vp]

@@ -63,14 +63,26 @@ def aggregate_rows_per_s(shard: RowShard, steps: int, seconds: float) -> float:
 
 # ---------------------------------------------------------------------------
 # Vocab sharding (a tensor-parallel LM head): every rank holds all B rows of
-# a contiguous slice of the vocabulary.  sampler.zig's normaliser is a
-# sequential f32 sum in global index order, and the exact GPU path needs a
-# row's logits in that order, so the exchange is a transpose: one all-to-all
-# gives rank g complete rows [g B/G, (g+1) B/G) ((G-1)/G of its shard crosses
-# NVLink), rank g samples them (seeds keyed by the global row), and an
-# all-gather replicates the B token ids on every rank.  A merge of per-shard
-# partial sums would change the normaliser's rounding (about 1e-4 relative)
-# and with it the kept-set probabilities and draws near boundaries.
+# a contiguous slice of the vocabulary, columns [g V/G, (g+1) V/G).
+#
+# Exact partial merge (the default, when the configuration has a top-k
+# bound): sampler.zig's normaliser is one sequential f32 sum over the whole
+# row in index order, reproduced as a chain over the shards in rank order.
+#   1. each rank: statistics of its shard -> per-row partial (max, sum
+#      relative to it, non-finite flag); one all-gather of the partials
+#      (16 B per row per rank)
+#   2. each rank: row reduction against the global maximum and the lower
+#      shards' mass estimate; main pass over its shard
+#   3. chain: rank g walks its shard's items from the exact running sum
+#      rank g-1 ended with (4 B per row, point to point); the last rank's
+#      result is the normaliser S, broadcast to all ranks
+#   4. one all-gather of each shard's candidates (its local top-k and above)
+#   5. every rank: filters and draw over the merged candidates with the
+#      row's RNG state, so every rank returns the same B tokens
+# Without a top-k bound (or with typical-p) a shard's candidates need not
+# cover the kept set, and the sampler falls back to a transpose: one
+# all-to-all gives rank g complete rows [g B/G, (g+1) B/G), it samples them
+# on one GPU, and an all-gather replicates the B token ids.
 @dataclass(frozen=True)
 class VocabShard:
     rank: int
@@ -105,6 +117,10 @@ class VocabShard:
     def seeds(self, base_seed: int) -> np.ndarray:
         return (np.arange(self.row0, self.row0 + self.rows_per_rank, dtype=np.uint64)
                 + np.uint64(base_seed)).astype(np.uint64)
+
+    def all_seeds(self, base_seed: int) -> np.ndarray:
+        """Seeds of all B rows (the exact merge keeps every row's RNG on every rank)."""
+        return (np.arange(self.rows, dtype=np.uint64) + np.uint64(base_seed)).astype(np.uint64)
 
     def shard_of(self, full):
         """This rank's slice of a full (B, V) matrix (for tests and benchmarks)."""
@@ -143,31 +159,163 @@ def gather_tokens(lay: VocabShard, local, dist, out=None):
     return out
 
 
-class VocabShardedSampler:
-    """Sampler.sample over vocab-sharded logits: every rank passes its
-    (B, V/G) shard and gets the same B token ids back."""
+CAND_CAP = 512   # BS_VSHARD_CAND_CAP: candidates a shard exports per row
 
-    def __init__(self, cfg, rows: int, vocab: int, dist=None, device: int = 0, seeds_base: int | None = None):
+
+class _ShardState:
+    """One rank's handle and buffers of the exact partial merge."""
+
+    def __init__(self, cfg, lay: VocabShard, device: int, seeds):
         import torch
         from .sampler import Sampler
+        self.lay = lay
+        self.smp = Sampler(cfg, batch=lay.rows, vocab=lay.cols, device=device, seeds=seeds)
+        dev = torch.device("cuda", device)
+        B = lay.rows
+        self.part = torch.empty((B, 2), dtype=torch.int64, device=dev)          # 16 B per row
+        self.exit = torch.empty((B,), dtype=torch.float32, device=dev)
+        self.cand = torch.empty((B, CAND_CAP, 2), dtype=torch.int32, device=dev)
+        self.count = torch.empty((B,), dtype=torch.int32, device=dev)
+        self.out = torch.empty((B,), dtype=torch.int32, device=dev)
+
+    def _lib(self):
+        from .sampler import lib, _check
+        return lib(), _check
+
+    def stats(self, shard, prev, stream):
+        L, check = self._lib()
+        pp, n_prev = (None, 0) if prev is None else (prev.data_ptr(), prev.shape[1])
+        check(L.bs_vshard_stats(self.smp._h, shard.data_ptr(), shard.stride(0), self.lay.col0, self.lay.rows,
+                                pp, n_prev, self.part.data_ptr(), stream), "bs_vshard_stats")
+        return self.part
+
+    def main(self, parts_all, stream):
+        L, check = self._lib()
+        check(L.bs_vshard_main(self.smp._h, parts_all.data_ptr(), self.lay.world, self.lay.rank, stream),
+              "bs_vshard_main")
+
+    def walk(self, entry, stream):
+        L, check = self._lib()
+        check(L.bs_vshard_walk(self.smp._h, None if entry is None else entry.data_ptr(), self.exit.data_ptr(),
+                               stream), "bs_vshard_walk")
+        return self.exit
+
+    def export(self, stream):
+        L, check = self._lib()
+        check(L.bs_vshard_export(self.smp._h, self.lay.col0, self.cand.data_ptr(), self.count.data_ptr(), stream),
+              "bs_vshard_export")
+        return self.cand, self.count
+
+    def draw(self, cand_all, count_all, S, stream):
+        L, check = self._lib()
+        check(L.bs_vshard_draw(self.smp._h, cand_all.data_ptr(), count_all.data_ptr(), self.lay.world,
+                               S.data_ptr(), self.out.data_ptr(), stream), "bs_vshard_draw")
+        return self.out
+
+
+def exact_merge_supported(cfg) -> bool:
+    """The exact partial merge needs a top-k bound (0 < top_k <= 256), a
+    positive temperature and typical-p off."""
+    typ = 0.0 < cfg.typical_p < 1.0
+    return cfg.temperature > 0 and 0 < cfg.top_k <= 256 and not typ
+
+
+def sample_vocab_sharded_emulated(states, shards, prevs=None):
+    """The exact partial merge with every rank in this process on one GPU:
+    the collectives become copies.  `states` and `shards` are per rank.
+    Returns each rank's (B,) tokens (all equal)."""
+    import torch
+    stream = torch.cuda.current_stream().cuda_stream
+    G = len(states)
+    parts = torch.stack([st.stats(shards[g], None if prevs is None else prevs[g], stream).clone()
+                         for g, st in enumerate(states)])
+    for st in states:
+        st.main(parts, stream)
+    entry = None
+    for st in states:
+        entry = st.walk(entry, stream).clone()
+    S = entry
+    cands, counts = zip(*[(c.clone(), n.clone()) for c, n in (st.export(stream) for st in states)])
+    cand_all, count_all = torch.stack(cands), torch.stack(counts)
+    return [st.draw(cand_all, count_all, S, stream).clone() for st in states]
+
+
+class VocabShardedSampler:
+    """Sampler.sample over vocab-sharded logits: every rank passes its
+    (B, V/G) shard (and, for the repetition penalty, the (B, n_prev) previous
+    token ids) and gets the same B token ids back."""
+
+    def __init__(self, cfg, rows: int, vocab: int, dist=None, device: int = 0, seeds_base: int | None = None,
+                 exact: bool | None = None):
+        import torch
         world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
         rank = dist.get_rank() if world > 1 else 0
         self.lay = VocabShard(rank, world, rows, vocab)
         self.dist = dist
+        self.device = device
         base = cfg.seed if seeds_base is None else seeds_base
-        self.local = Sampler(cfg, batch=self.lay.rows_per_rank, vocab=vocab, device=device,
-                             seeds=self.lay.seeds(base))
+        self.exact = exact_merge_supported(cfg) if exact is None else exact
+        if self.exact and not exact_merge_supported(cfg):
+            raise ValueError("the exact partial merge needs 0 < top_k <= 256, temperature > 0 and typical-p off")
         dev = torch.device("cuda", device)
         R, C, G = self.lay.rows_per_rank, self.lay.cols, world
-        self._recv = torch.empty((G, R, C), dtype=torch.float32, device=dev) if G > 1 else None
-        self._rows = torch.empty((R, vocab), dtype=torch.float32, device=dev) if G > 1 else None
-        self._tok = torch.empty((R,), dtype=torch.int32, device=dev)
-        self._all = torch.empty((rows,), dtype=torch.int32, device=dev)
+        if self.exact:
+            self.st = _ShardState(cfg, self.lay, device, self.lay.all_seeds(base))
+            self._parts = torch.empty((G, rows, 2), dtype=torch.int64, device=dev)
+            self._cand_all = torch.empty((G, rows, CAND_CAP, 2), dtype=torch.int32, device=dev)
+            self._count_all = torch.empty((G, rows), dtype=torch.int32, device=dev)
+            self._entry = torch.empty((rows,), dtype=torch.float32, device=dev)
+            self._S = torch.empty((rows,), dtype=torch.float32, device=dev)
+        else:
+            from .sampler import Sampler
+            self.local = Sampler(cfg, batch=R, vocab=vocab, device=device, seeds=self.lay.seeds(base))
+            self._recv = torch.empty((G, R, C), dtype=torch.float32, device=dev) if G > 1 else None
+            self._rows = torch.empty((R, vocab), dtype=torch.float32, device=dev) if G > 1 else None
+            self._tok = torch.empty((R,), dtype=torch.int32, device=dev)
+            self._all = torch.empty((rows,), dtype=torch.int32, device=dev)
 
-    def sample(self, shard):
-        rows = rows_from_vocab_shards(self.lay, shard, self.dist, self._recv, self._rows)
-        self.local.sample(rows, out=self._tok)
-        return gather_tokens(self.lay, self._tok, self.dist, self._all)
+    def sample(self, shard, prev_tokens=None):
+        import torch
+        if not self.exact:
+            if prev_tokens is not None:
+                raise ValueError("the transpose path takes no previous tokens; use a top-k bound")
+            rows = rows_from_vocab_shards(self.lay, shard, self.dist, self._recv, self._rows)
+            self.local.sample(rows, out=self._tok)
+            return gather_tokens(self.lay, self._tok, self.dist, self._all)
+        lay, st, dist = self.lay, self.st, self.dist
+        stream = torch.cuda.current_stream().cuda_stream
+        prev = None if prev_tokens is None else prev_tokens.to(torch.int32).contiguous()
+        part = st.stats(shard, prev, stream)
+        if lay.world == 1:
+            self._parts[0].copy_(part)
+        else:
+            dist.all_gather_into_tensor(self._parts, part)
+        st.main(self._parts, stream)
+        entry = None
+        if lay.rank > 0:
+            dist.recv(self._entry, src=lay.rank - 1)
+            entry = self._entry
+        exit_ = st.walk(entry, stream)
+        if lay.rank < lay.world - 1:
+            dist.send(exit_, dst=lay.rank + 1)
+        else:
+            self._S.copy_(exit_)
+        if lay.world > 1:
+            dist.broadcast(self._S, src=lay.world - 1)
+        cand, count = st.export(stream)
+        if lay.world == 1:
+            self._cand_all[0].copy_(cand)
+            self._count_all[0].copy_(count)
+        else:
+            dist.all_gather_into_tensor(self._cand_all, cand)
+            dist.all_gather_into_tensor(self._count_all, count)
+        return st.draw(self._cand_all, self._count_all, self._S, stream)
+
+    def last_status(self) -> int:
+        return self.st.smp.last_status() if self.exact else self.local.last_status()
 
     def close(self):
-        self.local.close()
+        if self.exact:
+            self.st.smp.close()
+        else:
+            self.local.close()

@@ -437,3 +437,42 @@ def test_argmax_after_prologue(gpu_pkg, orc, softcap, scale):
     s.set_logit_prologue(softcap, scale)
     assert np.array_equal(s.sample(torch.from_numpy(x).cuda()).cpu().numpy(), ref)
     s.close()
+
+
+@pytest.mark.parametrize("world,rows,extras", [(2, 64, False), (4, 64, True), (8, 32, False), (2, 512, False)])
+def test_vocab_sharded_exact_merge_emulated(gpu_pkg, orc, world, rows, extras):
+    # config 4's exact partial merge with `world` ranks emulated on one GPU
+    # (the collectives are copies): every rank's tokens and RNG states equal
+    # one sampler's over the whole rows, over two steps; with extras, a
+    # repetition penalty and the logit prologue on every shard
+    sh = gpu_pkg.sharding
+    w = gpu_pkg.workloads.WORKLOADS["c4"]
+    c = w.config(repetition_window=16, repetition_penalty=1.3) if extras else w.config()
+    cfg = gpu_pkg.SamplerConfig(**c)
+    lays = [sh.VocabShard(g, world, rows, w.vocab) for g in range(world)]
+    states = [sh._ShardState(cfg, lay, 0, lay.all_seeds(w.seed)) for lay in lays]
+    if extras:
+        for st in states:
+            st.smp.set_logit_prologue(30.0, 2.0)
+    rng = np.random.default_rng(world)
+    x = np.stack([gpu_pkg.workloads.make_logits(w, step=s, rows=rows) for s in range(2)])
+    prev = rng.integers(0, w.vocab, size=(2, rows, 24)).astype(np.uint32) if extras else None
+    if extras:
+        prev[:, :, -3:] = np.argsort(-x, axis=2)[:, :, :3]
+    toks = []
+    for s in range(2):
+        shards = [torch.from_numpy(np.ascontiguousarray(lay.shard_of(x[s]))).cuda() for lay in lays]
+        pv = None if prev is None else [torch.from_numpy(prev[s].astype(np.int32)).cuda()] * world
+        out = sh.sample_vocab_sharded_emulated(states, shards, pv)
+        got = [o.cpu().numpy().astype(np.uint32) for o in out]
+        for g in range(1, world):
+            assert np.array_equal(got[g], got[0])
+        toks.append(got[0])
+        for st in states:
+            assert st.smp.last_status() == 0
+    xr = np.stack([orc.prologue(x[s], 30.0, 2.0) for s in range(2)]) if extras else x
+    ref = run_oracle(orc, c, xr, w.seeds(rows), prev)
+    assert np.array_equal(np.array(toks), ref[0])
+    for st in states:
+        assert np.array_equal(st.smp.rng_state, ref[1][-1])
+        st.smp.close()
