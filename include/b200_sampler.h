@@ -20,6 +20,8 @@
  *                           (src/engine.zig:341-354, src/main.zig:653-666), from
  *                           ModelConfig.final_logit_softcapping / logit_scale (src/model.zig:34-35)
  *   bs_get/set_rng_state <- the DefaultPrng field    src/sampler.zig:17
+ *   bs_seed_state        <- its initialisation in Sampler.init, host only
+ *                           src/sampler.zig:22
  *   bs_destroy           <- (Zig: the Sampler goes out of scope)
  *   bs_status            <- error.OutOfMemory        src/sampler.zig:26 (!TokenID)
  *
@@ -36,7 +38,11 @@
  * Rows the sampler could not finish: such a row's token comes back as
  * 0xFFFFFFFF and its RNG state is left as it was (no draw).  With a handle,
  * bs_last_device_status reports why; the condition is per call, so the next
- * call starts clean.
+ * call starts clean.  The causes are a bounded device wait that gave up
+ * (BS_ETIMEOUT) and, for the vocabulary-sharded draw only, a shard whose
+ * candidates overflowed (BS_EINTERNAL).  A row whose candidate set or
+ * typical-p band fails its cover check is not among them: it is sorted again
+ * over the whole vocabulary on the device (slower, same result).
  *
  * Repetition penalty: the last min(n_prev, repetition_window) previous ids of
  * each row are penalised once each, for windows of any length (sampler.zig:
@@ -125,7 +131,7 @@ bs_status bs_argmax_ex(const float *d_logits, size_t ld, uint32_t rows, uint32_t
  * read, not rewritten.  (0, 1) turns it off. */
 bs_status bs_set_logit_prologue(bs_sampler *s, float final_logit_softcapping, float logit_scale);
 
-/* Vocabulary sharding for a tensor-parallel LM head (BASELINE config 4):
+/* Vocabulary sharding for a tensor-parallel LM head:
  * rank g of `world` holds columns [col0, col0 + vocab) of every row, the
  * handle created with the shard width as its vocab and the same seeds on
  * every rank.  Replaces the reference's LM head -> host logits -> sample
@@ -160,6 +166,14 @@ bs_status bs_vshard_draw(bs_sampler *s, const bs_vshard_cand *d_cand_all, const 
 /* Per-row xoshiro256++ state, batch x 4 u64 (host memory).  Synchronous. */
 bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state);
 bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state);
+
+/* The xoshiro256++ state that Sampler.init gives a seed (replaces the prng
+ * field's initialisation at src/sampler.zig:19-23: DefaultPrng.init(seed, or
+ * 0xDEADBEEF when seed is 0), i.e. four SplitMix64 outputs).  Host only: it
+ * touches no device and allocates nothing, so a Sampler can be initialised
+ * before any device exists and hand the state over with bs_set_rng_state
+ * when it first samples. */
+bs_status bs_seed_state(uint64_t seed, uint64_t *h_state4);
 
 /* Status of the last bs_sample on this handle after the stream reached it:
  * BS_OK, or the first device-side error (e.g. BS_EINTERNAL).  Synchronous. */

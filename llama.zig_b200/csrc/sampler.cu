@@ -770,6 +770,10 @@ __device__ __forceinline__ bool seg_bulk_ok(const float *xs, uint32_t n) {
 __device__ __forceinline__ bool seg_issue(const float *xs, uint32_t n, float4 *sbuf, uint64_t *bar, uint64_t pol) {
     const bool bulk = seg_bulk_ok(xs, n);
     if (bulk && threadIdx.x == 0) {
+        // a persistent CTA's earlier task wrote this buffer with ordinary
+        // stores (seen by this thread after the task's closing barrier):
+        // order them before the copy's asynchronous-proxy writes
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_init(bar, 1);
         bulk_load(sbuf, xs, n * 4u, bar, pol);
     }
@@ -857,8 +861,7 @@ __device__ __forceinline__ float4 tile_quad(const K12Params &P, const float *x, 
 // top-k floor, the tail-element histogram.  No cross-CTA step: the row
 // reduction is k1_rows.
 // Shared memory of one statistics task (segment `seg` of row `row`).
-struct __align__(128) StatsSmem {
-    float4 sbuf[SEG_ELEMS / 4];          // the segment's logits
+struct __align__(16) StatsSmem {
     uint32_t mh[KH_BINS];                // tail element counts per bin
     float th[KH_BINS];                   // typical band: mass per bin
     float wm[K12_THREADS / 32];
@@ -866,8 +869,12 @@ struct __align__(128) StatsSmem {
     double wd[K12_THREADS / 32], wd2[K12_THREADS / 32];
 };
 
-__device__ __forceinline__ void stats_task(const K12Params &P, uint32_t seg, uint32_t row, StatsSmem &ss_,
-                                           uint64_t *barp) {
+// `sbuf` (SEG_ELEMS floats of shared memory, 16-byte aligned) receives the
+// segment; returns whether it was staged there, with the prologue and the
+// penalty applied (block-uniform), so that a main task of the same segment
+// on the same CTA can run from it.
+__device__ __forceinline__ bool stats_task(const K12Params &P, uint32_t seg, uint32_t row, StatsSmem &ss_,
+                                           float4 *const sbuf, uint64_t *barp) {
     const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
@@ -875,7 +882,6 @@ __device__ __forceinline__ void stats_task(const K12Params &P, uint32_t seg, uin
     const float c2 = P.c2;
     const uint32_t ntile = min((uint32_t)SEG_TILES, P.ntiles_total - seg * SEG_TILES);
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
-    float4 *const sbuf = ss_.sbuf;
     uint64_t &bar = *barp;
     uint32_t *const mh = ss_.mh;
     float *const th = ss_.th;
@@ -1008,13 +1014,15 @@ __device__ __forceinline__ void stats_task(const K12Params &P, uint32_t seg, uin
             P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = (float)mh[b] * exp2f(-0.25f * (float)b);
     if (t_band)
         for (uint32_t b = tid; b < KH_BINS; b += K12_THREADS) P.mhist[((size_t)hrow * MAX_SEG + seg) * KH_BINS + b] = th[b];
+    return staged;
 }
 
 __global__ void __launch_bounds__(K12_THREADS, 5) k1_stats(K12Params P) {
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ StatsSmem sm;
     __shared__ __align__(8) uint64_t bar;
     grid_dep_launch();
-    stats_task(P, blockIdx.x, blockIdx.y, sm, &bar);
+    stats_task(P, blockIdx.x, blockIdx.y, sm, sbuf, &bar);
 }
 
 // Row reduction, one CTA per row: the row maximum M, the raw prefix estimate
@@ -1350,8 +1358,7 @@ enum : int { TERM_P = 0, TERM_H = 1 };
 
 // Shared memory of one main-pass task (segment `seg` of row `row`).
 constexpr uint32_t RC_CAP = 512;   // uncertified terms recounted one per thread (entropy pass)
-struct __align__(128) MainSmem {
-    float4 sbuf[SEG_ELEMS / 4];         // the segment's logits; later the item phase's arrays
+struct __align__(16) MainSmem {
     TileRec rec[SEG_TILES];
     double wtmp_d[K12_THREADS / 32 + 1];
     double hbase;
@@ -1380,9 +1387,12 @@ __device__ __forceinline__ RowInfo ld_rowinfo(const RowInfo *p) {
     return r;
 }
 
+// `sbuf` (SEG_ELEMS floats of shared memory, 16-byte aligned) holds the
+// segment's logits, later the item phase's arrays.  `pre`: the statistics
+// task of this segment left it staged there, prologue and penalty applied.
 template <int TERM>
 __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint32_t row, MainSmem &ms_,
-                                          uint64_t *barp) {
+                                          float4 *const sbuf, uint64_t *barp, bool pre = false) {
     const uint32_t hrow = P.row0 + row;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = K12_THREADS / 32;
@@ -1398,7 +1408,6 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     uint32_t *const wtmp_u = ms_.wtmp_u;
     SegComp *const wtmp_s = ms_.wtmp_s;
     TileRec *const rec = ms_.rec;
-    float4 *const sbuf = ms_.sbuf;
     uint64_t &bar = *barp;
     // the item phase's arrays reuse the segment copy, which is dead by then
     // (6 KB less shared memory per CTA: five CTAs fit an SM instead of four)
@@ -1420,7 +1429,7 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     const uint32_t nseg_el = min((uint32_t)SEG_ELEMS, P.vocab - seg * SEG_ELEMS);
     const uint32_t *bm = penalty_active(P) ? P.pen_bm + (size_t)hrow * P.ntiles_total : nullptr;
     bool bulk = false;
-    if (TERM == TERM_P) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
+    if (TERM == TERM_P && !pre) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
     // the tile statistics come from the statistics pass, complete before this
     // grid could start (the row reduction lets it launch only after its own
     // wait): load them before waiting for the row reduction
@@ -1528,11 +1537,11 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     const bool t_nan = T != T, t_inf = isinf(T);
     const bool check_nan = ri.check_nan != 0;
     Candidate *cand = P.cand + (size_t)hrow * P.cand_stride;
-    const bool staged = bulk && seg_wait(P, &bar);
+    const bool staged = pre || (bulk && seg_wait(P, &bar));
     // the prologue and the penalty on this thread's own staged tile; other
     // threads read it only after the barriers below
-    if (staged && P.pro && live) prologue_tile_smem(P, tid, reinterpret_cast<float *>(sbuf));
-    if (staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
+    if (!pre && staged && P.pro && live) prologue_tile_smem(P, tid, reinterpret_cast<float *>(sbuf));
+    if (!pre && staged && bm && live) patch_tile_smem(P, hrow, seg, tid, reinterpret_cast<float *>(sbuf));
     const uint32_t tt = live ? (uint32_t)tid : 0u;
     auto quad = [&](int j) { return tile_quad(P, x, seg, tt, j, sbuf, staged, bm, pol); };
     const uint32_t g0 = seg * SEG_ELEMS + (uint32_t)tid * TILE;
@@ -2000,13 +2009,14 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
 
 template <int TERM>
 __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ MainSmem ms;
     __shared__ __align__(8) uint64_t bar;
     // segment-major order over a 1-D grid: every row's segment 0 first (the
     // row start holds most exact-pass tiles, so those CTAs live several times
     // longer), the last segments last, so the kernel's tail is short CTAs
     const uint32_t seg = blockIdx.x / P.rows, row = blockIdx.x - seg * P.rows;
-    main_task<TERM>(P, seg, row, ms, &bar);
+    main_task<TERM>(P, seg, row, ms, sbuf, &bar);
 }
 
 // ---------------------------------------------------------------------------
@@ -2028,7 +2038,7 @@ __global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
 enum : uint32_t { TK_STATS = 0, TK_MAIN = 1, TK_EXIT = 2 };
 constexpr uint64_t FUSED_WAIT_NS = 1000000000ull;   // one second without a task
 
-union __align__(128) FusedSmem {
+union __align__(16) FusedSmem {
     StatsSmem s;
     RowsSmem r;
     MainSmem m;
@@ -2045,6 +2055,7 @@ __device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned l
 
 constexpr int FUSED_CTAS_PER_SM = 4;
 __global__ void __launch_bounds__(K12_THREADS, FUSED_CTAS_PER_SM) k_fused(K12Params P) {
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ FusedSmem u;
     __shared__ __align__(8) uint64_t bar;
     __shared__ uint32_t t_kind, t_row, t_seg, t_last;
@@ -2106,7 +2117,7 @@ __global__ void __launch_bounds__(K12_THREADS, FUSED_CTAS_PER_SM) k_fused(K12Par
         const uint32_t kind = t_kind, row = t_row, seg = t_seg;
         if (kind == TK_EXIT) break;
         if (kind == TK_STATS) {
-            stats_task(P, seg, row, u.s, &bar);
+            stats_task(P, seg, row, u.s, sbuf, &bar);
             __syncthreads();
             if (threadIdx.x == 0) {
                 __threadfence();   // the task's statistics before its count
@@ -2125,8 +2136,67 @@ __global__ void __launch_bounds__(K12_THREADS, FUSED_CTAS_PER_SM) k_fused(K12Par
             }
         } else {
             __threadfence();   // after thread 0's acquire of the slot: the row's reduction
-            main_task<TERM_P>(P, seg, row, u.m, &bar);
+            main_task<TERM_P>(P, seg, row, u.m, sbuf, &bar);
         }
+        __syncthreads();   // the task's shared memory is free again
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Read-once persistent form of the statistics pass, the row reduction and
+// the normaliser's main pass.  A CTA takes (row, segment) tasks in row-major
+// order from one counter, stages the segment in shared memory and computes
+// its statistics; the CTA that completes a row's statistics runs the row
+// reduction and publishes the row; the others wait for that, and every CTA
+// then runs the main pass on the segment it still holds.  The logits cross
+// HBM once per call instead of twice.
+// Progress: a CTA waits only for its own row, whose other segments are held
+// by running CTAs or taken next (tasks are taken in order), so with at least
+// one row's worth of CTAs running every wait ends; each is bounded anyway
+// (a timeout marks the call failed through the error word).
+constexpr int RES_CTAS_PER_SM = 4;
+__global__ void __launch_bounds__(K12_THREADS, RES_CTAS_PER_SM) k_resident(K12Params P) {
+    __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
+    __shared__ FusedSmem u;
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t t_task, t_last;
+    const uint32_t nseg = P.nseg, total = P.rows * P.nseg;
+    uint32_t *const next = P.ctl;
+    uint32_t *const row_done = P.ctl + 4;
+    for (;;) {
+        if (threadIdx.x == 0) t_task = atomicAdd(next, 1u);
+        __syncthreads();
+        const uint32_t t = t_task;
+        if (t >= total) break;
+        const uint32_t row = t / nseg, seg = t - row * nseg;
+        const bool staged = stats_task(P, seg, row, u.s, sbuf, &bar);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();   // the task's statistics before its count
+            t_last = atomicAdd(row_done + row, 1u) + 1u == nseg ? 1u : 0u;
+        }
+        __syncthreads();
+        if (t_last) {
+            __threadfence();   // every statistics task of the row before its reduction
+            rows_task(P, row, u.r);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                st_release_u64(P.ready + row, ((unsigned long long)P.seq << 32) | row);
+            }
+        } else if (threadIdx.x == 0) {
+            const uint64_t t0 = global_ns();
+            for (uint32_t it = 0; (uint32_t)(ld_acquire_u64(P.ready + row) >> 32) != P.seq; it++) {
+                if (global_ns() - t0 > FUSED_WAIT_NS || it > (1u << 24)) {
+                    atomicExch(P.kerr, P.seq);
+                    break;
+                }
+                __nanosleep(256);
+            }
+        }
+        __syncthreads();
+        __threadfence();   // after thread 0's acquire: the row's reduction
+        main_task<TERM_P>(P, seg, row, u.m, sbuf, &bar, staged);
         __syncthreads();   // the task's shared memory is free again
     }
 }
@@ -2171,6 +2241,7 @@ struct KBParams {
     const float *vs_S;
     const RowInfo *rinfo;   // per handle row
     uint32_t tmode;      // TYP_*
+    uint32_t force_full;    // test hook: every row takes the full-vocabulary retry
     uint32_t *out;       // per call row
 };
 
@@ -2467,59 +2538,81 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
     const Candidate *cl = P.cand + (size_t)hrow * P.cand_stride;
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
     unsigned long long *gk1 = gk0 + P.cand_stride;
-    const uint32_t n = min(mode == TYP_SELECTED ? hdr->n_sel : hdr->n_cand, P.cand_stride);
-    const bool big = n > (uint32_t)CAND_SMEM;
+    const uint32_t n_list = min(mode == TYP_SELECTED ? hdr->n_sel : hdr->n_cand, P.cand_stride);
     uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // radix scratch (big lists keep P in global memory)
-    __shared__ uint32_t n_keep_sh, status_sh, nk_pow_sh;
+    __shared__ uint32_t n_keep_sh, status_sh, nk_pow_sh, retry_sh;
 
-    // 1. keys (dev, index), ascending
-    uint32_t npow = 1;
-    while (npow < n) npow <<= 1;
-    unsigned long long *keys = big ? gk0 : skeys;
-    for (uint32_t i = tid; i < (big ? n : npow); i += KB_THREADS) {
-        unsigned long long k = ~0ull;
-        if (i < n) {
-            const Candidate c = cl[i];
-            const float Pi = mode == TYP_SELECTED ? c.v : __fdiv_rn(prob_unnorm(c.v, M, P.T), S);
-            const float sur = Pi > 0.0f ? -log_ref(Pi) : __int_as_float(0x7f800000);
-            const float dev = fabsf(__fsub_rn(sur, H));
-            k = ((unsigned long long)__float_as_uint(dev) << 32) | c.idx;
+    // A band that cannot be shown to cover the kept set (or every band, with
+    // the test hook) is replaced by the whole vocabulary: the reference's
+    // full dev sort, by the whole CTA in global memory.
+    uint32_t n = n_list;
+    bool big = false;
+    unsigned long long *keys = skeys;
+    float *pd = sprobs;
+    bool went_full = false;
+    for (bool full = false;; full = true) {
+        went_full = full;
+        n = full ? P.vocab : n_list;
+        big = full || n > (uint32_t)CAND_SMEM;
+        // 1. keys (dev, index), ascending
+        uint32_t npow = 1;
+        while (npow < n) npow <<= 1;
+        keys = big ? gk0 : skeys;
+        for (uint32_t i = tid; i < (big ? n : npow); i += KB_THREADS) {
+            unsigned long long k = ~0ull;
+            if (i < n) {
+                float Pi;
+                uint32_t id = i;
+                if (full) {
+                    Pi = __fdiv_rn(exact_p_at(P, row, hrow, i, M), S);
+                } else {
+                    const Candidate c = cl[i];
+                    Pi = mode == TYP_SELECTED ? c.v : __fdiv_rn(prob_unnorm(c.v, M, P.T), S);
+                    id = c.idx;
+                }
+                const float sur = Pi > 0.0f ? -log_ref(Pi) : __int_as_float(0x7f800000);
+                const float dev = fabsf(__fsub_rn(sur, H));
+                k = ((unsigned long long)__float_as_uint(dev) << 32) | id;
+            }
+            keys[i] = k;
         }
-        keys[i] = k;
-    }
-    __syncthreads();
-    if (big) {
-        keys = cta_radix_sort(gk0, gk1, n, cnt, red2);
-    } else {
-        block_bitonic(keys, npow);
-    }
-    // 2. P in dev order, recomputed from the logits as the normaliser pass did
-    float *pd = big ? reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0) : sprobs;
-    for (uint32_t i = tid; i < n; i += KB_THREADS)
-        pd[i] = __fdiv_rn(exact_p_at(P, row, hrow, (uint32_t)keys[i], M), S);
-    __syncthreads();
-    // 3. cum_typ (sequential f32 in dev order)
-    if (tid == 0) {
-        uint32_t nk = n, st = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
-        float cum = 0.0f;
-        nk = seq_first_exceed([&](uint32_t i) { return pd[i]; }, n, P.typical_p, cum);
-        const bool crossed = nk < n;
-        if (mode == TYP_BAND && st == ROW_OK) {
-            // the band held every token with approximate dev <= dband, where
-            // the approximation used H_raw: tokens with exact dev up to
-            // dband - |H_raw - H| - (surprise error) are surely in it
-            const float dcross = crossed ? __uint_as_float((uint32_t)(keys[nk] >> 32)) : __int_as_float(0x7f800000);
-            const float herr = fabsf((float)ri.H_raw - H);
-            const float safe = ri.dband - herr - (1e-4f * (fabsf(H) + dcross) + 1e-4f);
-            if (!crossed || !(dcross <= safe)) st = ROW_ENOTSUP;
+        __syncthreads();
+        if (big) {
+            keys = cta_radix_sort(gk0, gk1, n, cnt, red2);
+        } else {
+            block_bitonic(keys, npow);
         }
-        uint32_t np2 = 1;
-        while (np2 < nk) np2 <<= 1;
-        n_keep_sh = nk;
-        status_sh = st;
-        nk_pow_sh = np2;
+        // 2. P in dev order, recomputed from the logits as the normaliser pass did
+        pd = big ? reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0) : sprobs;
+        for (uint32_t i = tid; i < n; i += KB_THREADS)
+            pd[i] = __fdiv_rn(exact_p_at(P, row, hrow, (uint32_t)keys[i], M), S);
+        __syncthreads();
+        // 3. cum_typ (sequential f32 in dev order)
+        if (tid == 0) {
+            uint32_t nk = n, st = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+            float cum = 0.0f;
+            nk = seq_first_exceed([&](uint32_t i) { return pd[i]; }, n, P.typical_p, cum);
+            const bool crossed = nk < n;
+            bool retry = false;
+            if (mode == TYP_BAND && st == ROW_OK && !full) {
+                // the band held every token with approximate dev <= dband, where
+                // the approximation used H_raw: tokens with exact dev up to
+                // dband - |H_raw - H| - (surprise error) are surely in it
+                const float dcross = crossed ? __uint_as_float((uint32_t)(keys[nk] >> 32)) : __int_as_float(0x7f800000);
+                const float herr = fabsf((float)ri.H_raw - H);
+                const float safe = ri.dband - herr - (1e-4f * (fabsf(H) + dcross) + 1e-4f);
+                retry = !crossed || !(dcross <= safe) || P.force_full;
+            }
+            uint32_t np2 = 1;
+            while (np2 < nk) np2 <<= 1;
+            n_keep_sh = nk;
+            status_sh = st;
+            nk_pow_sh = np2;
+            retry_sh = retry ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!retry_sh) break;
     }
-    __syncthreads();
     const uint32_t nk = n_keep_sh, nkp = nk_pow_sh;
     // 4. the kept tokens by (P descending, index ascending): each thread
     // rewrites its own entries in place
@@ -2560,7 +2653,7 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
     tr.u = u;
     tr.n_kept = nk;
     tr.path = path;
-    tr.flags = hdr->flags | (status == ROW_ENOTSUP ? RF_TYP_BAND : 0u);
+    tr.flags = hdr->flags | (big ? RF_CAND_BIG : 0u) | (went_full ? RF_FULL : 0u);
     tr.n_cand = n;
     tr.status = status;
     tr.n_items = 0;
@@ -2609,15 +2702,17 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     const uint32_t spec = ITEM_SMEM / nseg;
     const Item *ib = P.items + (size_t)hrow * P.ntiles_total;
     static_assert(sizeof(Item) == 32, "an item is two 16-byte chunks");
-    for (uint32_t i = tid; i < 2 * nseg * spec; i += KB_THREADS) {
+    const bool walks = P.vs_mode != VS_DRAW;   // (a shard draw takes S from the chain)
+    for (uint32_t i = tid; walks && i < 2 * nseg * spec; i += KB_THREADS) {
         const uint32_t it = i >> 1, sg = it / spec, j = it - sg * spec;
         if (sg * SEG_TILES + j < P.ntiles_total && j < (uint32_t)SEG_TILES)
             cp_async16(reinterpret_cast<uint4 *>(sall) + i, reinterpret_cast<const uint4 *>(ib + sg * SEG_TILES + j) + (i & 1u));
     }
     // the stored exact terms (rows of WC_CAP * TILE floats, 16-byte aligned)
     const float *wcg = P.wcdata + (size_t)hrow * WC_CAP * TILE;
-    for (uint32_t i = tid; i < n_wc * (TILE / 4); i += KB_THREADS) cp_async16(wcs + 4 * i, wcg + 4 * i);
-    if ((uint32_t)tid < nseg) s_nit[tid] = min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES));
+    for (uint32_t i = tid; walks && i < n_wc * (TILE / 4); i += KB_THREADS) cp_async16(wcs + 4 * i, wcg + 4 * i);
+    if ((uint32_t)tid < nseg)
+        s_nit[tid] = walks ? min(hdr->seg_items[tid], min((uint32_t)SEG_TILES, P.ntiles_total - tid * SEG_TILES)) : 0u;
     cp_async_wait_all();
     const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
@@ -2862,31 +2957,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         return;
     }
 
-    // large candidate sets: keys, then a stable radix sort in global memory
-    // (whole CTA)
-    unsigned long long *keys = skeys;
-    float *probs = sprobs;
-    if (big) {
-        uint32_t nz = 0;
-        for (uint32_t i = tid; i < n_cand; i += KB_THREADS) {
-            const Candidate c = cg_[i];
-            const float p = prob_unnorm(c.v, M, P.T);
-            gk0[i] = cand_key(c.idx, p);
-            nz += p > 0.0f ? 0u : 1u;
-        }
-        if (nz) atomicAdd(&n_zero, nz);
-        __syncthreads();
-        uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // 16 * KB_THREADS words
-        keys = cta_radix_sort(gk0, gk1, n_cand, cnt, red2);
-        probs = reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0);
-        __syncthreads();
-    }
-
-    const uint32_t n_pos = n_cand - n_zero;   // p = 0 candidates sort last and never matter
     const float S = S_sh;
     // a NaN anywhere in the row makes the sum NaN (for shards: the chain's S)
     const bool nan_row = P.vs_mode == VS_DRAW ? (S != S) : (flags0 & RF_NAN) != 0;
-    __shared__ uint32_t rawarg_sh;
+    __shared__ uint32_t rawarg_sh, retry_sh;
     __shared__ ArgBest rbest[KB_THREADS / 32];
     if (!nan_row && !(S > 0.0f) && P.vs_mode != VS_DRAW) {
         // sum <= 0 (sampler.zig:89): sampleArgmax of the raw logits.  Not
@@ -2909,22 +2983,121 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         }
         __syncthreads();
     }
-    // exact probs in sorted order (sampler.zig:90)
-    for (uint32_t i = tid; i < n_pos; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
-    __syncthreads();
-    // distinct p can round to equal probs; the stable sort then wants index
-    // order among them.  Rare: the block checks adjacent pairs first
-    bool tie_fix = false;
-    {
-        const uint32_t *ix = reinterpret_cast<const uint32_t *>(keys);
-        bool mine = false;
-        for (uint32_t i = tid + 1; i < n_pos; i += KB_THREADS)
-            mine |= probs[i] == probs[i - 1] && ix[2 * (i - 1)] > ix[2 * i];
-        tie_fix = __syncthreads_or(mine) != 0;
+
+    // thread 0's state, kept across the retry below
+    uint32_t status = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
+    uint32_t flags = flags0 | walk_flags | (big ? RF_CAND_BIG : 0u);
+    uint32_t n_sel = 0;
+    bool cover_ok = false;
+    float *cums = nullptr;
+    uint32_t *idxs = nullptr;   // idxs[2*i] aliases the low word of keys[i]
+
+    // The candidates are sorted by (p descending, index ascending), the
+    // filters run over them, and the kept prefix is checked to lie inside
+    // them.  A row whose check fails (or every row, with the test hook) goes
+    // round once more with every token of the vocabulary as a candidate: the
+    // reference's full sort, by the whole CTA in global memory.  Not for a
+    // shard's draw, whose logits are spread over the shards.
+    unsigned long long *keys = skeys;
+    float *probs = sprobs;
+    uint32_t n_pos = 0, nc = n_cand;
+    for (bool full = false;; full = true) {
+        nc = full ? P.vocab : n_cand;
+        if (big || full) {
+            // keys, then a stable radix sort in global memory (whole CTA)
+            uint32_t nz = 0;
+            for (uint32_t i = tid; i < nc; i += KB_THREADS) {
+                float p;
+                uint32_t id = i;
+                if (full) {
+                    p = exact_p_at(P, row, hrow, i, M);
+                } else {
+                    const Candidate c = cg_[i];
+                    p = prob_unnorm(c.v, M, P.T);
+                    id = c.idx;
+                }
+                gk0[i] = cand_key(id, p);
+                nz += p > 0.0f ? 0u : 1u;
+            }
+            if (nz) atomicAdd(&n_zero, nz);
+            __syncthreads();
+            uint32_t *cnt = reinterpret_cast<uint32_t *>(sprobs);   // 16 * KB_THREADS words
+            keys = cta_radix_sort(gk0, gk1, nc, cnt, red2);
+            probs = reinterpret_cast<float *>(keys == gk0 ? gk1 : gk0);
+            __syncthreads();
+        }
+        n_pos = nc - n_zero;   // p = 0 candidates sort last and never matter
+        // exact probs in sorted order (sampler.zig:90)
+        for (uint32_t i = tid; i < n_pos; i += KB_THREADS) probs[i] = __fdiv_rn(key_p(keys[i]), S);
+        __syncthreads();
+        // distinct p can round to equal probs; the stable sort then wants index
+        // order among them.  Rare: the block checks adjacent pairs first
+        bool tie_fix = false;
+        {
+            const uint32_t *ix = reinterpret_cast<const uint32_t *>(keys);
+            bool mine = false;
+            for (uint32_t i = tid + 1; i < n_pos; i += KB_THREADS)
+                mine |= probs[i] == probs[i - 1] && ix[2 * (i - 1)] > ix[2 * i];
+            tie_fix = __syncthreads_or(mine) != 0;
+        }
+        if (tid == 0) {
+            bool retry = false;
+            if (!nan_row && S > 0.0f) {
+                idxs = reinterpret_cast<uint32_t *>(keys);
+                // ties: equal probs from distinct p keep index order (stable sort)
+                for (uint32_t i = 1; tie_fix && i < n_pos; i++) {
+                    if (probs[i] == probs[i - 1] && idxs[2 * (i - 1)] > idxs[2 * i]) {
+                        uint32_t j = i;
+                        const uint32_t id = idxs[2 * j];
+                        const float pr = probs[j];
+                        while (j > 0 && probs[j - 1] == pr && idxs[2 * (j - 1)] > id) {
+                            idxs[2 * j] = idxs[2 * (j - 1)];
+                            j--;
+                        }
+                        idxs[2 * j] = id;
+                    }
+                }
+                // The candidates are every token above a floor, i.e. a prefix of
+                // the reference's sorted order.  The kept prefix is settled inside
+                // it when some filter cuts before its end, when the candidates are
+                // all tokens with p > 0, or when the floor is the binding filter's
+                // own bound.
+                n_sel = n_pos;
+                const uint32_t binding = hdr->binding;
+                const bool k_act = P.top_k > 0 && P.top_k < P.vocab;
+                // top-k (sampler.zig:106-109)
+                if (k_act && n_sel > P.top_k) n_sel = P.top_k;
+                // top-p (sampler.zig:111-118): the crossing token is deselected
+                // too.  Its running sums are kept (in the stored terms' area, free
+                // after the walk): the kept mass below is the same sum over a prefix
+                cums = nullptr;
+                if (P.top_p > 0.0f && P.top_p < 1.0f) {
+                    float cum = 0.0f;
+                    if (n_sel <= (uint32_t)(WC_CAP * TILE)) cums = wcs;
+                    n_sel = seq_first_exceed([&](uint32_t j) { return probs[j]; }, n_sel, P.top_p, cum, cums);
+                }
+                // min-p (sampler.zig:120-126) against probs[indices[0]]
+                if (P.min_p > 0.0f && n_pos > 0) {
+                    const float thr = __fmul_rn(probs[0], P.min_p);
+                    uint32_t j = 0;
+                    while (j < n_sel && !(probs[j] < thr)) j++;
+                    n_sel = j;
+                }
+                cover_ok = full || ((binding == 0 || binding == 1 || binding == 3 || binding == 4 ||
+                                     n_sel < n_pos || (k_act && P.top_k <= n_pos)) &&
+                                    !(flags0 & RF_CAND_SHORT));   // (a shard's candidates overflowed)
+                if (status == ROW_OK && !full && P.vs_mode != VS_DRAW && (!cover_ok || P.force_full))
+                    retry = true;
+            }
+            if (full) flags |= RF_FULL | RF_CAND_BIG;
+            n_zero = 0;
+            retry_sh = retry ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!retry_sh) break;
     }
     if (tid != 0) return;
 
-    uint32_t status = *P.kerr == P.seq ? (uint32_t)ROW_ETIMEOUT : (uint32_t)ROW_OK;
     bool pending = false;
     uint32_t token = 0;
     uint32_t path = 0;
@@ -2933,7 +3106,6 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     uint64_t s4[4];
     uint64_t *rng = P.rng + (size_t)hrow * 4;
     s4[0] = rng[0]; s4[1] = rng[1]; s4[2] = rng[2]; s4[3] = rng[3];
-    uint32_t flags = flags0 | walk_flags | (big ? RF_CAND_BIG : 0u);
     float S_rep = S;
 
     if (nan_row) {
@@ -2950,53 +3122,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         path = 1;
         if (P.vs_mode == VS_DRAW) status = ROW_EINTERNAL;   // the raw logits are spread over the shards
     } else {
-        // idxs[2*i] aliases the low word of keys[i]
-        uint32_t *idxs = reinterpret_cast<uint32_t *>(keys);
-        // ties: equal probs from distinct p keep index order (stable sort)
-        for (uint32_t i = 1; tie_fix && i < n_pos; i++) {
-            if (probs[i] == probs[i - 1] && idxs[2 * (i - 1)] > idxs[2 * i]) {
-                uint32_t j = i;
-                const uint32_t id = idxs[2 * j];
-                const float pr = probs[j];
-                while (j > 0 && probs[j - 1] == pr && idxs[2 * (j - 1)] > id) {
-                    idxs[2 * j] = idxs[2 * (j - 1)];
-                    j--;
-                }
-                idxs[2 * j] = id;
-            }
-        }
-        // The candidates are every token above a floor, i.e. a prefix of the
-        // reference's sorted order.  The kept prefix is settled inside it when
-        // some filter cuts before its end, when the candidates are all tokens
-        // with p > 0, or when the floor is the binding filter's own bound.
-        uint32_t n_sel = n_pos;
-        const uint32_t binding = hdr->binding;
-        const bool k_act = P.top_k > 0 && P.top_k < P.vocab;
-        // top-k (sampler.zig:106-109)
-        if (k_act && n_sel > P.top_k) n_sel = P.top_k;
-        // top-p (sampler.zig:111-118): the crossing token is deselected too.
-        // Its running sums are kept (in the stored terms' area, free after
-        // the walk): the kept mass below is the same sum over a prefix
-        float *cums = nullptr;
-        if (P.top_p > 0.0f && P.top_p < 1.0f) {
-            float cum = 0.0f;
-            if (n_sel <= (uint32_t)(WC_CAP * TILE)) cums = wcs;
-            n_sel = seq_first_exceed([&](uint32_t j) { return probs[j]; }, n_sel, P.top_p, cum, cums);
-        }
-        // min-p (sampler.zig:120-126) against probs[indices[0]]
-        if (P.min_p > 0.0f && n_pos > 0) {
-            const float thr = __fmul_rn(probs[0], P.min_p);
-            uint32_t j = 0;
-            while (j < n_sel && !(probs[j] < thr)) j++;
-            n_sel = j;
-        }
-        const bool cover_ok = (binding == 0 || binding == 1 || binding == 3 || binding == 4 || n_sel < n_pos ||
-                               (k_act && P.top_k <= n_pos)) &&
-                              !(flags0 & RF_CAND_SHORT);   // (a shard's candidates overflowed)
         if (status != ROW_OK) {
             // a bounded device wait gave up: nothing of this call is trusted
         } else if (!cover_ok) {
-            status = ROW_EINTERNAL;
+            status = ROW_EINTERNAL;   // (only a shard's draw: other rows took the retry)
             flags |= RF_CAND_SHORT;
         } else if (P.tmode != TYP_OFF) {
             // typical-p follows in the entropy passes (sampler.zig:128-154):
@@ -3007,6 +3136,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
                 for (uint32_t j = 0; j < n_sel; j++) cw[j] = Candidate{idxs[2 * j], probs[j]};
             hdr->n_sel = P.tmode == TYP_SELECTED ? n_sel : 0u;
             hdr->top_idx = n_pos > 0 ? idxs[0] : 0u;
+            hdr->flags = flags0 | (flags & RF_FULL);   // (the typical tail's trace reports it)
         } else {
             // kept mass in sorted order (sampler.zig:156-159): the same adds
             // from 0 as top-p's running sum, so its value at the last kept
@@ -3048,7 +3178,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     tr.n_kept = n_kept;
     tr.path = path;
     tr.flags = flags;
-    tr.n_cand = n_cand;
+    tr.n_cand = nc;
     tr.status = status;
     tr.n_items = walk_items;
     tr.n_wc = hdr->n_wc;
@@ -3172,6 +3302,7 @@ struct bs_sampler {
     uint32_t *d_kerr;        // sequence number of the last call whose bounded device wait gave up
     uint32_t seq;            // sequence number of the last call (0 before the first)
     uint32_t fused;          // 1: the persistent kernel instead of separate statistics / row / main kernels
+    uint32_t force_full;     // test hook: every row takes the full-vocabulary retry
     Prologue pro;            // the logit prologue set by bs_set_logit_prologue (pro.pro == 0: none)
     // the vocabulary-shard call in progress (bs_vshard_stats sets it up)
     K12Params vs_A;
@@ -3272,20 +3403,23 @@ static cudaError_t ensure_kernel_attrs(int dev) {
     return e;
 }
 
-// Resident CTAs of the persistent kernel on a device (all of them run at once).
-static int g_fused_ctas[MAX_DEVICES];
-static cudaError_t fused_grid(int dev, int *ctas) {
-    if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+// Resident CTAs of a persistent kernel on a device (all of them run at once):
+// kind 1 the task-queue kernel k_fused, kind 2 the read-once kernel k_resident.
+static int g_fused_ctas[MAX_DEVICES][2];
+static cudaError_t fused_grid(int dev, int *ctas, uint32_t kind = 1) {
+    if (dev < 0 || dev >= MAX_DEVICES || kind < 1 || kind > 2) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_attrs_mu);
-    if (g_fused_ctas[dev] == 0) {
+    int &n = g_fused_ctas[dev][kind - 1];
+    if (n == 0) {
         int per_sm = 0, sms = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused, K12_THREADS, 0);
+        cudaError_t e = kind == 1 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused, K12_THREADS, 0)
+                                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_resident, K12_THREADS, 0);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         if (per_sm <= 0 || sms <= 0) return cudaErrorInvalidConfiguration;
-        g_fused_ctas[dev] = per_sm * sms;
+        n = per_sm * sms;
     }
-    *ctas = g_fused_ctas[dev];
+    *ctas = n;
     return cudaSuccess;
 }
 
@@ -3504,6 +3638,7 @@ static void make_params(const bs_sampler *s, uint32_t seq, const float *d_logits
     B.pinv = s->pro.pinv;
     B.rinfo = s->d_rinfo;
     B.tmode = A.tmode;
+    B.force_full = s->force_full;
     B.out = d_out;
     B.vs_mode = VS_OFF;
     B.vs_entry = nullptr;
@@ -3540,12 +3675,17 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
     // the separate kernels, whose groups the events can split
     if (!ev && s->fused && s->d_fctl) {
         int ctas = 0;
-        cudaError_t e = fused_grid(s->device, &ctas);
+        const uint32_t kind = s->fused == 2 ? 2u : 1u;
+        cudaError_t e = fused_grid(s->device, &ctas, kind);
         const uint32_t tasks = rows * s->nseg;
         if (e == cudaSuccess) e = cudaMemsetAsync(s->d_fctl, 0, (4 + (size_t)rows) * sizeof(uint32_t), st);
         if (e == cudaSuccess && pen)
             k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, 0u, row0, s->ntiles_total, s->d_penbm);
-        if (e == cudaSuccess) k_fused<<<(uint32_t)ctas < tasks ? (uint32_t)ctas : tasks, K12_THREADS, 0, st>>>(A);
+        const uint32_t grid = (uint32_t)ctas < tasks ? (uint32_t)ctas : tasks;
+        if (e == cudaSuccess) {
+            if (kind == 2) k_resident<<<grid, K12_THREADS, 0, st>>>(A);
+            else k_fused<<<grid, K12_THREADS, 0, st>>>(A);
+        }
         const dim3 g2(s->nseg * rows);
         if (A.tmode != TYP_OFF) {
             if (e == cudaSuccess) {
@@ -3724,16 +3864,28 @@ extern "C" bs_status bs_sample_host(bs_sampler *s, const float *h_logits, size_t
     return BS_OK;
 }
 
-// Test and tuning hooks: 1 selects the persistent kernel instead of the
-// separate kernels (same results); the persistent kernel's grid on a device.
+// Test and tuning hooks: 1 selects the task-queue persistent kernel, 2 the
+// read-once persistent kernel, 0 the separate kernels (same results); the
+// persistent kernels' grids on a device.
 extern "C" bs_status bs_debug_set_fused(bs_sampler *s, uint32_t fused) {
     if (!s) return BS_EINVAL;
     s->fused = fused;
     return BS_OK;
 }
+// Test hook: 1 sends every row through the full-vocabulary retry (the path
+// of rows whose candidates or typical-p band fail their cover check).
+extern "C" bs_status bs_debug_set_force_full(bs_sampler *s, uint32_t on) {
+    if (!s) return BS_EINVAL;
+    s->force_full = on;
+    return BS_OK;
+}
 extern "C" int bs_debug_fused_ctas(int device) {
     int ctas = 0;
     return fused_grid(device, &ctas) == cudaSuccess ? ctas : -1;
+}
+extern "C" int bs_debug_resident_ctas(int device) {
+    int ctas = 0;
+    return fused_grid(device, &ctas, 2u) == cudaSuccess ? ctas : -1;
 }
 
 extern "C" bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state) {
@@ -3749,6 +3901,12 @@ extern "C" bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state) {
     BS_CUDA(cudaSetDevice(s->device));
     BS_CUDA(cudaDeviceSynchronize());
     BS_CUDA(cudaMemcpy(s->d_rng, h_state, (size_t)s->batch * 4 * sizeof(uint64_t), cudaMemcpyHostToDevice));
+    return BS_OK;
+}
+
+extern "C" bs_status bs_seed_state(uint64_t seed, uint64_t *h_state4) {
+    if (!h_state4) return BS_EINVAL;
+    rng_seed(h_state4, seed != 0 ? seed : 0xDEADBEEFULL);
     return BS_OK;
 }
 

@@ -25,6 +25,7 @@ enum : uint32_t {
     RF_CAND_SHORT = 1u << 2,    // candidate set did not cover the kept prefix
     RF_SLOW_WALK = 1u << 3,     // walker needed the recompute path (diagnostic)
     RF_TYP_BAND = 1u << 4,      // typical-p: the dev band did not cover the kept set
+    RF_FULL = 1u << 5,          // resolved by the retry with every token as a candidate
 };
 
 // Typical-p modes of a row (sampler.zig:128-154).

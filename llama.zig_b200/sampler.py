@@ -34,7 +34,7 @@ EXPORTS = [
     "bs_config_default", "bs_create", "bs_sample", "bs_sample_host", "bs_argmax",
     "bs_get_rng_state", "bs_set_rng_state", "bs_last_device_status", "bs_destroy",
     "bs_status_string", "bs_profile_enable", "bs_profile_read", "bs_argmax_ex", "bs_set_logit_prologue",
-    "bs_sample_static",
+    "bs_sample_static", "bs_seed_state",
 ]
 
 
@@ -127,6 +127,8 @@ def lib() -> ctypes.CDLL:
         for name in ("bs_vshard_stats", "bs_vshard_main", "bs_vshard_walk", "bs_vshard_export", "bs_vshard_draw"):
             getattr(L, name).restype = ctypes.c_int
         L.bs_get_rng_state.argtypes = [vp, u64p]
+        L.bs_seed_state.argtypes = [ctypes.c_uint64, u64p]
+        L.bs_seed_state.restype = ctypes.c_int
         L.bs_set_rng_state.argtypes = [vp, u64p]
         L.bs_last_device_status.argtypes = [vp]
         L.bs_destroy.argtypes = [vp]
@@ -164,6 +166,15 @@ def _stream_ptr(stream) -> int:
     return int(getattr(stream, "cuda_stream", stream))
 
 
+def seed_state(seed: int) -> np.ndarray:
+    """The xoshiro256++ state Sampler.init gives ``seed`` (sampler.zig:22;
+    0 -> 0xDEADBEEF), computed by the library on the host (bs_seed_state)."""
+    st = np.zeros(4, dtype=np.uint64)
+    _check(lib().bs_seed_state(ctypes.c_uint64(int(seed) & (2**64 - 1)),
+                               st.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))), "bs_seed_state")
+    return st
+
+
 class Sampler:
     """``batch`` independent Zig Samplers on one GPU (Sampler.init, sampler.zig:19-24).
 
@@ -172,20 +183,53 @@ class Sampler:
 
     def __init__(self, cfg: SamplerConfig, batch: int = 1, vocab: int = 0, device: int = 0,
                  seeds=None):
-        if vocab <= 0:
-            raise ValueError("vocab must be positive")
         self.cfg = cfg
         self.batch = int(batch)
         self.vocab = int(vocab)
         self.device = int(device)
         self._h = ctypes.c_void_p()
-        c = cfg.to_c()
+        self._pending_state = None
+        if self.vocab <= 0:
+            # Sampler.init(cfg) exactly (sampler.zig:19-24): no vocabulary yet,
+            # so the state is seeded on the host and the device handle is made
+            # by the first sample, sized by that call's logits
+            if self.batch != 1 or seeds is not None or vocab < 0:
+                raise ValueError("vocab must be positive (only a one-row Sampler binds it lazily)")
+            self._pending_state = seed_state(cfg.seed)[None, :]
+            return
+        self._create(seeds)
+
+    @classmethod
+    def init(cls, cfg: SamplerConfig, device: int = 0) -> "Sampler":
+        """Sampler.init (sampler.zig:19-24): one row, no device work until
+        the first :meth:`sample`, which takes the vocabulary from its logits."""
+        return cls(cfg, batch=1, vocab=0, device=device)
+
+    def _create(self, seeds=None) -> None:
+        c = self.cfg.to_c()
         sp = None
         if seeds is not None:
             self._seeds = np.ascontiguousarray(seeds, dtype=np.uint64)
             sp = self._seeds.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
         _check(lib().bs_create(ctypes.byref(c), self.batch, self.vocab, self.device, sp,
                                ctypes.byref(self._h)), "bs_create")
+        if getattr(self, "_prologue", None) is not None:
+            _check(lib().bs_set_logit_prologue(self._h, *self._prologue), "bs_set_logit_prologue")
+
+    def _bind(self, vocab: int) -> None:
+        """Make (or remake, for another vocabulary) the lazily bound handle,
+        carrying the xoshiro256++ state over."""
+        if self._h and vocab == self.vocab:
+            return
+        if self._pending_state is None:
+            if not self._h:
+                raise ValueError("sampler is closed")
+            self._pending_state = self.rng_state
+            self.close()
+        self.vocab = int(vocab)
+        self._create()
+        self.rng_state = self._pending_state
+        self._pending_state = None
 
     def close(self) -> None:
         if self._h:
@@ -209,12 +253,19 @@ class Sampler:
         ``prev_tokens``: previous token ids for the repetition penalty, rows x
         n_prev (same device kind as ``logits``).
         """
+        lazy = self._pending_state is not None or getattr(self, "_lazy", False)
         if isinstance(logits, np.ndarray) or isinstance(logits, (list, tuple)):
+            if lazy:
+                self._lazy = True
+                self._bind(np.shape(logits)[-1])
             return self._sample_host(logits, prev_tokens, row0)
         import torch
         x = logits
         if x.dim() == 1:
             x = x.unsqueeze(0)
+        if lazy:
+            self._lazy = True
+            self._bind(x.shape[1])
         if x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1:
             raise ValueError("logits must be a CUDA float32 tensor with unit column stride")
         rows = x.shape[0]
@@ -252,6 +303,8 @@ class Sampler:
     # -- PRNG state ------------------------------------------------------------
     @property
     def rng_state(self) -> np.ndarray:
+        if self._pending_state is not None:
+            return self._pending_state.copy()
         st = np.zeros((self.batch, 4), dtype=np.uint64)
         _check(lib().bs_get_rng_state(self._h, st.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))),
                "bs_get_rng_state")
@@ -260,6 +313,9 @@ class Sampler:
     @rng_state.setter
     def rng_state(self, st) -> None:
         a = np.ascontiguousarray(st, dtype=np.uint64).reshape(self.batch, 4)
+        if self._pending_state is not None and not self._h:
+            self._pending_state = a.copy()
+            return
         _check(lib().bs_set_rng_state(self._h, a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))),
                "bs_set_rng_state")
 
@@ -267,7 +323,9 @@ class Sampler:
         """The engine's logit prologue (engine.zig:341-354) for every later
         sample(): soft-cap tanh(v / s) * s when s > 0, then v * (1 / logit_scale)
         unless it is 1 or 0; the model's ModelConfig fields (model.zig:34-35)."""
-        _check(lib().bs_set_logit_prologue(self._h, final_logit_softcapping, logit_scale), "bs_set_logit_prologue")
+        self._prologue = (float(final_logit_softcapping), float(logit_scale))
+        if self._h:
+            _check(lib().bs_set_logit_prologue(self._h, *self._prologue), "bs_set_logit_prologue")
 
     def last_status(self) -> int:
         return lib().bs_last_device_status(self._h)

@@ -291,6 +291,16 @@ class VocabShardedSampler:
         else:
             dist.all_gather_into_tensor(self._parts, part)
         st.main(self._parts, stream)
+        # the candidates are final after the main pass: their all-gather runs
+        # while the chain of walks does
+        cand, count = st.export(stream)
+        works = []
+        if lay.world == 1:
+            self._cand_all[0].copy_(cand)
+            self._count_all[0].copy_(count)
+        else:
+            works.append(dist.all_gather_into_tensor(self._cand_all, cand, async_op=True))
+            works.append(dist.all_gather_into_tensor(self._count_all, count, async_op=True))
         entry = None
         if lay.rank > 0:
             dist.recv(self._entry, src=lay.rank - 1)
@@ -302,13 +312,8 @@ class VocabShardedSampler:
             self._S.copy_(exit_)
         if lay.world > 1:
             dist.broadcast(self._S, src=lay.world - 1)
-        cand, count = st.export(stream)
-        if lay.world == 1:
-            self._cand_all[0].copy_(cand)
-            self._count_all[0].copy_(count)
-        else:
-            dist.all_gather_into_tensor(self._cand_all, cand)
-            dist.all_gather_into_tensor(self._count_all, count)
+        for wk in works:
+            wk.wait()
         return st.draw(self._cand_all, self._count_all, self._S, stream)
 
     def last_status(self) -> int:

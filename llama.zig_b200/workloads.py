@@ -47,7 +47,7 @@ class Workload:
         return (np.arange(offset, offset + n, dtype=np.uint64) + np.uint64(self.seed)).astype(np.uint64)
 
 
-# BASELINE configurations 0-4 plus the headline B=256 cases.
+# The benchmark configurations 0-4 of BASELINE.json plus the headline B=256 cases.
 WORKLOADS = {
     # config 0: the CLI's single-row sampler, top-p only, 1000 sequential steps
     "c0": Workload("c0", 1, 128256, 3.0, 16, 5.0, 15.0, 0.0, 0.8, top_p=0.9, steps=1000),

@@ -56,3 +56,31 @@ def test_invalid_arguments_are_rejected_without_gpu(pkg):
     assert L.bs_create(None, 1, 100, 0, None, ctypes.byref(h)) == 1
     assert L.bs_sample(None, None, 0, 0, 1, None, 0, None, None) == 1
     assert L.bs_argmax(None, 0, 1, 10, None, None) == 1
+
+
+# SplitMix64 (Steele, Lea & Flood) from x = 1234567: the published first
+# outputs of the reference implementation.  Sampler.init's DefaultPrng takes
+# its four state words from these (sampler.zig:22).
+SPLITMIX64_1234567 = [6457827717110365317, 3203168211198807973, 9817491932198370423,
+                      4593380528125082431, 16408922859458223821]
+
+
+def test_seed_state_is_splitmix64_on_the_host(pkg, orc):
+    st = pkg.sampler.seed_state(1234567)
+    assert [int(v) for v in st] == SPLITMIX64_1234567[:4]
+    assert [int(v) for v in orc.rng_seed(1234567)] == SPLITMIX64_1234567[:4]
+    # seed 0 is replaced by 0xDEADBEEF (sampler.zig:22)
+    assert list(pkg.sampler.seed_state(0)) == list(pkg.sampler.seed_state(0xDEADBEEF))
+    for seed in (1, 42, 2**63 + 5, 2**64 - 1):
+        assert list(pkg.sampler.seed_state(seed)) == list(orc.rng_seed(seed))
+    assert pkg.lib().bs_seed_state(0, None) == 1
+
+
+def test_sampler_init_needs_no_device(pkg):
+    # Sampler.init(cfg) (sampler.zig:19-24) takes no vocabulary and does no
+    # device work: the handle is made by the first sample
+    s = pkg.Sampler.init(pkg.SamplerConfig(seed=1234567))
+    assert not s._h and s.vocab == 0
+    assert [int(v) for v in s.rng_state[0]] == SPLITMIX64_1234567[:4]
+    s.rng_state = [[1, 2, 3, 4]]
+    assert [int(v) for v in s.rng_state[0]] == [1, 2, 3, 4]

@@ -196,6 +196,32 @@ def test_host_path_matches_device_path(gpu_pkg, orc):
     assert np.array_equal(s.rng_state, st)
 
 
+def test_sampler_init_binds_lazily_like_the_reference(gpu_pkg, orc):
+    # the drop-in's life cycle: Sampler.init(cfg) with no vocabulary
+    # (sampler.zig:19-24), then sample(allocator, logits, prev) per token
+    # (sampler.zig:26-28, engine.zig:355) with the history growing; a second
+    # vocabulary rebinds the handle and keeps the xoshiro256++ stream
+    cfgd = dict(temperature=0.7, top_k=40, top_p=0.95, min_p=0.05, seed=4242,
+                repetition_window=16, repetition_penalty=1.3)
+    s = gpu_pkg.Sampler.init(gpu_pkg.SamplerConfig(**cfgd))
+    r = orc.Sampler(orc.make_config(**cfgd))
+    rng = np.random.default_rng(11)
+    hist = []
+    for step in range(12):
+        V = 3001 if step < 8 else 5003
+        x = (rng.standard_normal(V) * 3).astype(np.float32)
+        if step % 2:
+            got = s.sample(x, prev_tokens=np.array(hist, dtype=np.uint32) if hist else None)
+        else:
+            pt = torch.tensor(hist, dtype=torch.int32).cuda() if hist else None
+            got = int(s.sample(torch.from_numpy(x).cuda(), prev_tokens=pt).cpu()[0])
+        exp = r.sample(x, np.array(hist, dtype=np.uint32) if hist else None)
+        assert got == exp, step
+        hist.append(got)
+    assert np.array_equal(s.rng_state[0], r.state)
+    s.close()
+
+
 def test_rng_state_roundtrip_and_resync(gpu_pkg, orc):
     w, x = _workload(gpu_pkg, "c1", 4, steps=3)
     c = w.config()
@@ -366,10 +392,14 @@ def test_config0_thousand_sequential_steps(gpu_pkg, orc):
     s.close()
 
 
-@pytest.mark.parametrize("name,rows", [("c1", 64), ("headline_topp", 256), ("c2", 64), ("c3_topk1", 64)])
-def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows):
-    # the persistent-kernel form of the statistics, row reduction and main
-    # pass (one launch, tasks claimed from device counters) against the checker
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("name,rows", [("c1", 64), ("headline_topp", 256), ("c2", 64), ("c3_topk1", 64),
+                                       ("headline", 256), ("c4", 512)])
+def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows, mode):
+    # the persistent-kernel forms of the statistics, row reduction and main
+    # pass (one launch, tasks claimed from device counters) against the
+    # checker: 1 the task queue, 2 the read-once kernel (a CTA keeps its
+    # segment from the statistics to the main pass)
     import ctypes
     L = gpu_pkg.sampler.lib()
     L.bs_debug_set_fused.argtypes = [ctypes.c_void_p, ctypes.c_uint32]
@@ -377,7 +407,7 @@ def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows):
     c = w.config()
     seeds = w.seeds(rows)
     s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=rows, vocab=w.vocab, seeds=seeds)
-    assert L.bs_debug_set_fused(s._h, 1) == 0
+    assert L.bs_debug_set_fused(s._h, mode) == 0
     toks, states = [], []
     for i in range(2):
         toks.append(s.sample(torch.from_numpy(x[i]).cuda()).cpu().numpy().astype(np.uint32))
@@ -389,7 +419,8 @@ def test_persistent_kernel_matches_checker(gpu_pkg, orc, name, rows):
     assert np.array_equal(np.array(states), ref[1]), name
 
 
-@pytest.mark.parametrize("softcap,scale,fused", [(30.0, 1.0, 0), (0.0, 8.0, 0), (30.0, 0.5, 0), (30.0, 8.0, 1)])
+@pytest.mark.parametrize("softcap,scale,fused", [(30.0, 1.0, 0), (0.0, 8.0, 0), (30.0, 0.5, 0), (30.0, 8.0, 1),
+                                                 (30.0, 8.0, 2), (0.0, 1.0, 2)])
 def test_logit_prologue_matches_checker(gpu_pkg, orc, softcap, scale, fused):
     # the engine's prologue (engine.zig:341-354: soft-cap, then 1 / logit_scale)
     # fused into the sampler, with a repetition penalty on top; the checker
@@ -476,3 +507,46 @@ def test_vocab_sharded_exact_merge_emulated(gpu_pkg, orc, world, rows, extras):
     for st in states:
         assert np.array_equal(st.smp.rng_state, ref[1][-1])
         st.smp.close()
+
+
+RF_FULL = 1 << 5
+
+
+@pytest.mark.parametrize("name,rows,vocab,extra", [
+    ("c1", 12, 128256, {}),
+    ("headline_topp", 8, 128256, {}),
+    ("c3_topk1", 4, 256000, {}),
+    ("c2", 8, 151936, {}),                       # typical-p alone: the band's retry
+    ("c2", 6, 50000, dict(top_k=200, min_p=0.01)),   # typical-p over a selected set
+    ("c1", 6, 40000, dict(top_k=0, top_p=1.0, min_p=0.0)),   # nothing filtered: every token kept
+])
+def test_full_vocabulary_retry_matches_checker(gpu_pkg, orc, name, rows, vocab, extra):
+    # the path of rows whose candidates (or typical-p band) fail their cover
+    # check: the whole vocabulary sorted by the CTA.  The test hook sends
+    # every row through it, with penalised history and the logit prologue
+    import ctypes
+    L = gpu_pkg.sampler.lib()
+    L.bs_debug_set_force_full.argtypes = [ctypes.c_void_p, ctypes.c_uint32]
+    w = gpu_pkg.workloads.WORKLOADS[name]
+    c = dict(w.config(), **extra)
+    x = gpu_pkg.workloads.make_logits(w, rows=rows, vocab=vocab)
+    seeds = w.seeds(rows)
+    rng = np.random.default_rng(5)
+    prev = rng.integers(0, vocab, size=(rows, 24)).astype(np.uint32)
+    c = dict(c, repetition_penalty=1.2, repetition_window=20)
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=rows, vocab=vocab, seeds=seeds)
+    assert L.bs_debug_set_force_full(s._h, 1) == 0
+    got = s.sample(torch.from_numpy(x).cuda(), prev_tokens=torch.from_numpy(prev.astype(np.int32)).cuda())
+    got = got.cpu().numpy().astype(np.uint32)
+    torch.cuda.synchronize()
+    tr = s.traces()
+    st = s.rng_state
+    s.close()
+    exp, _, ost = orc.sample_batch(orc.make_config(**c), x, seeds=seeds, prev=prev)
+    for r in range(rows):
+        assert tr[r].status == 0, (name, r, tr[r].status, tr[r].flags)
+    if c["temperature"] > 0:
+        assert all(tr[r].flags & RF_FULL for r in range(rows)), [tr[r].flags for r in range(rows)]
+    bad = np.flatnonzero(got != exp)
+    assert len(bad) == 0, f"{name}: rows {bad[:8]} gpu {got[bad[:8]]} ref {exp[bad[:8]]}"
+    assert np.array_equal(st, ost)
