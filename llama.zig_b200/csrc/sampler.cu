@@ -1368,7 +1368,7 @@ struct __align__(16) MainSmem {
     uint16_t rcl[RC_CAP];               // (tile << 5) | element
     uint32_t nrc, rc_fb[SEG_TILES / 32];
     uint32_t nlist, nanflag;
-    int32_t lo0;
+    uint32_t wuni[K12_THREADS / 32];
     uint32_t wsum_u[K12_THREADS / 32];
     uint64_t ch_a[K12_THREADS / 32], ch_b[K12_THREADS / 32];
     uint32_t ch_heads[K12_THREADS / 32], ch_start[K12_THREADS / 32];
@@ -1437,6 +1437,9 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     if (live) ts_pre = ld_tilestat(P.tstat + (size_t)hrow * P.ntiles_total + seg * SEG_TILES + tid);
     grid_dep_wait();   // the row reduction (and, for the entropy, the normaliser's walk)
     const RowInfo ri = ld_rowinfo(P.rinfo + hrow);
+    // the segment's prefix estimate, requested with the row's information
+    // (one round trip for both)
+    const double base_p = TERM == TERM_P ? __ldcg(&P.sstat[(size_t)hrow * MAX_SEG + seg].base) : 0.0;
     const float M = ri.M;
     if (TERM == TERM_H && __ldcg(&hdr->tdone)) return;   // the row's token is already final
     if (TERM == TERM_H) bulk = seg_issue(x + seg * SEG_ELEMS, nseg_el, sbuf, &bar, pol);
@@ -1477,7 +1480,7 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
         }
         double base;
         if (TERM == TERM_P) {
-            base = __ldcg(&P.sstat[(size_t)hrow * MAX_SEG + seg].base);
+            base = base_p;
         } else {
             // entropy mass of the earlier segments, from their statistics
             if (warp == 0) {
@@ -1662,48 +1665,6 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
         base = __shfl_sync(0xffffffffu, base, 0);
         if (special) wlist[base + __popc(m & ((1u << lane) - 1u))] = tid;
     }
-    // candidates (index, logit): warp-aggregated reservation.  The
-    // normaliser pass takes every token above the floor; the entropy pass,
-    // for typical-p alone, every token whose approximate dev = |-ln P - H|
-    // is inside the band
-    auto is_cand = [&](float d) {
-        if (TERM == TERM_P) return (d == 0.0f ? 0.0f : d * c2) >= xf2;
-        const float w = fminf(fmaf(d, c2, -l2S) * -0.6931472f, 1e30f);
-        return fabsf(w - Hr) <= dband;
-    };
-    const bool tc = live && (tp.info & TP_CAND);
-    if (__any_sync(0xffffffffu, tc)) {
-        uint32_t nc = 0;
-        if (tc) {
-#pragma unroll 1
-            for (int j = 0; j < 8; j++) {
-                const float4 q = quad(j);
-                const float a4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int c = 0; c < 4; c++) nc += is_cand(__fsub_rn(a4[c], M)) ? 1u : 0u;
-            }
-        }
-        const uint32_t incl = warp_incl_scan_u(nc);
-        const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
-        uint32_t cb = 0;
-        if (lane == 31 && wtot) cb = atomicAdd(&hdr->n_cand, wtot);
-        cb = __shfl_sync(0xffffffffu, cb, 31);
-        uint32_t pos = cb + incl - nc;
-        if (nc) {
-#pragma unroll 1
-            for (int j = 0; j < 8; j++) {
-                const float4 q = quad(j);
-                const float a4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    if (is_cand(__fsub_rn(a4[c], M))) {
-                        if (pos < P.cand_stride) cand[pos] = Candidate{g0 + tile_elem(tid, j, c), a4[c]};
-                        pos++;
-                    }
-                }
-            }
-        }
-    }
     if (__any_sync(0xffffffffu, nanl != 0) && lane == 0) atomicOr(&nanflag, 1u);
     __syncthreads();
     if (nanflag && tid == 0) atomicOr(&hdr->flags, RF_NAN);
@@ -1766,6 +1727,49 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
         }
         if (lane == 0) rec[lt] = r;
     }
+    // candidates (index, logit), after the warp's exact-pass tiles and in
+    // the same barrier interval: warp-aggregated reservation.  The
+    // normaliser pass takes every token above the floor; the entropy pass,
+    // for typical-p alone, every token whose approximate dev = |-ln P - H|
+    // is inside the band
+    auto is_cand = [&](float d) {
+        if (TERM == TERM_P) return (d == 0.0f ? 0.0f : d * c2) >= xf2;
+        const float w = fminf(fmaf(d, c2, -l2S) * -0.6931472f, 1e30f);
+        return fabsf(w - Hr) <= dband;
+    };
+    const bool tc = live && (tp.info & TP_CAND);
+    if (__any_sync(0xffffffffu, tc)) {
+        uint32_t nc = 0;
+        if (tc) {
+#pragma unroll 1
+            for (int j = 0; j < 8; j++) {
+                const float4 q = quad(j);
+                const float a4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int c = 0; c < 4; c++) nc += is_cand(__fsub_rn(a4[c], M)) ? 1u : 0u;
+            }
+        }
+        const uint32_t incl = warp_incl_scan_u(nc);
+        const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t cb = 0;
+        if (lane == 31 && wtot) cb = atomicAdd(&hdr->n_cand, wtot);
+        cb = __shfl_sync(0xffffffffu, cb, 31);
+        uint32_t pos = cb + incl - nc;
+        if (nc) {
+#pragma unroll 1
+            for (int j = 0; j < 8; j++) {
+                const float4 q = quad(j);
+                const float a4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    if (is_cand(__fsub_rn(a4[c], M))) {
+                        if (pos < P.cand_stride) cand[pos] = Candidate{g0 + tile_elem(tid, j, c), a4[c]};
+                        pos++;
+                    }
+                }
+            }
+        }
+    }
     __syncthreads();
 
     // ---- items: a stretch of SIMPLE tiles of one binade, a stretch of WINDOW
@@ -1777,19 +1781,24 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
     // the common segment (past the row start): every tile SIMPLE in one
     // binade with parity-free counts -- a single item, from a block sum
     {
-        int32_t &lo0 = ms_.lo0;
+        // (the tile records are final after the exact pass's barrier)
         uint32_t *const wsum_u = ms_.wsum_u;
-        if (tid == 0) lo0 = rec[0].lo;
-        __syncthreads();
+        uint32_t *const wuni = ms_.wuni;
+        const int32_t lo0 = rec[0].lo;
         const TileRec rt = live ? rec[tid] : rec[0];
-        const bool uni = __syncthreads_and(rt.cls == CLS_SIMPLE && rt.lo == lo0 && rt.qlo.q0 == rt.qlo.q1) != 0;
-        if (uni) {
-            // a tile counts < 2^22.5, so 256 of them fit 32 bits
-            uint32_t q = live ? rt.qlo.q0 : 0u;
+        const bool mine = rt.cls == CLS_SIMPLE && rt.lo == lo0 && rt.qlo.q0 == rt.qlo.q1;
+        // a tile counts < 2^22.5, so 256 of them fit 32 bits
+        const uint32_t qw = __reduce_add_sync(0xffffffffu, live ? rt.qlo.q0 : 0u);
+        const bool wall = __all_sync(0xffffffffu, mine);
+        if (lane == 0) {
+            wsum_u[warp] = qw;
+            wuni[warp] = wall ? 1u : 0u;
+        }
+        __syncthreads();
+        bool uni = true;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-            if (lane == 0) wsum_u[warp] = q;
-            __syncthreads();
+        for (int w = 0; w < NW; w++) uni = uni && wuni[w] != 0u;
+        if (uni) {
             if (tid == 0) {
                 uint32_t tot = 0;
                 for (int w = 0; w < NW; w++) tot += wsum_u[w];
@@ -2008,7 +2017,7 @@ __device__ __forceinline__ void main_task(const K12Params &P, uint32_t seg, uint
 }
 
 template <int TERM>
-__global__ void __launch_bounds__(K12_THREADS) k2_main(K12Params P) {
+__global__ void __launch_bounds__(K12_THREADS, 5) k2_main(K12Params P) {
     __shared__ __align__(128) float4 sbuf[SEG_ELEMS / 4];
     __shared__ MainSmem ms;
     __shared__ __align__(8) uint64_t bar;
