@@ -142,6 +142,76 @@ def parity_check(pkg, w, smp, dev_x, host_x, states):
     return orc.parity_report(got, ref, traces)
 
 
+def graph_step_times(torch, smp, dev, out, n):
+    """Per-step device time of the step replayed from CUDA graphs (one graph
+    per rotating input, each one captured bs_sample call): median and p95."""
+    graphs = []
+    for x in dev:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            smp.sample(x, out=out)
+        graphs.append(g)
+    for i in range(8):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    stream = torch.cuda.current_stream()
+    for i in range(n):
+        evs[i][0].record(stream)
+        graphs[i % len(graphs)].replay()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    us = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
+    del graphs
+    return {"median": us[len(us) // 2], "p95": us[min(len(us) - 1, int(0.95 * len(us)))], "steps": n}
+
+
+def b1_token_latency(torch, pkg, local, n=500):
+    """Config 0's decode step: one row of V=128256 logits already in HBM,
+    with a 32-token history for the repetition penalty (window 32, 1.1, the
+    SamplerConfig defaults), token id left in HBM.  Per-token device latency
+    replayed from a CUDA graph (no host synchronisation between tokens) and
+    with eager launches; median and p95."""
+    w = pkg.workloads.WORKLOADS["c0"]
+    cfg = pkg.SamplerConfig(**w.config(repetition_window=32, repetition_penalty=1.1))
+    smp = pkg.Sampler(cfg, batch=1, vocab=w.vocab, device=local, seeds=w.seeds(1))
+    xs = [torch.from_numpy(pkg.workloads.make_logits(w, step=s, rows=1)).cuda() for s in range(2)]
+    hist = torch.randint(0, w.vocab, (1, 32), dtype=torch.int32, device="cuda")
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def timed(step):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            evs[i][0].record(stream)
+            step(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        us = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
+        return {"median": us[len(us) // 2], "p95": us[min(len(us) - 1, int(0.95 * len(us)))]}
+
+    for i in range(10):
+        smp.sample(xs[i % 2], prev_tokens=hist, out=out)
+    torch.cuda.synchronize()
+    eager = timed(lambda i: smp.sample(xs[i % 2], prev_tokens=hist, out=out))
+    graphs = []
+    for x in xs:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            smp.sample(x, prev_tokens=hist, out=out)
+        graphs.append(g)
+    for i in range(10):
+        graphs[i % 2].replay()
+    graph = timed(lambda i: graphs[i % 2].replay())
+    st = smp.last_status()
+    del graphs
+    smp.close()
+    if st != 0:
+        raise RuntimeError(f"sampler status {st}")
+    return {"graph_us": graph, "eager_us": eager, "tokens": n,
+            "config": "c0: B=1 V=128256 T=0.8 top_p=0.9, penalty 1.1 over a 32-token history"}
+
+
 def run_reference(args, pkg, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -266,6 +336,7 @@ def main():
                     help="seconds the reference arm may take in all (sizes its rows per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-b1", action="store_true", help="skip the B=1 per-token latency (config 0)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -334,6 +405,7 @@ def main():
     per_us = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
     step_us = {"median": per_us[len(per_us) // 2], "p95": per_us[min(len(per_us) - 1, int(0.95 * len(per_us)))],
                "steps": nper}
+    graph_us = graph_step_times(torch, smp, dev, out, nper)
     launches_per_step = 1 if greedy else (6 if w.typical_p < 1.0 else 4)
     kernel_ms = None
     if not greedy:
@@ -400,7 +472,10 @@ def main():
                     "d2h_bytes_per_step": 4 * B, "api": "bs_sample_host (pinned host logits)"},
             "gpu_launches": launches_per_step * args.steps,
             "step_us": step_us,
+            "graph_step_us": graph_us,
         }
+        if not args.no_b1:
+            line["b1_latency"] = b1_token_latency(torch, pkg, local)
         if parity is not None:
             line["parity"] = parity
         if not args.no_cpu_baseline:

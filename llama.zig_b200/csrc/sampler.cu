@@ -2688,6 +2688,10 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     __shared__ uint32_t woff[ITEM_SMEM];         // WINDOW item: its prefix table in wpool, or ~0u
     __shared__ __align__(8) WTile wpool[WPOOL];
     __shared__ uint32_t s_nit[MAX_SEG], wsum[KB_THREADS / 32 + 1], wcnt[KB_THREADS / 32], n_fit;
+    // the walk's order of items: slots of sall, or ITEM_SMEM + s for a
+    // segment s with more items than its slots (walked from global memory)
+    __shared__ uint16_t fidx[ITEM_SMEM + MAX_SEG];
+    __shared__ uint32_t n_flat, n_items_all;
     __shared__ __align__(16) float tilep[TILE];   // a recomputed tile's p, for the walker
     __shared__ float S_sh;
     __shared__ uint32_t walk_flags, walk_items, walk_slow, n_zero;
@@ -2736,6 +2740,36 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
         S_sh = __int_as_float(0x7fc00000);
     }
     __syncthreads();
+    if (warp == KB_THREADS / 32 - 1) {
+        // the flat list the walk runs through (a loop over segments and their
+        // items costs it several times more per item); two segments per lane
+        const uint32_t s0 = lane, s1 = lane + 32;
+        const uint32_t n0 = s0 < nseg ? s_nit[s0] : 0u, n1 = s1 < nseg ? s_nit[s1] : 0u;
+        const uint32_t c0 = s0 < nseg ? (n0 <= spec ? n0 : 1u) : 0u;
+        const uint32_t c1 = s1 < nseg ? (n1 <= spec ? n1 : 1u) : 0u;
+        const uint32_t i0 = warp_incl_scan_u(c0);
+        const uint32_t t0 = __shfl_sync(0xffffffffu, i0, 31);
+        const uint32_t i1 = t0 + warp_incl_scan_u(c1);
+        const uint32_t all = __reduce_add_sync(0xffffffffu, n0 + n1);
+        if (s0 < nseg) {
+            if (n0 <= spec) {
+                for (uint32_t j = 0; j < n0; j++) fidx[i0 - c0 + j] = (uint16_t)(s0 * spec + j);
+            } else {
+                fidx[i0 - c0] = (uint16_t)(ITEM_SMEM + s0);
+            }
+        }
+        if (s1 < nseg) {
+            if (n1 <= spec) {
+                for (uint32_t j = 0; j < n1; j++) fidx[i1 - c1 + j] = (uint16_t)(s1 * spec + j);
+            } else {
+                fidx[i1 - c1] = (uint16_t)(ITEM_SMEM + s1);
+            }
+        }
+        if (lane == 31) {
+            n_flat = i1;
+            n_items_all = all;
+        }
+    }
     // prefix tables of the WINDOW items held in shared memory (offsets by a
     // block scan over the item slots, two per thread; tables that do not fit
     // stay in global memory).  Slots are scanned in order, so the tables that
@@ -2881,40 +2915,70 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
                 for (uint32_t tt = from; tt < ntl; tt++) add_tile(it.tile + tt);
             }
         };
-        for (uint32_t sgi = 0; sgi < nseg; sgi++) {
-            const uint32_t nit = s_nit[sgi];
-            nitems_all += nit;
-            // the segment's items from the shared copy, or, when it has more
-            // than that holds, in chunks from global memory (one call site of
-            // slow_item, so that it is inlined and the walk state stays in
-            // registers)
-            const bool held = nit <= spec;
-            for (uint32_t i0 = 0; i0 < nit; i0 += ITEM_CHUNK) {
-                const Item *src = sall + sgi * spec;
-                uint32_t nc = nit;
-                if (!held) {
-                    nc = min((uint32_t)ITEM_CHUNK, nit - i0);
-                    __syncwarp();
-                    for (uint32_t j = lane; j < nc; j += 32) sitems[j] = ib[sgi * SEG_TILES + i0 + j];
-                    __syncwarp();
-                    src = sitems;
+        // The items in walk order from the flat list: the common case stays
+        // in the tight loop (the running sum is in the item's binade and
+        // stays there: a SIMPLE stretch, or a WINDOW stretch that does not
+        // cross), with the next slot and item requested a step ahead; every
+        // other item goes through the one call site of slow_item below (so
+        // that it is inlined and the walk state stays in registers).  A
+        // segment with more items than its shared slots is walked from
+        // global memory in chunks.
+        static_assert(ITEM_SMEM + MAX_SEG <= 65535, "slots fit 16 bits");
+        const uint32_t nf = n_flat;
+        nitems_all = n_items_all;
+        uint32_t j = 0;
+        uint32_t gseg = 0xFFFFFFFFu, gpos = 0, gn = 0;   // the segment walked from global memory
+        uint32_t ix = nf > 0 ? fidx[0] : 0u, ixn = nf > 1 ? fidx[1] : 0u;
+        for (;;) {
+            Item it;
+            uint32_t wo = 0xFFFFFFFFu;
+            if (gseg != 0xFFFFFFFFu) {
+                if (gpos == gn) {
+                    gseg = 0xFFFFFFFFu;
+                    continue;
                 }
-                // the common case stays in this loop: the running sum is in
-                // the item's binade and stays there (a SIMPLE stretch, or a
-                // WINDOW stretch that does not cross)
-                for (uint32_t j = 0; j < nc; j++) {
-                    const Item it = src[j];
-                    if (st.e == it.lo) {
-                        const uint32_t q = (st.m & 1u) ? it.q[1] : it.q[0];
-                        if (st.m + q < QLIM && q < QSAT) {
-                            st.m += q;
-                            continue;
-                        }
+                const uint32_t k = gpos % ITEM_CHUNK;
+                if (k == 0) {
+                    const uint32_t nc = min((uint32_t)ITEM_CHUNK, gn - gpos);
+                    __syncwarp();
+                    for (uint32_t q = lane; q < nc; q += 32) sitems[q] = ib[gseg * SEG_TILES + gpos + q];
+                    __syncwarp();
+                }
+                it = sitems[k];
+                gpos++;
+                if (st.e == it.lo) {
+                    const uint32_t q = (st.m & 1u) ? it.q[1] : it.q[0];
+                    if (st.m + q < QLIM && q < QSAT) {
+                        st.m += q;
+                        continue;
                     }
-                    slow_item(it, held ? woff[sgi * spec + j] : 0xFFFFFFFFu);
                 }
-                if (held) break;
+            } else {
+                for (; j < nf && ix < (uint32_t)ITEM_SMEM; j++) {
+                    // kind, lo, q[0], q[1]: the first 16 bytes of the item
+                    const uint4 f = *reinterpret_cast<const uint4 *>(sall + ix);
+                    const uint32_t ixnn = j + 2 < nf ? fidx[j + 2] : 0u;
+                    const uint32_t q = (st.m & 1u) ? f.w : f.z;
+                    if (!(st.e == (int)f.y && st.m + q < QLIM && q < QSAT)) break;
+                    st.m += q;
+                    ix = ixn;
+                    ixn = ixnn;
+                }
+                if (j >= nf) break;
+                const uint32_t cur = ix;
+                j++;
+                ix = ixn;
+                ixn = j + 1 < nf ? fidx[j + 1] : 0u;
+                if (cur >= (uint32_t)ITEM_SMEM) {
+                    gseg = cur - ITEM_SMEM;
+                    gpos = 0;
+                    gn = s_nit[gseg];
+                    continue;
+                }
+                it = sall[cur];
+                wo = woff[cur];
             }
+            slow_item(it, wo);
         }
         if (lane == 0) {
             S_sh = float_of(st);
@@ -3656,6 +3720,35 @@ static void make_params(const bs_sampler *s, uint32_t seq, const float *d_logits
 
 }
 
+// Rows [row0, row0 + rows) of a call through the separate kernels on one
+// stream: penalty bitmap, statistics, row reduction, main pass, walk and draw
+// (with typical-p, the entropy main pass and walk).  The kernels after the
+// statistics pass overlap their predecessors (programmatic dependent launch).
+static cudaError_t launch_group(bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
+                                uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out,
+                                cudaStream_t st) {
+    K12Params A;
+    KBParams B;
+    bool pen = false;
+    uint32_t win = 0;
+    make_params(s, seq, d_logits, ld, row0, rows, d_prev, n_prev, d_out, A, B, pen, win);
+    const dim3 g12(s->nseg, rows), g2(s->nseg * rows);
+    if (pen) k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, 0u, row0, s->ntiles_total, s->d_penbm);
+    k1_stats<<<g12, K12_THREADS, 0, st>>>(A);
+    cudaError_t e = launch_dependent(k1_rows, dim3(rows), dim3(K12_THREADS), 0, st, A);
+    if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_P>, g2, dim3(K12_THREADS), 0, st, A);
+    if (A.tmode != TYP_OFF) {
+        if (e == cudaSuccess) e = launch_dependent(kernel_b<TERM_P>, dim3(rows), dim3(KB_THREADS), s->smem_b, st, B);
+        if (e == cudaSuccess) e = launch_dependent(k2_main<TERM_H>, g2, dim3(K12_THREADS), 0, st, A);
+    }
+    if (e == cudaSuccess)
+        e = launch_dependent(A.tmode != TYP_OFF ? kernel_b<TERM_H> : kernel_b<TERM_P>, dim3(rows), dim3(KB_THREADS),
+                             s->smem_b, st, B);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
+    return e;
+}
+
 // One sampling call; `seq` numbers it for the error word (never 0).
 static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits, size_t ld, uint32_t row0,
                              uint32_t rows, const uint32_t *d_prev, uint32_t n_prev, uint32_t *d_out, void *stream) {
@@ -3710,9 +3803,9 @@ static bs_status sample_impl(bs_sampler *s, uint32_t seq, const float *d_logits,
         if (e != cudaSuccess) fprintf(stderr, "b200_sampler: launch failed: %s\n", cudaGetErrorString(e));
         return cuda_status(e);
     }
-    // (with profiling on, the event records between the groups keep them
-    // from overlapping; the unprofiled step overlaps every boundary after the
-    // statistics pass)
+    if (!ev) return cuda_status(launch_group(s, seq, d_logits, ld, row0, rows, d_prev, n_prev, d_out, st));
+    // profiled: the same launches with event records between the kernel
+    // groups (which keep them from overlapping)
     const dim3 g12(s->nseg, rows), g2(s->nseg * rows);
     if (ev) cudaEventRecord(ev[0], st);
     if (pen) k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, 0u, row0, s->ntiles_total, s->d_penbm);

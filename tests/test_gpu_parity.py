@@ -550,3 +550,43 @@ def test_full_vocabulary_retry_matches_checker(gpu_pkg, orc, name, rows, vocab, 
     bad = np.flatnonzero(got != exp)
     assert len(bad) == 0, f"{name}: rows {bad[:8]} gpu {got[bad[:8]]} ref {exp[bad[:8]]}"
     assert np.array_equal(st, ost)
+
+
+def test_cuda_graph_capture_matches_eager(gpu_pkg, orc):
+    # the device-resident decode step: bs_sample captured into a CUDA graph
+    # (static input, history and output buffers, no host synchronisation)
+    # and replayed token after token gives the eager tokens and RNG states,
+    # which match the checker
+    w, x = _workload(gpu_pkg, "c1", 8, steps=4)
+    c = w.config(repetition_window=16, repetition_penalty=1.3)
+    seeds = w.seeds(8)
+    rng = np.random.default_rng(3)
+    prev = rng.integers(0, w.vocab, size=(4, 8, 20)).astype(np.uint32)
+    s = gpu_pkg.Sampler(gpu_pkg.SamplerConfig(**c), batch=8, vocab=w.vocab, seeds=seeds)
+    st0 = s.rng_state
+    eager = []
+    for i in range(4):
+        pv = torch.from_numpy(prev[i].astype(np.int32)).cuda()
+        eager.append(s.sample(torch.from_numpy(x[i]).cuda(), pv).cpu().numpy().astype(np.uint32))
+    st_e = s.rng_state
+    s.rng_state = st0
+    xin = torch.empty((8, w.vocab), dtype=torch.float32, device="cuda")
+    hin = torch.empty((8, 20), dtype=torch.int32, device="cuda")
+    out = torch.empty(8, dtype=torch.int32, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        s.sample(xin, hin, out=out)
+    graph = []
+    for i in range(4):
+        xin.copy_(torch.from_numpy(x[i]))
+        hin.copy_(torch.from_numpy(prev[i].astype(np.int32)))
+        g.replay()
+        graph.append(out.cpu().numpy().astype(np.uint32))
+    st_g = s.rng_state
+    assert s.last_status() == 0
+    del g
+    s.close()
+    assert np.array_equal(np.array(graph), np.array(eager))
+    assert np.array_equal(st_g, st_e)
+    ref = run_oracle(orc, c, x, seeds, prev)
+    assert np.array_equal(np.array(graph), ref[0])
