@@ -277,9 +277,31 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
             vs.sample(dev[i % ROTATE])
         end.record(stream)
         torch.cuda.synchronize()
-    ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
+    eager_ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
     if vs.last_status() != 0:
         raise RuntimeError(f"sampler status {vs.last_status()}")
+    ms = eager_ms
+    graphed = False
+    if vs.exact:
+        # the step as CUDA graphs (one per rotating input; collectives
+        # inside), replayed with no host work between steps
+        graphs = [vs.graph(x)[0] for x in dev]
+        for i in range(args.warmup):
+            graphs[i % ROTATE].replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            graphs[i % ROTATE].replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = pkg.sharding.max_over_ranks(start.elapsed_time(end), dist, device="cuda")
+        del graphs
+        graphed = True
+        if vs.last_status() != 0:
+            raise RuntimeError(f"sampler status {vs.last_status()}")
     # end to end: pinned host shard -> device, sample, B token ids -> host
     pinned = [torch.from_numpy(h).pin_memory() for h in host[:2]]
     d_in = torch.empty_like(dev[0])
@@ -314,6 +336,8 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
                     "h2d_bytes_per_step": int(per_gpu_bytes), "d2h_bytes_per_step": 4 * B,
                     "api": "VocabShardedSampler.sample (pinned host shard)"},
             "gpu_launches": (8 if vs.exact else 4) * args.steps,
+            "timing": ("CUDA-graph replay of the whole step (collectives captured)" if graphed else "eager launches"),
+            "eager_ms_per_step": eager_ms / args.steps,
         }
         print(json.dumps(line), flush=True)
     vs.close()

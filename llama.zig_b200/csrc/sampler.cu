@@ -9,35 +9,52 @@
 // Every decision downstream of `sum` depends on its exact f32 value, so this
 // implementation reproduces the sequential f32 sum bit for bit, in parallel:
 //
-//   Kernel A (one thread-block cluster per row, one CTA per row segment, the
-//   segment resident in shared memory; HBM is read once):
-//     1. load the segment, row max M via DSMEM;
-//     2. approximate tile sums (ex2.approx) -> cluster-wide prefix P_raw(t);
-//     3. rounding-aware tile sums: each p rounded to the grid of the binade
-//        the running sum is expected to be in -> prefix P(t), which tracks the
-//        reference's running sum to ~1e-6;
-//     4. every 32-element tile gets the candidate binades [lo, hi] of the
-//        running sum over it; tiles with lo == hi are SIMPLE; inside one binade
-//        e the f32 add s + p is exactly s + u_e * round_e(p) (u_e the ulp of
-//        binade e, round-half-even whose tie direction depends on the parity
-//        of s), so a tile reduces to two integer counts (entry parity 0/1);
-//        WINDOW (hi = lo+1) and COMPLEX tiles keep their exact p for an
-//        element-wise add;
-//     5. consecutive SIMPLE tiles of one binade are composed into one item.
-//   Kernel B (one CTA per row): a single warp walks the ~30-60 items with the
-//   exact state (binade, integer mantissa): an item applies in O(1) when the
-//   state is in its binade and does not leave it; otherwise the tile is added
-//   element by element with the same f32 adds as the reference.  The result
-//   is the reference's `sum`, bit for bit, for every input (a speculation miss
-//   only costs time).  Meanwhile the other warps sort the candidate tokens;
-//   then exact probs, the filters, the kept mass and the draw follow the
-//   reference's sequential f32 order on the (small) candidate prefix.
+//   k0_penalty  (a repetition penalty only) one bit per token of the row's
+//               last `window` previous ids; the passes below apply the
+//               penalty (and the engine's logit prologue, if one is set)
+//               while loading.
+//   k1_stats    one CTA per 8192-logit segment, one 32-logit tile per thread,
+//               the segment bulk-copied into shared memory (the one full HBM
+//               read): tile maxima and approximate tile sums of
+//               2^((v - tile max) log2e / T); segment maxima and sums; the
+//               histograms the candidate floor (top-p) or the typical-p band
+//               need.
+//   k1_rows     one CTA per row: the row maximum M, an approximate running
+//               sum at every segment start, and the candidate floor: top-k
+//               from the tile maxima, top-p from a tail-mass bound, min-p
+//               from its threshold.
+//   k2_main     one CTA per segment again: each tile gets the binades
+//               [lo, hi] its running sum can be in.  Inside one binade e the
+//               f32 add s + p is exactly s + u_e round(p / u_e) (u_e the ulp
+//               of binade e; round half to even, whose tie direction depends
+//               on the parity of s), so a tile whose window is one binade
+//               (SIMPLE) reduces to a pair of integer counts (entry parity
+//               0/1).  The counts come from ex2.approx bracketed by a proven
+//               error bound; a tile whose bracket is ambiguous, or that spans
+//               more binades (WINDOW / COMPLEX), is counted exactly by one
+//               warp with the restated expf, COMPLEX tiles keeping their exact
+//               terms.  Runs of tiles become walk items; tokens above the
+//               floor become candidates (index, logit).
+//   kernel_b    one CTA per row: warp 0 walks the ~40 items with the exact
+//               state (binade, integer mantissa): an item applies in O(1)
+//               when the state is in its binade and stays there; otherwise
+//               the tile is added element by element with the reference's
+//               f32 adds.  The result is the reference's `sum`, bit for bit,
+//               for every input (a wrong prediction only costs time).
+//               Meanwhile the other warps sort the candidates; then exact
+//               probs, the filters, the kept mass and the draw follow the
+//               reference's sequential f32 order on the candidate prefix.
+//   Typical-p runs k2_main and kernel_b once more over the entropy terms
+//   P (-ln P), which reproduces H bit for bit in the same way.
 //
-// Candidates: Kernel A keeps only tokens above a floor that provably contains
-// the kept prefix and the token that ends it (top-k: the k-th largest tile
-// maximum; top-p: a mass bound; min-p: its threshold); Kernel B verifies the
-// cover and reports BS_ENOTSUP if it ever fails.
-#include <cooperative_groups.h>
+// Candidates: k2_main keeps only tokens above a floor that provably contains
+// the kept prefix and the token that ends it; kernel_b verifies the cover,
+// and a row whose check fails is sorted again over its whole vocabulary in
+// the same CTA (the reference's full sort; slower, same token).
+//
+// Also here: argmax_kernel (T <= 0), persistent forms of the first three
+// passes (k_fused, k_resident; opt-in), the vocabulary-sharded entry points
+// (bs_vshard_*), and the allocation-free entry point (bs_sample_static).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -49,8 +66,6 @@
 #include "../../include/b200_sampler.h"
 #include "bs_math.cuh"
 #include "sampler_kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace bs {
 

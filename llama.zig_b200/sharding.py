@@ -255,6 +255,7 @@ class VocabShardedSampler:
         self.device = device
         base = cfg.seed if seeds_base is None else seeds_base
         self.exact = exact_merge_supported(cfg) if exact is None else exact
+        self._capturing = False
         if self.exact and not exact_merge_supported(cfg):
             raise ValueError("the exact partial merge needs 0 < top_k <= 256, temperature > 0 and typical-p off")
         dev = torch.device("cuda", device)
@@ -299,22 +300,45 @@ class VocabShardedSampler:
             self._cand_all[0].copy_(cand)
             self._count_all[0].copy_(count)
         else:
-            works.append(dist.all_gather_into_tensor(self._cand_all, cand, async_op=True))
-            works.append(dist.all_gather_into_tensor(self._count_all, count, async_op=True))
-        entry = None
-        if lay.rank > 0:
-            dist.recv(self._entry, src=lay.rank - 1)
-            entry = self._entry
-        exit_ = st.walk(entry, stream)
-        if lay.rank < lay.world - 1:
-            dist.send(exit_, dst=lay.rank + 1)
+            # (asynchronous when eager; a captured step keeps stream order)
+            a = not self._capturing
+            works.append(dist.all_gather_into_tensor(self._cand_all, cand, async_op=a))
+            works.append(dist.all_gather_into_tensor(self._count_all, count, async_op=a))
+        # the chain of walks in rank order: link k broadcasts rank k's exit
+        # state, which is rank k + 1's entry; the last link's is the row's S.
+        # Every rank takes part in every link (one collective sequence on all
+        # ranks, which a CUDA graph can hold)
+        if lay.world == 1:
+            self._S.copy_(st.walk(None, stream))
         else:
-            self._S.copy_(exit_)
-        if lay.world > 1:
-            dist.broadcast(self._S, src=lay.world - 1)
+            for k in range(lay.world):
+                if lay.rank == k:
+                    self._S.copy_(st.walk(self._entry if k > 0 else None, stream))
+                dist.broadcast(self._S, src=k)
+                if lay.rank == k + 1:
+                    self._entry.copy_(self._S)
         for wk in works:
-            wk.wait()
+            if wk is not None:
+                wk.wait()
         return st.draw(self._cand_all, self._count_all, self._S, stream)
+
+    def graph(self, shard, prev_tokens=None):
+        """One sample() step on these buffers captured into a CUDA graph,
+        collectives included: ``g.replay()`` repeats the step (new logits
+        copied into ``shard`` first) with no host work.  Returns (graph,
+        token tensor).  Call sample() once before, so that the collectives'
+        communicators exist."""
+        import torch
+        if not self.exact:
+            raise ValueError("graph capture is built for the exact partial merge")
+        self._capturing = True
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self.sample(shard, prev_tokens)
+        finally:
+            self._capturing = False
+        return g, out
 
     def last_status(self) -> int:
         return self.st.smp.last_status() if self.exact else self.local.last_status()

@@ -35,11 +35,19 @@ def _rank(rank, world, port, rows, out_dir):
         w = pkg.workloads.WORKLOADS["c4"]
         vs = pkg.sharding.VocabShardedSampler(pkg.SamplerConfig(**w.config()), rows, w.vocab, dist, device=rank)
         toks = []
-        for step in range(2):
-            full = pkg.workloads.make_logits(w, step=step, rows=rows)
-            shard = torch.from_numpy(np.ascontiguousarray(vs.lay.shard_of(full))).cuda()
-            toks.append(vs.sample(shard).cpu().numpy())
+        shards = [torch.from_numpy(np.ascontiguousarray(vs.lay.shard_of(pkg.workloads.make_logits(w, step=step, rows=rows))))
+                  for step in range(3)]
+        # step 0 eager; steps 1 and 2 replayed from one CUDA graph of the
+        # whole step (collectives included) on a static shard buffer
+        buf = shards[0].cuda()
+        toks.append(vs.sample(buf).cpu().numpy())
+        g, out = vs.graph(buf)
+        for step in (1, 2):
+            buf.copy_(shards[step])
+            g.replay()
+            toks.append(out.cpu().numpy())
         torch.cuda.synchronize()
+        del g
         vs.close()
         np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.stack(toks))
     finally:
@@ -57,7 +65,7 @@ def test_vocab_sharded_two_gpus(tmp_path, orc):
     mp.start_processes(_rank, args=(2, _port(), rows, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     w = pkg.workloads.WORKLOADS["c4"]
     states = None
-    for step in range(2):
+    for step in range(3):
         x = pkg.workloads.make_logits(w, step=step, rows=rows)
         exp, _, states = orc.sample_batch(orc.make_config(**w.config()), x,
                                           seeds=w.seeds(rows) if states is None else None, states=states)
