@@ -148,6 +148,12 @@ def rows_from_vocab_shards(lay: VocabShard, shard, dist, recv=None, out=None):
     return out
 
 
+def history_rows(lay: VocabShard, prev_tokens):
+    """This rank's rows of a (B, n_prev) previous-token history: the rows the
+    transpose gives it, [row0, row0 + B/G)."""
+    return prev_tokens[lay.row0:lay.row0 + lay.rows_per_rank]
+
+
 def gather_tokens(lay: VocabShard, local, dist, out=None):
     """(B/G,) token ids of this rank's rows -> (B,) on every rank."""
     import torch
@@ -278,10 +284,9 @@ class VocabShardedSampler:
     def sample(self, shard, prev_tokens=None):
         import torch
         if not self.exact:
-            if prev_tokens is not None:
-                raise ValueError("the transpose path takes no previous tokens; use a top-k bound")
             rows = rows_from_vocab_shards(self.lay, shard, self.dist, self._recv, self._rows)
-            self.local.sample(rows, out=self._tok)
+            pv = None if prev_tokens is None else history_rows(self.lay, prev_tokens).to(torch.int32).contiguous()
+            self.local.sample(rows, pv, out=self._tok)
             return gather_tokens(self.lay, self._tok, self.dist, self._all)
         lay, st, dist = self.lay, self.st, self.dist
         stream = torch.cuda.current_stream().cuda_stream

@@ -90,7 +90,11 @@ def _vocab_rank_main(rank, world, port, rows, vocab, out_dir):
         shard = lay.shard_of(full).contiguous()
         mine = pkg.sharding.rows_from_vocab_shards(lay, shard, dist)
         assert torch.equal(mine, full[lay.row0:lay.row0 + lay.rows_per_rank])
-        tok, _, st = orc.sample_batch(orc.make_config(**w.config()), mine.numpy(), seeds=lay.seeds(w.seed))
+        # with a repetition penalty: each rank takes its rows of the history
+        hist = torch.from_numpy(np.random.default_rng(9).integers(0, vocab, size=(rows, 12)).astype(np.uint32))
+        prev = pkg.sharding.history_rows(lay, hist).numpy()
+        tok, _, st = orc.sample_batch(orc.make_config(**w.config(repetition_window=8, repetition_penalty=1.3)),
+                                      mine.numpy(), seeds=lay.seeds(w.seed), prev=prev)
         allt = pkg.sharding.gather_tokens(lay, torch.from_numpy(tok.astype(np.int64)), dist)
         if rank == 0:
             np.save(os.path.join(out_dir, "vocab_tokens.npy"), allt.numpy())
@@ -106,7 +110,9 @@ def test_vocab_sharded_transpose_matches_one_process(tmp_path, pkg, orc, world):
     got = np.load(tmp_path / "vocab_tokens.npy")
     w = pkg.workloads.WORKLOADS["c4"]
     x = pkg.workloads.make_logits(w, rows=rows, vocab=vocab)
-    tok, _, _ = orc.sample_batch(orc.make_config(**w.config()), x, seeds=w.seeds(rows))
+    hist = np.random.default_rng(9).integers(0, vocab, size=(rows, 12)).astype(np.uint32)
+    tok, _, _ = orc.sample_batch(orc.make_config(**w.config(repetition_window=8, repetition_penalty=1.3)), x,
+                                 seeds=w.seeds(rows), prev=hist)
     assert np.array_equal(got, tok.astype(np.int64))
 
 
