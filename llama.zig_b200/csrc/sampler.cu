@@ -2436,29 +2436,67 @@ __device__ __noinline__ unsigned long long *cta_radix_sort(unsigned long long *a
     const unsigned long long vary = red[0] ^ red[1];
     const uint32_t chunk = (n + KB_THREADS - 1) / KB_THREADS;
     const uint32_t lo = min(n, tid * chunk), hi = min(n, lo + chunk);
+    const int lane = tid & 31, warp = tid >> 5;
+    // per-thread digit counters in shared memory, column `tid` of 16 rows
+    // (a register array indexed by the digit would live in local memory)
+    uint32_t *const col = cnt + tid;
     for (int sh = 0; sh < 64; sh += 4) {
         if (((vary >> sh) & 0xFull) == 0) continue;
+#pragma unroll
+        for (int d = 0; d < 16; d++) col[d * KB_THREADS] = 0u;
+        for (uint32_t i = lo; i < hi; i++) col[((a[i] >> sh) & 0xF) * KB_THREADS]++;
         uint32_t c[16];
 #pragma unroll
-        for (int d = 0; d < 16; d++) c[d] = 0;
-        for (uint32_t i = lo; i < hi; i++) c[(a[i] >> sh) & 0xF]++;
-#pragma unroll
-        for (int d = 0; d < 16; d++) cnt[d * KB_THREADS + tid] = c[d];
+        for (int d = 0; d < 16; d++) c[d] = col[d * KB_THREADS];
+        // exclusive scan of the counts in digit-major order (digit d of thread
+        // t starts after every lower digit and after digit d of threads < t),
+        // in parallel: within each warp by shuffles, then over the warps and
+        // the digits through shared memory (the counter rows are free once
+        // every thread holds its counts)
         __syncthreads();
-        if (tid == 0) {   // exclusive scan, digit-major
-            uint32_t run = 0;
-            for (int i = 0; i < 16 * KB_THREADS; i++) {
-                const uint32_t v = cnt[i];
-                cnt[i] = run;
-                run += v;
+        uint32_t *const wt = cnt;                              // [warp][16] warp totals
+        uint32_t *const base = cnt + (KB_THREADS / 32) * 16;   // [warp][16] starts
+#pragma unroll
+        for (int d = 0; d < 16; d++) {
+            uint32_t incl = c[d];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += u;
+            }
+            if (lane == 31) wt[warp * 16 + d] = incl;
+            c[d] = incl - c[d];   // within the warp
+        }
+        __syncthreads();
+        if (tid < 32) {   // digit d = tid (< 16): where each warp's keys of digit d start
+            const int d = tid & 15;
+            uint32_t wcol[KB_THREADS / 32], tot = 0;
+#pragma unroll
+            for (int w = 0; w < KB_THREADS / 32; w++) {
+                wcol[w] = tot;
+                tot += wt[w * 16 + d];
+            }
+            uint32_t dincl = tid < 16 ? tot : 0u;   // prefix of the digit totals
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, dincl, o);
+                if (lane >= o) dincl += u;
+            }
+            if (tid < 16) {
+#pragma unroll
+                for (int w = 0; w < KB_THREADS / 32; w++) base[w * 16 + d] = dincl - tot + wcol[w];
             }
         }
         __syncthreads();
 #pragma unroll
-        for (int d = 0; d < 16; d++) c[d] = cnt[d * KB_THREADS + tid];
+        for (int d = 0; d < 16; d++) c[d] += base[warp * 16 + d];
+        __syncthreads();   // (the starts are read before the columns are rewritten)
+#pragma unroll
+        for (int d = 0; d < 16; d++) col[d * KB_THREADS] = c[d];
+        // stable scatter: each thread its contiguous range, in order
         for (uint32_t i = lo; i < hi; i++) {
             const unsigned long long k = a[i];
-            b[c[(k >> sh) & 0xF]++] = k;
+            b[col[((k >> sh) & 0xF) * KB_THREADS]++] = k;
         }
         __syncthreads();
         unsigned long long *t = a;
@@ -2720,6 +2758,9 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     const uint32_t flags0 = hdr->flags;
     const uint32_t n_cand = min(hdr->n_cand, P.cand_stride);
     const uint32_t n_wc = min(hdr->n_wc, (uint32_t)WC_CAP);
+    // (a bitonic network in shared memory, beside the walk, up to CAND_SMEM
+    // keys; longer lists take the block-wide radix sort in global memory
+    // after it)
     const bool big = TERM == TERM_P && n_cand > (uint32_t)CAND_SMEM;
 
     // the walk's inputs in shared memory, gathered with asynchronous copies
