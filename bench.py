@@ -498,7 +498,7 @@ def main():
             "step_us": step_us,
             "graph_step_us": graph_us,
         }
-        if not args.no_b1:
+        if not args.no_b1:   # (rank 0 only: the other ranks wait at the closing barrier)
             line["b1_latency"] = b1_token_latency(torch, pkg, local)
         if parity is not None:
             line["parity"] = parity
