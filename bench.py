@@ -259,7 +259,8 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
     token ids)."""
     B, V = w.rows, w.vocab
     cfg = pkg.SamplerConfig(**w.config())
-    vs = pkg.sharding.VocabShardedSampler(cfg, B, V, dist if world > 1 else None, device=local)
+    vs = pkg.sharding.VocabShardedSampler(cfg, B, V, dist if world > 1 else None, device=local,
+                                          transport=args.vs_transport)
     lay = vs.lay
     host = [np.ascontiguousarray(lay.shard_of(pkg.workloads.make_logits(w, step=s, rows=B))) for s in range(ROTATE)]
     dev = [torch.from_numpy(h).cuda() for h in host]
@@ -325,7 +326,8 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
             "data": "synthetic",
             "config": {"workload": workload_desc(w), "rows": B, "vocab": V,
                        "parallelism": (f"vocab-sharded x{world}: exact partial merge (all-gather of per-row "
-                                       "partials, chain of shard walks, all-gather of candidates)"
+                                       "partials, all-gather of candidates, chain of shard walks "
+                                       + ("through peer memory)" if vs.p2p else "by NCCL broadcasts)")
                                        if vs.exact else f"vocab-sharded x{world}: all-to-all transpose"),
                        "l2": f"{ROTATE} rotating shard batches ({ROTATE * per_gpu_bytes / 1e6:.0f} MB per GPU)"},
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
@@ -361,6 +363,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-b1", action="store_true", help="skip the B=1 per-token latency (config 0)")
+    ap.add_argument("--vs-transport", default="p2p", choices=["nccl", "p2p"],
+                    help="config 4's chain of walks: through peer memory (p2p) or by NCCL broadcasts")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

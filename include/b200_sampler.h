@@ -163,6 +163,32 @@ bs_status bs_vshard_export(bs_sampler *s, uint32_t col0, bs_vshard_cand *d_cand,
 bs_status bs_vshard_draw(bs_sampler *s, const bs_vshard_cand *d_cand_all, const uint32_t *d_count_all,
                          uint32_t world, const float *d_S, uint32_t *d_out, void *stream);
 
+/* The same step through peer memory over NVLink instead of host-issued
+ * collectives (one process per GPU, all GPUs of one node):
+ *   bs_vshard_ipc_handle  the 64-byte CUDA IPC handle of this rank's exchange
+ *                         words for `world` ranks (allocated on first use)
+ *   (the caller all-gathers the handles: world x 64 bytes of host memory)
+ *   bs_vshard_ipc_open    maps the other ranks' exchange words
+ * Then, with the handle's whole batch in every call:
+ *   bs_vshard_stats       with d_part = NULL stores each row's partial in
+ *                         every rank's words (no all-gather)
+ *   bs_vshard_main        with d_parts = NULL waits (bounded) for each row's
+ *                         partials of every rank
+ *   bs_vshard_export      with d_cand = d_count = NULL stores the candidates
+ *                         in every rank's words (no all-gather)
+ *   bs_vshard_chain       replaces bs_vshard_walk and the exit / S exchange:
+ *                         the walk of a row on rank g waits for rank g-1's
+ *                         exit of that row and stores its own into rank g+1's
+ *                         words; the last rank stores S into every rank's
+ *   bs_vshard_draw        with d_cand_all = d_count_all = d_S = NULL takes
+ *                         them from this rank's words.
+ * Every word is tagged with the step (a counter every rank advances in
+ * bs_vshard_stats), so a replayed CUDA graph works; every rank must make the
+ * same sequence of calls on its handle. */
+bs_status bs_vshard_ipc_handle(bs_sampler *s, uint32_t world, void *h_handle64);
+bs_status bs_vshard_ipc_open(bs_sampler *s, uint32_t world, uint32_t rank, const void *h_handles);
+bs_status bs_vshard_chain(bs_sampler *s, void *stream);
+
 /* Per-row xoshiro256++ state, batch x 4 u64 (host memory).  Synchronous. */
 bs_status bs_get_rng_state(bs_sampler *s, uint64_t *h_state);
 bs_status bs_set_rng_state(bs_sampler *s, const uint64_t *h_state);

@@ -596,6 +596,10 @@ struct K12Params {
     // or nullptr; this shard's rank
     const VsPart *vs_parts;
     uint32_t vs_world, vs_rank;
+    // the partials through peer memory: rank h's partial of row r is valid
+    // once vs_ptag[h * rows + r] carries the step's tag (*vs_epoch)
+    const unsigned long long *vs_ptag;
+    const uint32_t *vs_epoch;
     // persistent kernel (k_fused): task scheduler state of this call
     uint32_t *ctl;            // [0] next statistics task, [1] next main task, [2] ready rows;
                               // then per call row: statistics tasks done; all zeroed before the call
@@ -740,6 +744,42 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// System-scope forms (words another GPU writes or reads over NVLink).
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+constexpr uint64_t PEER_WAIT_NS = 1000000000ull;   // one second for a peer's word
+// Waits (one thread) for the word to carry this step's tag: true and its
+// 32-bit payload, or false after a second without it (the call's error word
+// `seq` then says so).
+__device__ bool wait_peer_bits(const unsigned long long *p, uint32_t tag, uint32_t seq, uint32_t *kerr,
+                               uint32_t &bits) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0;; it++) {
+        const unsigned long long v = ld_acquire_sys_u64(p);
+        if ((uint32_t)(v >> 32) == tag) {
+            bits = (uint32_t)v;
+            return true;
+        }
+        if (global_ns() - t0 > PEER_WAIT_NS || it > (1u << 26)) {
+            atomicExch(kerr, seq);
+            bits = 0u;
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+// The f32 payload, or NaN when the wait gave up.
+__device__ float wait_peer_word(const unsigned long long *p, uint32_t tag, uint32_t seq, uint32_t *kerr) {
+    uint32_t b;
+    return wait_peer_bits(p, tag, seq, kerr, b) ? __uint_as_float(b) : __int_as_float(0x7fc00000);
+}
+
 // Waits for phase `parity` of the barrier; false once `limit_ns` have passed
 // (or after 2^20 tries).  Each try lets the hardware suspend the thread until
 // the phase completes or a microsecond passes, so waiting threads do not
@@ -1121,6 +1161,13 @@ __device__ __forceinline__ void rows_task(const K12Params &P, uint32_t row, Rows
         if (P.vs_parts) {
             // a vocabulary shard: the row maximum over all shards, and the
             // estimate of the lower-index shards' mass at this shard's start
+            if (P.vs_ptag) {   // lane h waits for rank h's partial of this row
+                const uint32_t tag = *P.vs_epoch;
+                for (uint32_t h = lane; h < P.vs_world; h += 32) {
+                    uint32_t b;
+                    wait_peer_bits(P.vs_ptag + (size_t)h * P.rows + row, tag, P.seq, P.kerr, b);
+                }
+            }
             float gm = NEG_INF;
             uint32_t gnf = 0;
             for (uint32_t h = lane; h < P.vs_world; h += 32) {
@@ -2263,6 +2310,17 @@ struct KBParams {
     const float *vs_entry;
     float *vs_exit;
     const float *vs_S;
+    // the chain through peer memory instead (vs_p2p): 64-bit words
+    // (seq << 32) | f32 bits.  VS_WALK waits for its entry in vs_in[row]
+    // (written by the previous rank; rank 0: the empty sum) and stores its
+    // exit in the next rank's vs_next[row], or, on the last rank, the row's
+    // S in every rank's S words (vs_xs[g] + vs_soff + row); VS_DRAW waits
+    // for its S in vs_in[vs_soff + row]
+    uint32_t vs_p2p, vs_world, vs_rank, vs_soff;
+    const uint32_t *vs_epoch;   // the step's tag (a captured graph replays one seq)
+    unsigned long long *vs_in;
+    unsigned long long *vs_next;
+    unsigned long long *const *vs_xs;
     const RowInfo *rinfo;   // per handle row
     uint32_t tmode;      // TYP_*
     uint32_t force_full;    // test hook: every row takes the full-vocabulary retry
@@ -2897,12 +2955,20 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
 
     if (warp == 0 && P.vs_mode == VS_DRAW) {
         // the normaliser of every shard's terms, from the chain of walks
-        if (lane == 0) S_sh = P.vs_S[row];
+        if (lane == 0)
+            S_sh = P.vs_p2p ? wait_peer_word(P.vs_in + P.vs_soff + row, *P.vs_epoch, P.seq,
+                                             const_cast<uint32_t *>(P.kerr))
+                            : P.vs_S[row];
     } else if (warp == 0) {
         // ---- the exact walk of the sequential f32 sum (skipped for a NaN
         // row, whose sum is NaN whatever the order; warp 0 must still stay
         // out of the sort's named barrier below) ----
-        const float entry = P.vs_entry ? P.vs_entry[row] : 0.0f;
+        float entry = P.vs_entry ? P.vs_entry[row] : 0.0f;
+        if (P.vs_p2p && P.vs_rank > 0) {   // the previous rank's exit (a peer's store)
+            if (lane == 0)
+                entry = wait_peer_word(P.vs_in + row, *P.vs_epoch, P.seq, const_cast<uint32_t *>(P.kerr));
+            entry = __shfl_sync(0xffffffffu, entry, 0);
+        }
         if (!(flags0 & RF_NAN) && entry == entry) {
         SumState st = state_of(entry);   // the empty sum: binade -126, count 0
         uint32_t wflags = 0, nitems_all = 0, nslow = 0;
@@ -3078,7 +3144,16 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     }
     __syncthreads();
     if (P.vs_mode == VS_WALK) {   // this shard's part of the chain ends here
-        if (tid == 0) P.vs_exit[row] = S_sh;
+        if (tid == 0 && P.vs_p2p) {
+            const unsigned long long w = ((unsigned long long)*P.vs_epoch << 32) | __float_as_uint(S_sh);
+            if (P.vs_next) {
+                st_release_sys_u64(P.vs_next + row, w);
+            } else {   // the last rank: the row's S to every rank
+                for (uint32_t g = 0; g < P.vs_world; g++) st_release_sys_u64(P.vs_xs[g] + P.vs_soff + row, w);
+            }
+        } else if (tid == 0) {
+            P.vs_exit[row] = S_sh;
+        }
         return;
     }
     if (TERM == TERM_H) {
@@ -3316,10 +3391,45 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     P.trace[hrow] = tr;
 }
 
+// A rank's exchange words for the vocabulary-sharded step through peer
+// memory (u64 words; B = the handle's batch, G = the world):
+//   [0, B)            entry: the previous rank's exit state of each row
+//   [B, 2B)           S: the row's normaliser, from the last rank
+//   [2B]              the step tag (low 32 bits)
+//   then G x B        tags of the ranks' partials
+//   then G x B x 2    the ranks' partials (VsPart)
+//   then G x B        the ranks' candidate counts, tagged
+//   then G x B x CAP  the ranks' candidates (Candidate)
+// A tagged word is (tag << 32) | payload, stored with release semantics at
+// system scope after the data it covers.
+struct VsLayout {
+    size_t ptag, parts, ctag, cand, words;
+    __host__ __device__ VsLayout(uint32_t B, uint32_t G) {
+        ptag = 2 * (size_t)B + 1;
+        parts = ptag + (size_t)G * B;
+        ctag = parts + 2 * (size_t)G * B;
+        cand = ctag + (size_t)G * B;
+        words = cand + (size_t)G * B * VS_CAND_CAP;
+    }
+};
+struct VsPeer {
+    unsigned long long *const *xs;   // every rank's exchange words (null: host collectives)
+    unsigned long long *own;         // this rank's
+    uint32_t world, rank, batch;
+};
+
+// The peer-memory chain's step tag: one increment at the start of every step
+// (so a replayed CUDA graph tags each replay afresh; every rank makes the same
+// calls, so the ranks' tags agree).  Never 0, the value of unwritten words.
+__global__ void k_vs_epoch(uint32_t *epoch) {
+    const uint32_t e = *epoch + 1u;
+    *epoch = e == 0u ? 1u : e;
+}
+
 // Vocabulary sharding: each row's partial over this shard, from the
 // statistics pass's segment aggregates (one warp per row).
 __global__ void k_vs_partials(const SegStat *__restrict__ sstat, uint32_t nseg, uint32_t rows, float c2,
-                              VsPart *__restrict__ out) {
+                              VsPart *__restrict__ out, VsPeer pe) {
     const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31u;
     if (row >= rows) return;
     const SegStat *S = sstat + (size_t)row * MAX_SEG;
@@ -3335,33 +3445,73 @@ __global__ void k_vs_partials(const SegStat *__restrict__ sstat, uint32_t nseg, 
     for (uint32_t c = lane; c < nseg; c += 32)
         if (S[c].smax > NEG_INF) sum += S[c].ssum * (double)ex2_approx((S[c].smax - m) * c2);
     sum = warp_sum_d(sum);
-    if (lane == 0) out[row] = VsPart{m, nf, sum};
+    if (lane == 0 && !pe.xs) out[row] = VsPart{m, nf, sum};
+    if (pe.xs && lane < pe.world) {   // to every rank's words, then the tag
+        const VsLayout L(pe.batch, pe.world);
+        const uint32_t tag = *reinterpret_cast<const uint32_t *>(pe.own + 2 * (size_t)pe.batch);
+        unsigned long long *x = pe.xs[lane];
+        const size_t k = (size_t)pe.rank * pe.batch + row;
+        *reinterpret_cast<VsPart *>(x + L.parts + 2 * k) = VsPart{m, nf, sum};
+        st_release_sys_u64(x + L.ptag + k, ((unsigned long long)tag << 32) | 1ull);
+    }
 }
 
 // This shard's candidates with global token ids (col0 added), at most
 // VS_CAND_CAP per row; count[row] = VS_CAND_CAP + 1 marks an overflow.
 __global__ void k_vs_export(const RowHdr *__restrict__ hdr, const Candidate *__restrict__ cand, uint32_t cand_stride,
-                            uint32_t col0, Candidate *__restrict__ out, uint32_t *__restrict__ count) {
+                            uint32_t col0, Candidate *__restrict__ out, uint32_t *__restrict__ count, VsPeer pe) {
     const uint32_t row = blockIdx.x;
     const uint32_t n = hdr[row].n_cand;
     const uint32_t m = n < VS_CAND_CAP ? n : VS_CAND_CAP;
+    const uint32_t cnt = n <= VS_CAND_CAP ? n : VS_CAND_CAP + 1;
+    if (!pe.xs) {
+        for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+            const Candidate c = cand[(size_t)row * cand_stride + i];
+            out[(size_t)row * VS_CAND_CAP + i] = Candidate{c.idx + col0, c.v};
+        }
+        if (threadIdx.x == 0) count[row] = cnt;
+        return;
+    }
+    // to every rank's words; then, once the block's stores are done, the
+    // tagged counts
+    const VsLayout L(pe.batch, pe.world);
+    const size_t k = (size_t)pe.rank * pe.batch + row;
     for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
         const Candidate c = cand[(size_t)row * cand_stride + i];
-        out[(size_t)row * VS_CAND_CAP + i] = Candidate{c.idx + col0, c.v};
+        const Candidate o{c.idx + col0, c.v};
+        for (uint32_t g = 0; g < pe.world; g++)
+            *reinterpret_cast<Candidate *>(pe.xs[g] + L.cand + k * VS_CAND_CAP + i) = o;
     }
-    if (threadIdx.x == 0) count[row] = n <= VS_CAND_CAP ? n : VS_CAND_CAP + 1;
+    __syncthreads();
+    if (threadIdx.x < pe.world) {
+        __threadfence_system();
+        const uint32_t tag = *reinterpret_cast<const uint32_t *>(pe.own + 2 * (size_t)pe.batch);
+        st_release_sys_u64(pe.xs[threadIdx.x] + L.ctag + k, ((unsigned long long)tag << 32) | cnt);
+    }
 }
 
 // The candidates of every shard ([world][rows][VS_CAND_CAP]) as this
 // handle's candidate list of each row (a shard that overflowed flags the row).
 __global__ void k_vs_merge(const Candidate *__restrict__ all, const uint32_t *__restrict__ counts, uint32_t world,
-                           uint32_t rows, RowHdr *__restrict__ hdr, Candidate *__restrict__ cand, uint32_t cand_stride) {
+                           uint32_t rows, RowHdr *__restrict__ hdr, Candidate *__restrict__ cand, uint32_t cand_stride,
+                           VsPeer pe, uint32_t seq, uint32_t *kerr) {
     const uint32_t row = blockIdx.x;
-    __shared__ uint32_t base[65];
+    __shared__ uint32_t base[65], pcount[64];
+    if (pe.xs) {   // the ranks' candidates in this rank's words, once their counts carry the step's tag
+        const VsLayout L(pe.batch, pe.world);
+        all = reinterpret_cast<const Candidate *>(pe.own + L.cand);
+        if (threadIdx.x < world) {
+            const uint32_t tag = *reinterpret_cast<const uint32_t *>(pe.own + 2 * (size_t)pe.batch);
+            uint32_t c = 0;
+            wait_peer_bits(pe.own + L.ctag + (size_t)threadIdx.x * pe.batch + row, tag, seq, kerr, c);
+            pcount[threadIdx.x] = c;   // (0 when the wait gave up: the call's rows then fail)
+        }
+        __syncthreads();
+    }
     if (threadIdx.x == 0) {
         uint32_t b = 0, over = 0;
         for (uint32_t h = 0; h < world; h++) {
-            const uint32_t c = counts[(size_t)h * rows + row];
+            const uint32_t c = pe.xs ? pcount[h] : counts[(size_t)h * rows + row];
             base[h] = b;
             over |= c > VS_CAND_CAP ? 1u : 0u;
             b += c > VS_CAND_CAP ? VS_CAND_CAP : c;
@@ -3375,7 +3525,8 @@ __global__ void k_vs_merge(const Candidate *__restrict__ all, const uint32_t *__
         const uint32_t n = base[h + 1] - base[h];
         for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
             if (base[h] + i < cand_stride)
-                cand[(size_t)row * cand_stride + base[h] + i] = all[((size_t)h * rows + row) * VS_CAND_CAP + i];
+                cand[(size_t)row * cand_stride + base[h] + i] =
+                    all[((size_t)h * (pe.xs ? pe.batch : rows) + row) * VS_CAND_CAP + i];
     }
 }
 
@@ -3438,6 +3589,13 @@ struct bs_sampler {
     KBParams vs_B;
     uint32_t vs_rows;
     bool vs_ready;
+    // peer-memory chain: this rank's exchange words (entry, then S, batch
+    // each), the ranks' exchange words as this device sees them (opened
+    // peer mappings), and the device array of those pointers
+    unsigned long long *d_xchg;
+    unsigned long long *peer_xchg[64];
+    unsigned long long **d_peer_xchg;
+    uint32_t p2p_world, p2p_rank, xchg_world;
     float *d_logits_stage;   // host-path staging
     uint32_t *d_prev_stage;
     uint32_t *d_out_stage;
@@ -3508,6 +3666,10 @@ static void free_all(bs_sampler *s) {
     cudaFree(s->d_logits_stage);
     cudaFree(s->d_prev_stage);
     cudaFree(s->d_out_stage);
+    for (uint32_t g = 0; g < s->p2p_world && g < 64; g++)
+        if (g != s->p2p_rank && s->peer_xchg[g]) cudaIpcCloseMemHandle(s->peer_xchg[g]);
+    cudaFree(s->d_peer_xchg);
+    cudaFree(s->d_xchg);
     if (s->stream) cudaStreamDestroy(s->stream);
     for (uint32_t i = 0; s->prof_ev && i < 4 * s->prof_cap; i++) cudaEventDestroy(s->prof_ev[i]);
     delete[] s->prof_ev;
@@ -3736,6 +3898,8 @@ static void make_params(const bs_sampler *s, uint32_t seq, const float *d_logits
     A.vs_parts = nullptr;
     A.vs_world = 1;
     A.vs_rank = 0;
+    A.vs_ptag = nullptr;
+    A.vs_epoch = nullptr;
     A.typical_p = c.typical_p;
     A.tmode = typical_mode(c.typical_p, c.top_k, s->vocab, c.top_p, c.min_p);
 
@@ -3773,6 +3937,14 @@ static void make_params(const bs_sampler *s, uint32_t seq, const float *d_logits
     B.vs_entry = nullptr;
     B.vs_exit = nullptr;
     B.vs_S = nullptr;
+    B.vs_p2p = 0;
+    B.vs_world = 1;
+    B.vs_rank = 0;
+    B.vs_soff = 0;
+    B.vs_in = nullptr;
+    B.vs_epoch = nullptr;
+    B.vs_next = nullptr;
+    B.vs_xs = nullptr;
 
 }
 
@@ -3911,6 +4083,19 @@ extern "C" bs_status bs_sample(bs_sampler *s, const float *d_logits, size_t ld, 
 //                     row's RNG state (the same on every rank)
 // Exact only with a top-k bound: every kept token is among its shard's local
 // top-k, which each shard's candidates contain.
+// The peer-memory exchange of this handle (all null before bs_vshard_ipc_open).
+static VsPeer vs_peer(const bs_sampler *s) {
+    VsPeer pe{};
+    if (s->d_peer_xchg) {
+        pe.xs = s->d_peer_xchg;
+        pe.own = s->d_xchg;
+        pe.world = s->p2p_world;
+        pe.rank = s->p2p_rank;
+        pe.batch = s->batch;
+    }
+    return pe;
+}
+
 static bool vs_supported(const bs_sampler *s) {
     const bs_config &c = s->cfg;
     return c.temperature > 0.0f && c.top_k > 0 && c.top_k <= (uint32_t)KSEL_MAX &&
@@ -3919,7 +4104,9 @@ static bool vs_supported(const bs_sampler *s) {
 
 extern "C" bs_status bs_vshard_stats(bs_sampler *s, const float *d_shard, size_t ld, uint32_t col0, uint32_t rows,
                                      const uint32_t *d_prev, uint32_t n_prev, bs_vshard_part *d_part, void *stream) {
-    if (!s || !d_shard || !d_part || ld < s->vocab || rows == 0 || rows > s->batch) return BS_EINVAL;
+    if (!s || !d_shard || ld < s->vocab || rows == 0 || rows > s->batch) return BS_EINVAL;
+    if (!d_part && !s->d_peer_xchg) return BS_EINVAL;     // (NULL: the partials go to the peers' words)
+    if (s->d_peer_xchg && rows != s->batch) return BS_EINVAL;   // (the exchange words are laid out by the batch)
     if (!vs_supported(s)) return BS_ENOTSUP;
     cudaStream_t st = (cudaStream_t)stream;
     bool pen = false;
@@ -3927,21 +4114,30 @@ extern "C" bs_status bs_vshard_stats(bs_sampler *s, const float *d_shard, size_t
     make_params(s, next_seq(s->seq), d_shard, ld, 0, rows, d_prev, n_prev, nullptr, s->vs_A, s->vs_B, pen, win);
     s->vs_rows = rows;
     s->vs_ready = true;
+    if (s->d_peer_xchg) k_vs_epoch<<<1, 1, 0, st>>>(reinterpret_cast<uint32_t *>(s->d_xchg + 2 * (size_t)s->batch));
     if (pen)
         k0_penalty<<<rows, 256, 0, st>>>(d_prev, n_prev, win, s->vocab, col0, 0u, s->ntiles_total, s->d_penbm);
     k1_stats<<<dim3(s->nseg, rows), K12_THREADS, 0, st>>>(s->vs_A);
+    VsPeer pe = vs_peer(s);
+    if (d_part) pe.xs = nullptr;   // (partials to the caller's buffer, host collectives)
     k_vs_partials<<<(rows + 7) / 8, 256, 0, st>>>(s->d_sstat, s->nseg, rows, s->vs_A.c2,
-                                                   reinterpret_cast<VsPart *>(d_part));
+                                                   reinterpret_cast<VsPart *>(d_part), pe);
     return cuda_status(cudaGetLastError());
 }
 
 extern "C" bs_status bs_vshard_main(bs_sampler *s, const bs_vshard_part *d_parts, uint32_t world, uint32_t rank,
                                     void *stream) {
-    if (!s || !d_parts || world == 0 || world > 64 || rank >= world) return BS_EINVAL;
-    if (!s->vs_ready) return BS_EINVAL;
+    if (!s || world == 0 || world > 64 || rank >= world) return BS_EINVAL;
+    if (!s->vs_ready || (!d_parts && !s->d_peer_xchg)) return BS_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
     K12Params A = s->vs_A;
     A.vs_parts = reinterpret_cast<const VsPart *>(d_parts);
+    if (!d_parts) {   // the partials in this rank's exchange words, each waited for by its tag
+        const VsLayout L(s->batch, s->p2p_world);
+        A.vs_parts = reinterpret_cast<const VsPart *>(s->d_xchg + L.parts);
+        A.vs_ptag = s->d_xchg + L.ptag;
+        A.vs_epoch = reinterpret_cast<const uint32_t *>(s->d_xchg + 2 * (size_t)s->batch);
+    }
     A.vs_world = world;
     A.vs_rank = rank;
     k1_rows<<<s->vs_rows, K12_THREADS, 0, st>>>(A);
@@ -3960,24 +4156,104 @@ extern "C" bs_status bs_vshard_walk(bs_sampler *s, const float *d_entry, float *
     return cuda_status(cudaGetLastError());
 }
 
+// Peer-memory chain.  Every rank exports the IPC handle of its exchange words
+// (bs_vshard_ipc_handle), the caller all-gathers the handles (host memory,
+// world x 64 bytes), and every rank opens the others' (bs_vshard_ipc_open).
+// Then bs_vshard_chain replaces bs_vshard_walk and the exit/S exchange, and
+// bs_vshard_draw takes d_S = NULL (S arrives in the exchange words).
+extern "C" bs_status bs_vshard_ipc_handle(bs_sampler *s, uint32_t world, void *h_handle) {
+    if (!s || !h_handle || world < 2 || world > 64 || (s->d_xchg && world != s->xchg_world)) return BS_EINVAL;
+    BS_CUDA(cudaSetDevice(s->device));
+    if (!s->d_xchg) {   // the exchange words (VsLayout), zeroed: no word carries a tag yet
+        const size_t bytes = VsLayout(s->batch, world).words * sizeof(unsigned long long);
+        s->xchg_world = world;
+        if (cudaMalloc(&s->d_xchg, bytes) != cudaSuccess) return BS_ENOMEM;
+        BS_CUDA(cudaMemset(s->d_xchg, 0, bytes));
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "an IPC handle is 64 bytes");
+    cudaIpcMemHandle_t h;
+    BS_CUDA(cudaIpcGetMemHandle(&h, s->d_xchg));
+    memcpy(h_handle, &h, sizeof(h));
+    return BS_OK;
+}
+
+extern "C" bs_status bs_vshard_ipc_open(bs_sampler *s, uint32_t world, uint32_t rank, const void *h_handles) {
+    if (!s || !h_handles || world < 2 || world > 64 || rank >= world || !s->d_xchg || s->d_peer_xchg ||
+        world != s->xchg_world)
+        return BS_EINVAL;
+    BS_CUDA(cudaSetDevice(s->device));
+    s->p2p_world = world;
+    s->p2p_rank = rank;
+    for (uint32_t g = 0; g < world; g++) {
+        if (g == rank) {
+            s->peer_xchg[g] = s->d_xchg;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const unsigned char *>(h_handles) + 64 * (size_t)g, sizeof(h));
+        void *ptr = nullptr;
+        BS_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        s->peer_xchg[g] = static_cast<unsigned long long *>(ptr);
+    }
+    if (cudaMalloc(&s->d_peer_xchg, world * sizeof(unsigned long long *)) != cudaSuccess) return BS_ENOMEM;
+    BS_CUDA(cudaMemcpy(s->d_peer_xchg, s->peer_xchg, world * sizeof(unsigned long long *), cudaMemcpyHostToDevice));
+    return BS_OK;
+}
+
+// The chain of walks through peer memory: rank g's walk of a row waits for
+// rank g-1's exit word of that row and stores its own into rank g+1's; the
+// last rank stores the row's S into every rank's words.  Rows pipeline across
+// the ranks; no collective.  Every rank must make the same calls (the words
+// are tagged with the call's sequence number).
+extern "C" bs_status bs_vshard_chain(bs_sampler *s, void *stream) {
+    if (!s || !s->vs_ready || !s->d_peer_xchg) return BS_EINVAL;
+    KBParams B = s->vs_B;
+    B.vs_mode = VS_WALK;
+    B.vs_entry = nullptr;
+    B.vs_exit = nullptr;
+    B.vs_p2p = 1;
+    B.vs_world = s->p2p_world;
+    B.vs_rank = s->p2p_rank;
+    B.vs_soff = s->batch;
+    B.vs_in = s->d_xchg;
+    B.vs_epoch = reinterpret_cast<const uint32_t *>(s->d_xchg + 2 * (size_t)s->batch);
+    B.vs_next = s->p2p_rank + 1 < s->p2p_world ? s->peer_xchg[s->p2p_rank + 1] : nullptr;
+    B.vs_xs = s->d_peer_xchg;
+    kernel_b<TERM_P><<<s->vs_rows, KB_THREADS, s->smem_b, (cudaStream_t)stream>>>(B);
+    return cuda_status(cudaGetLastError());
+}
+
 extern "C" bs_status bs_vshard_export(bs_sampler *s, uint32_t col0, bs_vshard_cand *d_cand, uint32_t *d_count,
                                       void *stream) {
-    if (!s || !d_cand || !d_count || !s->vs_ready) return BS_EINVAL;
+    if (!s || !s->vs_ready) return BS_EINVAL;
+    if ((!d_cand || !d_count) && !s->d_peer_xchg) return BS_EINVAL;   // (NULL: to the peers' words)
+    VsPeer pe = vs_peer(s);
+    if (d_cand) pe.xs = nullptr;
     k_vs_export<<<s->vs_rows, 256, 0, (cudaStream_t)stream>>>(s->d_hdr, s->d_cand, s->cand_stride, col0,
-                                                               reinterpret_cast<Candidate *>(d_cand), d_count);
+                                                               reinterpret_cast<Candidate *>(d_cand), d_count, pe);
     return cuda_status(cudaGetLastError());
 }
 
 extern "C" bs_status bs_vshard_draw(bs_sampler *s, const bs_vshard_cand *d_cand_all, const uint32_t *d_count_all,
                                     uint32_t world, const float *d_S, uint32_t *d_out, void *stream) {
-    if (!s || !d_cand_all || !d_count_all || !d_S || !d_out || world == 0 || world > 64 || !s->vs_ready)
-        return BS_EINVAL;
+    if (!s || !d_out || world == 0 || world > 64 || !s->vs_ready) return BS_EINVAL;
+    // (NULL candidates / S: from this rank's exchange words)
+    if ((!d_cand_all || !d_count_all || !d_S) && !s->d_peer_xchg) return BS_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
+    VsPeer pe = vs_peer(s);
+    if (d_cand_all) pe.xs = nullptr;
     k_vs_merge<<<s->vs_rows, 256, 0, st>>>(reinterpret_cast<const Candidate *>(d_cand_all), d_count_all, world,
-                                          s->vs_rows, s->d_hdr, s->d_cand, s->cand_stride);
+                                          s->vs_rows, s->d_hdr, s->d_cand, s->cand_stride, pe, s->vs_B.seq,
+                                          s->d_kerr);
     KBParams B = s->vs_B;
     B.vs_mode = VS_DRAW;
     B.vs_S = d_S;
+    if (!d_S) {
+        B.vs_p2p = 1;
+        B.vs_soff = s->batch;
+        B.vs_in = s->d_xchg;
+        B.vs_epoch = reinterpret_cast<const uint32_t *>(s->d_xchg + 2 * (size_t)s->batch);
+    }
     B.out = d_out;
     kernel_b<TERM_P><<<s->vs_rows, KB_THREADS, s->smem_b, st>>>(B);
     return cuda_status(cudaGetLastError());

@@ -124,7 +124,11 @@ def lib() -> ctypes.CDLL:
         L.bs_vshard_walk.argtypes = [vp, vp, vp, vp]
         L.bs_vshard_export.argtypes = [vp, u32, vp, vp, vp]
         L.bs_vshard_draw.argtypes = [vp, vp, vp, u32, vp, vp, vp]
-        for name in ("bs_vshard_stats", "bs_vshard_main", "bs_vshard_walk", "bs_vshard_export", "bs_vshard_draw"):
+        L.bs_vshard_ipc_handle.argtypes = [vp, u32, vp]
+        L.bs_vshard_ipc_open.argtypes = [vp, u32, u32, ctypes.c_char_p]
+        L.bs_vshard_chain.argtypes = [vp, vp]
+        for name in ("bs_vshard_stats", "bs_vshard_main", "bs_vshard_walk", "bs_vshard_export", "bs_vshard_draw",
+                     "bs_vshard_ipc_handle", "bs_vshard_ipc_open", "bs_vshard_chain"):
             getattr(L, name).restype = ctypes.c_int
         L.bs_get_rng_state.argtypes = [vp, u64p]
         L.bs_seed_state.argtypes = [ctypes.c_uint64, u64p]

@@ -188,17 +188,19 @@ class _ShardState:
         from .sampler import lib, _check
         return lib(), _check
 
-    def stats(self, shard, prev, stream):
+    def stats(self, shard, prev, stream, push=False):
+        """push: the partials go straight to every rank's exchange words."""
         L, check = self._lib()
         pp, n_prev = (None, 0) if prev is None else (prev.data_ptr(), prev.shape[1])
         check(L.bs_vshard_stats(self.smp._h, shard.data_ptr(), shard.stride(0), self.lay.col0, self.lay.rows,
-                                pp, n_prev, self.part.data_ptr(), stream), "bs_vshard_stats")
+                                pp, n_prev, None if push else self.part.data_ptr(), stream), "bs_vshard_stats")
         return self.part
 
     def main(self, parts_all, stream):
+        """parts_all None: the partials from the exchange words."""
         L, check = self._lib()
-        check(L.bs_vshard_main(self.smp._h, parts_all.data_ptr(), self.lay.world, self.lay.rank, stream),
-              "bs_vshard_main")
+        check(L.bs_vshard_main(self.smp._h, None if parts_all is None else parts_all.data_ptr(), self.lay.world,
+                               self.lay.rank, stream), "bs_vshard_main")
 
     def walk(self, entry, stream):
         L, check = self._lib()
@@ -206,17 +208,37 @@ class _ShardState:
                                stream), "bs_vshard_walk")
         return self.exit
 
-    def export(self, stream):
+    def export(self, stream, push=False):
+        """push: the candidates go straight to every rank's exchange words."""
         L, check = self._lib()
-        check(L.bs_vshard_export(self.smp._h, self.lay.col0, self.cand.data_ptr(), self.count.data_ptr(), stream),
-              "bs_vshard_export")
+        check(L.bs_vshard_export(self.smp._h, self.lay.col0, None if push else self.cand.data_ptr(),
+                                 None if push else self.count.data_ptr(), stream), "bs_vshard_export")
         return self.cand, self.count
 
     def draw(self, cand_all, count_all, S, stream):
+        """S: the normaliser per row, or None to take it from the peer-memory
+        chain's exchange words."""
         L, check = self._lib()
-        check(L.bs_vshard_draw(self.smp._h, cand_all.data_ptr(), count_all.data_ptr(), self.lay.world,
-                               S.data_ptr(), self.out.data_ptr(), stream), "bs_vshard_draw")
+        check(L.bs_vshard_draw(self.smp._h, None if cand_all is None else cand_all.data_ptr(),
+                               None if count_all is None else count_all.data_ptr(), self.lay.world,
+                               None if S is None else S.data_ptr(), self.out.data_ptr(), stream), "bs_vshard_draw")
         return self.out
+
+    def open_peers(self, dist):
+        """Exchange the CUDA IPC handles of the ranks' chain words (host
+        all-gather) and map the others' (bs_vshard_ipc_handle / _open)."""
+        import ctypes
+        L, check = self._lib()
+        h = ctypes.create_string_buffer(64)
+        check(L.bs_vshard_ipc_handle(self.smp._h, self.lay.world, h), "bs_vshard_ipc_handle")
+        hs = [None] * self.lay.world
+        dist.all_gather_object(hs, h.raw)
+        allh = b"".join(hs)
+        check(L.bs_vshard_ipc_open(self.smp._h, self.lay.world, self.lay.rank, allh), "bs_vshard_ipc_open")
+
+    def chain(self, stream):
+        L, check = self._lib()
+        check(L.bs_vshard_chain(self.smp._h, stream), "bs_vshard_chain")
 
 
 def exact_merge_supported(cfg) -> bool:
@@ -252,7 +274,7 @@ class VocabShardedSampler:
     token ids) and gets the same B token ids back."""
 
     def __init__(self, cfg, rows: int, vocab: int, dist=None, device: int = 0, seeds_base: int | None = None,
-                 exact: bool | None = None):
+                 exact: bool | None = None, transport: str = "nccl"):
         import torch
         world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
         rank = dist.get_rank() if world > 1 else 0
@@ -262,12 +284,18 @@ class VocabShardedSampler:
         base = cfg.seed if seeds_base is None else seeds_base
         self.exact = exact_merge_supported(cfg) if exact is None else exact
         self._capturing = False
+        if transport not in ("nccl", "p2p"):
+            raise ValueError("transport is 'nccl' or 'p2p'")
+        # p2p: the chain of walks through peer memory (exact merge, 2+ ranks)
+        self.p2p = transport == "p2p" and world > 1 and self.exact
         if self.exact and not exact_merge_supported(cfg):
             raise ValueError("the exact partial merge needs 0 < top_k <= 256, temperature > 0 and typical-p off")
         dev = torch.device("cuda", device)
         R, C, G = self.lay.rows_per_rank, self.lay.cols, world
         if self.exact:
             self.st = _ShardState(cfg, self.lay, device, self.lay.all_seeds(base))
+            if self.p2p:
+                self.st.open_peers(dist)
             self._parts = torch.empty((G, rows, 2), dtype=torch.int64, device=dev)
             self._cand_all = torch.empty((G, rows, CAND_CAP, 2), dtype=torch.int32, device=dev)
             self._count_all = torch.empty((G, rows), dtype=torch.int32, device=dev)
@@ -291,6 +319,16 @@ class VocabShardedSampler:
         lay, st, dist = self.lay, self.st, self.dist
         stream = torch.cuda.current_stream().cuda_stream
         prev = None if prev_tokens is None else prev_tokens.to(torch.int32).contiguous()
+        if self.p2p:
+            # the whole step through peer memory, no collective: partials and
+            # candidates stored straight into every rank's exchange words,
+            # each waited for by its step tag; the chain inside the walk
+            # kernels; the draw from this rank's words
+            st.stats(shard, prev, stream, push=True)
+            st.main(None, stream)
+            st.export(stream, push=True)
+            st.chain(stream)
+            return st.draw(None, None, None, stream)
         part = st.stats(shard, prev, stream)
         if lay.world == 1:
             self._parts[0].copy_(part)

@@ -21,7 +21,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, rows, out_dir):
+def _rank(rank, world, port, rows, out_dir, transport):
     import datetime
     import sys
     sys.path.insert(0, ROOT)
@@ -33,7 +33,9 @@ def _rank(rank, world, port, rows, out_dir):
                             device_id=torch.device("cuda", rank))
     try:
         w = pkg.workloads.WORKLOADS["c4"]
-        vs = pkg.sharding.VocabShardedSampler(pkg.SamplerConfig(**w.config()), rows, w.vocab, dist, device=rank)
+        vs = pkg.sharding.VocabShardedSampler(pkg.SamplerConfig(**w.config()), rows, w.vocab, dist, device=rank,
+                                              transport=transport)
+        assert vs.p2p == (transport == "p2p")
         toks = []
         shards = [torch.from_numpy(np.ascontiguousarray(vs.lay.shard_of(pkg.workloads.make_logits(w, step=step, rows=rows))))
                   for step in range(3)]
@@ -54,7 +56,10 @@ def _rank(rank, world, port, rows, out_dir):
         dist.destroy_process_group()
 
 
-def test_vocab_sharded_two_gpus(tmp_path, orc):
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_vocab_sharded_two_gpus(tmp_path, orc, transport):
+    # nccl: the chain of walks as one broadcast per link; p2p: the chain
+    # inside the walk kernels through peer memory (CUDA IPC over NVLink)
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import sys
@@ -62,7 +67,8 @@ def test_vocab_sharded_two_gpus(tmp_path, orc):
     import __graft_entry__ as graft
     pkg = graft.load_package()
     rows = 32
-    mp.start_processes(_rank, args=(2, _port(), rows, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rank, args=(2, _port(), rows, str(tmp_path), transport), nprocs=2, join=True,
+                       start_method="spawn")
     w = pkg.workloads.WORKLOADS["c4"]
     states = None
     for step in range(3):
