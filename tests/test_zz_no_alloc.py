@@ -59,3 +59,30 @@ def test_static_scratch_rejects_oversize(gpu_pkg):
     big = torch.zeros((1, 140000), dtype=torch.float32, device="cuda")
     assert L.bs_sample_static(ctypes.byref(c), _ptr(rng), _ptr(big), ctypes.c_size_t(140000), 1, 140000,
                               None, 0, _ptr(out), None) == 1
+
+
+def test_static_scratch_matches_checker(gpu_pkg, orc):
+    # the allocation-free entry point directly against the CPU checker, with
+    # a repetition-penalty history, over two calls (RNG states carried on the
+    # device by the caller)
+    L = _lib(gpu_pkg)
+    w = gpu_pkg.workloads.WORKLOADS["c1"]
+    rows, V = 4, w.vocab
+    cfgd = w.config(repetition_window=16, repetition_penalty=1.3)
+    c = gpu_pkg.SamplerConfig(**cfgd).to_c()
+    seeds = w.seeds(rows)
+    states = np.stack([orc.rng_seed(int(sd)) for sd in seeds])
+    rng = torch.from_numpy(states.astype(np.uint64).view(np.int64).copy()).cuda()
+    prev = np.random.default_rng(4).integers(0, V, size=(rows, 20)).astype(np.uint32)
+    pd = torch.from_numpy(prev.astype(np.int32)).cuda()
+    for step in range(2):
+        x = gpu_pkg.workloads.make_logits(w, step=step, rows=rows)
+        xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        out = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+        st = L.bs_sample_static(ctypes.byref(c), _ptr(rng), _ptr(xd), ctypes.c_size_t(V), rows, V,
+                                _ptr(pd), 20, _ptr(out), None)
+        assert st == 0, gpu_pkg.status_string(st)
+        torch.cuda.synchronize()
+        exp, _, states = orc.sample_batch(orc.make_config(**cfgd), x, states=states, prev=prev)
+        assert np.array_equal(out.cpu().numpy().astype(np.uint32), exp), step
+        assert np.array_equal(rng.cpu().numpy().view(np.uint64), states), step
