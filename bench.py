@@ -337,7 +337,10 @@ def run_vocab_sharded(args, pkg, w, torch, dist, world, rank, local):
             "e2e": {"value": B * args.e2e_steps / e2e_s, "unit": "rows/s",
                     "h2d_bytes_per_step": int(per_gpu_bytes), "d2h_bytes_per_step": 4 * B,
                     "api": "VocabShardedSampler.sample (pinned host shard)"},
-            "gpu_launches": (8 if vs.exact else 4) * args.steps,
+            # per step: statistics and partials, row reduction and main pass,
+            # export, walk, merge and draw (the peer transport adds its
+            # one-thread step-tag kernel); the transpose: the single-GPU four
+            "gpu_launches": ((9 if vs.p2p else 8) if vs.exact else 4) * args.steps,
             "timing": ("CUDA-graph replay of the whole step (collectives captured)" if graphed else "eager launches"),
             "eager_ms_per_step": eager_ms / args.steps,
         }
