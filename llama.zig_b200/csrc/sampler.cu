@@ -3446,13 +3446,15 @@ __global__ void k_vs_partials(const SegStat *__restrict__ sstat, uint32_t nseg, 
         if (S[c].smax > NEG_INF) sum += S[c].ssum * (double)ex2_approx((S[c].smax - m) * c2);
     sum = warp_sum_d(sum);
     if (lane == 0 && !pe.xs) out[row] = VsPart{m, nf, sum};
-    if (pe.xs && lane < pe.world) {   // to every rank's words, then the tag
+    if (pe.xs) {   // to every rank's words (lane g, g + 32, ...), then the tag
         const VsLayout L(pe.batch, pe.world);
         const uint32_t tag = *reinterpret_cast<const uint32_t *>(pe.own + 2 * (size_t)pe.batch);
-        unsigned long long *x = pe.xs[lane];
         const size_t k = (size_t)pe.rank * pe.batch + row;
-        *reinterpret_cast<VsPart *>(x + L.parts + 2 * k) = VsPart{m, nf, sum};
-        st_release_sys_u64(x + L.ptag + k, ((unsigned long long)tag << 32) | 1ull);
+        for (uint32_t g = lane; g < pe.world; g += 32) {
+            unsigned long long *x = pe.xs[g];
+            *reinterpret_cast<VsPart *>(x + L.parts + 2 * k) = VsPart{m, nf, sum};
+            st_release_sys_u64(x + L.ptag + k, ((unsigned long long)tag << 32) | 1ull);
+        }
     }
 }
 
