@@ -2442,13 +2442,36 @@ __device__ __noinline__ float walk_recompute_tile(float s, const float *xrow, ui
     return s;
 }
 
-// Block-wide bitonic sort (ascending) of npow (a power of two) keys in shared
-// memory; every thread of the block takes part.
-__device__ void block_bitonic(unsigned long long *k, uint32_t npow) {
-    for (uint32_t size = 2; size <= npow; size <<= 1) {
-        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            __syncthreads();
-            for (uint32_t i = threadIdx.x; i < npow / 2; i += blockDim.x) {
+// Bitonic sort (ascending) of npow keys in shared memory (npow a power of two,
+// at least 32) by `nthr` threads of whole warps, t = 0 .. nthr - 1 their index
+// among them, `sync()` their barrier.  Only the stages with a stride of 32 or
+// more go through shared memory (one barrier each); the others run in
+// registers, lane l of a warp holding key 32 b + l of each block b the warp
+// takes, with shuffles: each merge's strides 16 .. 1, and the whole network up
+// to size 32 at the start.
+__device__ __forceinline__ unsigned long long bitonic_cmpx(unsigned long long k, uint32_t e, uint32_t s,
+                                                           uint32_t size) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, (int)s);
+    const bool up = (e & size) == 0u, lower = (e & s) == 0u;
+    return (lower == up) ? (k < o ? k : o) : (k < o ? o : k);
+}
+template <typename Sync>
+__device__ void bitonic_sort_keys(unsigned long long *k, uint32_t npow, uint32_t t, uint32_t nthr, Sync sync) {
+    const uint32_t lane = t & 31u, w = t >> 5, nw = nthr >> 5, nblk = npow >> 5;
+    // sizes 2 .. 32 in registers
+    for (uint32_t b = w; b < nblk; b += nw) {
+        const uint32_t e = 32u * b + lane;
+        unsigned long long v = k[e];
+#pragma unroll
+        for (uint32_t size = 2; size <= 32; size <<= 1)
+#pragma unroll
+            for (uint32_t st = size >> 1; st > 0; st >>= 1) v = bitonic_cmpx(v, e, st, size);
+        k[e] = v;
+    }
+    for (uint32_t size = 64; size <= npow; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride >= 32; stride >>= 1) {
+            sync();
+            for (uint32_t i = t; i < npow / 2; i += nthr) {
                 const uint32_t a = 2 * i - (i & (stride - 1));
                 const uint32_t b = a + stride;
                 const bool up = ((a & size) == 0);
@@ -2459,8 +2482,22 @@ __device__ void block_bitonic(unsigned long long *k, uint32_t npow) {
                 }
             }
         }
+        sync();
+        for (uint32_t b = w; b < nblk; b += nw) {
+            const uint32_t e = 32u * b + lane;
+            unsigned long long v = k[e];
+#pragma unroll
+            for (uint32_t st = 16; st > 0; st >>= 1) v = bitonic_cmpx(v, e, st, size);
+            k[e] = v;
+        }
     }
+    sync();
+}
+
+// Block-wide form (every thread of the block).
+__device__ void block_bitonic(unsigned long long *k, uint32_t npow) {
     __syncthreads();
+    bitonic_sort_keys(k, npow, threadIdx.x, blockDim.x, [] { __syncthreads(); });
 }
 
 // Candidate key: ascending key order == (p descending, index ascending).
@@ -2675,7 +2712,7 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
         n = full ? P.vocab : n_list;
         big = full || n > (uint32_t)CAND_SMEM;
         // 1. keys (dev, index), ascending
-        uint32_t npow = 1;
+        uint32_t npow = 32;   // (block_bitonic takes blocks of 32 keys)
         while (npow < n) npow <<= 1;
         keys = big ? gk0 : skeys;
         for (uint32_t i = tid; i < (big ? n : npow); i += KB_THREADS) {
@@ -2723,7 +2760,7 @@ __device__ void typical_tail(const KBParams &P, uint32_t row, uint32_t hrow, flo
                 const float safe = ri.dband - herr - (1e-4f * (fabsf(H) + dcross) + 1e-4f);
                 retry = !crossed || !(dcross <= safe) || P.force_full;
             }
-            uint32_t np2 = 1;
+            uint32_t np2 = 32;
             while (np2 < nk) np2 <<= 1;
             n_keep_sh = nk;
             status_sh = st;
@@ -2844,7 +2881,7 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
     const Candidate *cg_ = P.cand + (size_t)hrow * P.cand_stride;
     unsigned long long *gk0 = P.ctmp + (size_t)hrow * 2 * P.cand_stride;
     unsigned long long *gk1 = gk0 + P.cand_stride;
-    uint32_t npow = 1;
+    uint32_t npow = 32;   // (the sort's register phases take blocks of 32 keys)
     while (npow < n_cand) npow <<= 1;
     if (tid == 0) {
         walk_flags = 0;
@@ -3125,22 +3162,9 @@ __global__ void __launch_bounds__(KB_THREADS, 2) kernel_b(KBParams P) {
             skeys[i] = k;
         }
         if (nz) atomicAdd(&n_zero, nz);
-        for (uint32_t size = 2; size <= npow; size <<= 1) {
-            for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-                asm volatile("bar.sync 1, %0;" ::"r"(nthr));
-                for (uint32_t i = t2; i < npow / 2; i += nthr) {
-                    const uint32_t a = 2 * i - (i & (stride - 1));
-                    const uint32_t b = a + stride;
-                    const bool up = ((a & size) == 0);
-                    const unsigned long long ka = skeys[a], kb = skeys[b];
-                    if (up ? (ka > kb) : (ka < kb)) {
-                        skeys[a] = kb;
-                        skeys[b] = ka;
-                    }
-                }
-            }
-        }
         asm volatile("bar.sync 1, %0;" ::"r"(nthr));
+        bitonic_sort_keys(skeys, npow, (uint32_t)t2, (uint32_t)nthr,
+                          [nthr] { asm volatile("bar.sync 1, %0;" ::"r"(nthr)); });
     }
     __syncthreads();
     if (P.vs_mode == VS_WALK) {   // this shard's part of the chain ends here
