@@ -126,3 +126,13 @@ def test_vocab_shard_layout():
     assert list(lay.seeds(7)[:2]) == [263, 264]
     with pytest.raises(ValueError):
         sh.VocabShard(0, 3, 512, 128256)
+
+
+def test_vocab_sharded_transport_is_checked():
+    import sys
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as graft
+    pkg = graft.load_package()
+    cfg = pkg.SamplerConfig(top_k=50)
+    with pytest.raises(ValueError):
+        pkg.sharding.VocabShardedSampler(cfg, 8, 4096, None, transport="shm")
